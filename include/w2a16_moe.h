@@ -1,0 +1,171 @@
+/*
+ * w2a16_moe.h — C ABI of the B200 (sm_100a) W2A16 group-128 MoE decode GEMV library.
+ *
+ * Plain pointers and sizes only. Every device pointer is a CUDA device address (or a pinned host
+ * address reachable through unified addressing, where noted). Every entry point that launches
+ * work takes a cudaStream_t passed as `void* stream` (NULL = legacy default stream), performs no
+ * host synchronisation and no allocation, and returns a status code:
+ *
+ *   0 W2A16_OK            success (kernels enqueued)
+ *   1 W2A16_ERR_SHAPE     a dimension is not supported (K % 128, N % 4, ...)
+ *   2 W2A16_ERR_ALIGN     a stride or base address breaks the 16-byte rule
+ *   3 W2A16_ERR_LAUNCH    the CUDA launch failed (cudaGetLastError)
+ *   4 W2A16_ERR_ARG       a required pointer is NULL or an argument is out of range
+ *   5 W2A16_ERR_WORKSPACE the workspace is missing or too small
+ *   6 W2A16_ERR_DEVICE    no usable sm_100 device
+ *
+ * Layouts (the reference's N-contiguous int32-word layout, gemv/moe_gemv_int2_tab.py:3-5):
+ *   codes   int32 [K/16, N] per expert; value k of column n at bits 2*(k%16) of word k/16
+ *   scales  f16 or bf16 [K/128, N] per expert (scale_bf16 selects bf16)
+ *   zeros   uint8 [K/128, N/4] per expert, optional: zero point of column n at bits 2*(n%4) of
+ *           byte n/4. Without zeros the symmetric zero point 2 applies (gemv/moe_gemv_int2_tab.py:66)
+ *   w = (q - zp) * s.
+ *
+ * Device-side error word (`err`, optional, uint32 in device memory): bit 0 is set when an expert id
+ * lies outside [0, num_experts); such rows contribute zero. Bit 1 is set when a bounded wait inside
+ * a kernel gave up. The library never traps or aborts.
+ */
+#ifndef W2A16_MOE_H
+#define W2A16_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define W2A16_OK 0
+#define W2A16_ERR_SHAPE 1
+#define W2A16_ERR_ALIGN 2
+#define W2A16_ERR_LAUNCH 3
+#define W2A16_ERR_ARG 4
+#define W2A16_ERR_WORKSPACE 5
+#define W2A16_ERR_DEVICE 6
+
+/* Library version string, e.g. "w2a16_moe 0.1 sm_100a". */
+const char* w2a16_version(void);
+
+/* Human-readable name of a status code. */
+const char* w2a16_status_string(int status);
+
+/*
+ * Batch-1 MoE GEMV through int64 address tables.
+ * Replaces moe_gemv_int2_tab() — gemv/moe_gemv_int2_tab.py:72-85 (kernel :23-69), called from
+ * MoeWNA16Method._apply_gemv (patches/ncontig_gemv.py:229, :232).
+ *
+ *   c[r, n] = (mul_routed_weight ? topk_w[r] : 1)
+ *             * sum_k (q - zp) * s  of expert topk_ids[r], column n, times a[r / top_k, k]
+ *
+ * a        bf16 [*, K], row stride stride_am (elements)
+ * wtab     int64 [num_experts] base address of each expert's codes  (make_tables, :88-97)
+ * stab     int64 [num_experts] base address of each expert's scales
+ * ztab     int64 [num_experts] base address of each expert's zeros, or NULL (symmetric, zp = 2)
+ * topk_ids int32 [R] original expert ids; topk_w fp32 [R] (may be NULL if !mul_routed_weight)
+ * c        bf16 [R, N], row stride stride_cm (elements); written, never read
+ * stride_ww words per K/16 row of codes; stride_sg elements per scale row; stride_zg bytes per
+ *          zero row. K % 128 == 0, N % 4 == 0, strides multiples of 4, bases 16-byte aligned.
+ */
+int w2a16_moe_gemv_tab(const void* a, int64_t stride_am,
+                       const int64_t* wtab, const int64_t* stab, const int64_t* ztab, int num_experts,
+                       const int32_t* topk_ids, const float* topk_w,
+                       void* c, int64_t stride_cm,
+                       int R, int N, int K,
+                       int64_t stride_ww, int64_t stride_sg, int64_t stride_zg,
+                       int top_k, int mul_routed_weight, int scale_bf16,
+                       unsigned int* err, void* stream);
+
+/*
+ * The same GEMV over an expert arena addressed through an int32 slot table.
+ * Replaces the int64 address-table indirection of RowArena / ExpertElastic
+ * (gemv/row_arena.py:34-123, table writes gemv/expert_elastic.py:157, :220, :242;
+ * placed tables patches/placement.py:208-227): expert e lives at
+ *   codes_base  + slots[e] * codes_slot_bytes   (likewise scales, zeros)
+ * and slots[e] == -1 marks a non-resident expert whose rows contribute zero.
+ */
+int w2a16_moe_gemv_slots(const void* a, int64_t stride_am,
+                         const int32_t* slots, int num_experts,
+                         const void* codes_base, int64_t codes_slot_bytes,
+                         const void* scales_base, int64_t scales_slot_bytes,
+                         const void* zeros_base, int64_t zeros_slot_bytes,
+                         const int32_t* topk_ids, const float* topk_w,
+                         void* c, int64_t stride_cm,
+                         int R, int N, int K,
+                         int top_k, int mul_routed_weight, int scale_bf16,
+                         unsigned int* err, void* stream);
+
+/* Workspace bytes the decode-layer entry points need for M tokens (h buffer + control words). */
+size_t w2a16_moe_layer_workspace_bytes(int M, int H, int I, int top_k);
+
+/*
+ * Full decode MoE layer: gate_up GEMV, SiLU(gate) * up, down GEMV * routed weight, sum over the
+ * top-k experts of each token, times routed_scaling_factor.
+ * Replaces MoeWNA16Method._apply_gemv — patches/ncontig_gemv.py:218-238 (serving patch:3358-3400):
+ * the two moe_gemv_int2_tab launches, the torch SiLU*mul and the torch top-k sum.
+ *
+ * x        bf16 [M, H] (row stride H); y bf16 [M, H] output
+ * topk_ids int32 [M * top_k], topk_w fp32 [M * top_k] (token-major)
+ * gate_up expert tensors: codes [H/16, 2I], scales [H/128, 2I], zeros [H/128, 2I/4] or NULL;
+ *          rows [0, I) are gate, [I, 2I) are up (gemv/test_gemv_tab.py:32)
+ * down expert tensors:    codes [I/16, H],  scales [I/128, H],  zeros [I/128, H/4] or NULL
+ * workspace >= w2a16_moe_layer_workspace_bytes(); it must be zero-filled before its first use and
+ *          is left zero-filled in its control words by every call.
+ * H % 128 == 0, I % 128 == 0.
+ */
+int w2a16_moe_decode_layer_tab(const void* x, int M, int H, int I, int top_k,
+                               const int32_t* topk_ids, const float* topk_w, int num_experts,
+                               const int64_t* wtab13, const int64_t* stab13, const int64_t* ztab13,
+                               const int64_t* wtab2, const int64_t* stab2, const int64_t* ztab2,
+                               int scale_bf16, float routed_scaling_factor,
+                               void* y, void* workspace, size_t workspace_bytes,
+                               unsigned int* err, void* stream);
+
+/* The decode layer over an int32 slot table into expert arenas (slot -1 = not resident). */
+int w2a16_moe_decode_layer_slots(const void* x, int M, int H, int I, int top_k,
+                                 const int32_t* topk_ids, const float* topk_w,
+                                 const int32_t* slots, int num_experts,
+                                 const void* codes13, int64_t codes13_slot_bytes,
+                                 const void* scales13, int64_t scales13_slot_bytes,
+                                 const void* zeros13, int64_t zeros13_slot_bytes,
+                                 const void* codes2, int64_t codes2_slot_bytes,
+                                 const void* scales2, int64_t scales2_slot_bytes,
+                                 const void* zeros2, int64_t zeros2_slot_bytes,
+                                 int scale_bf16, float routed_scaling_factor,
+                                 void* y, void* workspace, size_t workspace_bytes,
+                                 unsigned int* err, void* stream);
+
+/*
+ * Loader relayout, bit-exact: uint8 [E, N, K/4] (value k at bits 2*(k%4) of byte k/4) ->
+ * int32 [E, K/16, N]. Replaces to_word_ncontig() — gemv/moe_gemv_int2_tab.py:100-109, applied in
+ * process_weights_after_loading (patches/ncontig_gemv.py:169-204).
+ */
+int w2a16_to_word_ncontig(const void* src_u8, void* dst_i32, int E, int N, int K, void* stream);
+
+/*
+ * Row gather through an address table: out[i, :] = the row_bytes bytes at tab[ids[i]].
+ * Replaces _gather_rows_tab_kernel — patches/placement.py:34-43 (arena fill,
+ * gemv/expert_elastic.py:45-51). row_bytes % 16 == 0, addresses 16-byte aligned.
+ */
+int w2a16_gather_rows_tab(const int64_t* tab, const int32_t* ids, int n, void* out, int64_t row_bytes,
+                          void* stream);
+
+/*
+ * INT8 dense projection GEMV: y[m, n] = sum_k (q[k, n] - zero) * s[k / group, n] * x[m, k].
+ * q packed 4 per int32 along K, int32 [K/4, N] (the auto_gptq layout of scripts/requant_int8.py:32-50);
+ * scales f16 [K/group, N] (group == K: one scale per output channel). Replaces the GPTQ Marlin INT8
+ * call SGLang makes for the dense projections (third party; docs/DECODE_PERF_PLAN.md:29).
+ * x bf16 [M, K] (row stride stride_xm), y bf16 [M, N] (row stride stride_ym).
+ * K % 128 == 0, N % 4 == 0, group % 128 == 0 and K % group == 0.
+ */
+int w2a16_int8_gemv(const void* x, int64_t stride_xm, const int32_t* qweight, const void* scales,
+                    int group, int zero, int M, int K, int N, void* y, int64_t stride_ym,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* Workspace bytes w2a16_int8_gemv needs (split-K partials + counters; zero-filled before first use). */
+size_t w2a16_int8_workspace_bytes(int M, int K, int N);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* W2A16_MOE_H */

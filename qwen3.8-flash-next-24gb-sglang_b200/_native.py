@@ -1,0 +1,83 @@
+"""ctypes binding of ``lib/libw2a16_moe.so`` (the C ABI of ``include/w2a16_moe.h``).
+
+The library is required: importing the ops without it raises immediately. There is no Python or
+CPU fallback for any kernel; a missing library or a non-CUDA tensor is an error.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "lib", "libw2a16_moe.so")
+
+STATUS = {
+    0: "ok", 1: "unsupported shape", 2: "misaligned stride or base address", 3: "CUDA launch failed",
+    4: "invalid argument", 5: "workspace missing or too small", 6: "no usable sm_100 device",
+}
+
+# name -> (restype, argtypes); mirrors include/w2a16_moe.h one for one
+c_i32, c_i64, c_f32, c_sz, c_vp = ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t, ctypes.c_void_p
+SIGNATURES = {
+    "w2a16_version": (ctypes.c_char_p, []),
+    "w2a16_status_string": (ctypes.c_char_p, [c_i32]),
+    "w2a16_moe_gemv_tab": (c_i32, [c_vp, c_i64, c_vp, c_vp, c_vp, c_i32, c_vp, c_vp, c_vp, c_i64,
+                                   c_i32, c_i32, c_i32, c_i64, c_i64, c_i64, c_i32, c_i32, c_i32, c_vp, c_vp]),
+    "w2a16_moe_gemv_slots": (c_i32, [c_vp, c_i64, c_vp, c_i32, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64,
+                                     c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp]),
+    "w2a16_moe_layer_workspace_bytes": (c_sz, [c_i32, c_i32, c_i32, c_i32]),
+    "w2a16_moe_decode_layer_tab": (c_i32, [c_vp, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp, c_i32,
+                                           c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i32, c_f32,
+                                           c_vp, c_vp, c_sz, c_vp, c_vp]),
+    "w2a16_moe_decode_layer_slots": (c_i32, [c_vp, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp, c_vp, c_i32,
+                                             c_vp, c_i64, c_vp, c_i64, c_vp, c_i64,
+                                             c_vp, c_i64, c_vp, c_i64, c_vp, c_i64,
+                                             c_i32, c_f32, c_vp, c_vp, c_sz, c_vp, c_vp]),
+    "w2a16_to_word_ncontig": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_i32, c_vp]),
+    "w2a16_gather_rows_tab": (c_i32, [c_vp, c_vp, c_i32, c_vp, c_i64, c_vp]),
+    "w2a16_int8_gemv": (c_i32, [c_vp, c_i64, c_vp, c_vp, c_i32, c_i32, c_i32, c_i32, c_i32, c_vp, c_i64,
+                                c_vp, c_sz, c_vp]),
+    "w2a16_int8_workspace_bytes": (c_sz, [c_i32, c_i32, c_i32]),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+class W2A16Error(RuntimeError):
+    """A C-ABI entry point returned a non-zero status."""
+
+    def __init__(self, fn: str, status: int):
+        super().__init__(f"{fn} failed: status {status} ({STATUS.get(status, 'unknown')})")
+        self.status = status
+
+
+def lib():
+    """Load the shared library once; raise if it is missing (no fallback exists)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise RuntimeError(
+                    f"W2A16 CUDA library not found at {LIB_PATH}; build it with the package's build.py "
+                    "(there is no CPU fallback)")
+            h = ctypes.CDLL(LIB_PATH)
+            for name, (res, args) in SIGNATURES.items():
+                f = getattr(h, name)
+                f.restype = res
+                f.argtypes = args
+            _lib = h
+    return _lib
+
+
+def call(name: str, *args) -> None:
+    st = getattr(lib(), name)(*args)
+    if st != 0:
+        raise W2A16Error(name, st)
+
+
+def version() -> str:
+    return lib().w2a16_version().decode()

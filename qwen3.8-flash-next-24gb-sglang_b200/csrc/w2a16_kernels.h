@@ -1,0 +1,67 @@
+// Internal host-side declarations shared by the kernel translation units and the C ABI layer.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+#include "w2a16_common.cuh"
+
+namespace w2a16 {
+
+struct GemvArgs {
+  const void* a;
+  int64_t stride_am;
+  ExpertMap map;
+  const int32_t* ids;
+  const float* topk_w;
+  void* out;
+  int64_t stride_om;
+  int R, N, K, top_k;
+  int64_t stride_ww, stride_sg, stride_zg;
+  int mul_routed_weight;
+  int scale_bf16;
+  unsigned* err;
+  cudaStream_t stream;
+};
+
+int gemv_plain(const GemvArgs& g);
+int gemv_gateup_silu(const GemvArgs& g, int I, float* h, int64_t stride_hm);
+int gemv_down_sum(const GemvArgs& g, int M, float routed_scaling);
+
+// Fused persistent decode layer (w2a16_layer.cu).
+struct LayerArgs {
+  const void* x;          // bf16 [M, H]
+  int M, H, I, top_k;
+  const int32_t* ids;     // [M * top_k]
+  const float* topk_w;    // [M * top_k]
+  ExpertMap map13;        // gate_up: codes [H/16, 2I], scales [H/128, 2I], zeros [H/128, 2I/4]
+  ExpertMap map2;         // down:    codes [I/16, H],  scales [I/128, H],  zeros [I/128, H/4]
+  int scale_bf16;
+  float routed_scaling;
+  void* y;                // bf16 [M, H]
+  void* workspace;
+  size_t workspace_bytes;
+  unsigned* err;
+  cudaStream_t stream;
+};
+size_t layer_workspace_bytes(int M, int H, int I, int top_k);
+int decode_layer_two_pass(const LayerArgs& a);
+int decode_layer_fused(const LayerArgs& a);
+
+// INT8 dense GEMV (w2a16_int8.cu).
+struct Int8Args {
+  const void* x;          // bf16 [M, K]
+  int64_t stride_xm;
+  const int32_t* qweight; // int32 [K/4, N], 4 uint8 along K per word
+  const void* scales;     // f16 [K/g, N]
+  int group;              // K for per-output-channel scales
+  int zero;               // 128 = symmetric
+  int M, K, N;
+  void* y;                // bf16 [M, N]
+  int64_t stride_ym;
+  cudaStream_t stream;
+};
+int int8_gemv(const Int8Args& a, void* workspace, size_t workspace_bytes);
+size_t int8_workspace_bytes(int M, int K, int N);
+int to_word_ncontig(const void* src, void* dst, int E, int N, int K, cudaStream_t stream);
+int gather_rows_tab(const int64_t* tab, const int32_t* ids, int n, void* out, int64_t row_bytes, cudaStream_t stream);
+
+}  // namespace w2a16

@@ -1,0 +1,88 @@
+"""The C-ABI library: it loads, exports every function include/w2a16_moe.h declares, and rejects bad
+arguments with status codes before touching the device (no GPU needed)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "w2a16_moe.h")
+
+
+def header_functions():
+    txt = open(HEADER).read()
+    txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
+    return sorted(set(re.findall(r"\b(w2a16_[a-z0-9_]+)\s*\(", txt)))
+
+
+def test_header_declares_entry_points():
+    names = header_functions()
+    for n in ("w2a16_moe_gemv_tab", "w2a16_moe_gemv_slots", "w2a16_moe_decode_layer_tab",
+              "w2a16_moe_decode_layer_slots", "w2a16_to_word_ncontig", "w2a16_gather_rows_tab",
+              "w2a16_int8_gemv"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol(pkg):
+    lib = pkg._native.lib()
+    missing = [n for n in header_functions() if not hasattr(lib, n)]
+    assert not missing, missing
+    # and the Python binding covers every declared function
+    assert set(header_functions()) <= set(pkg._native.SIGNATURES)
+
+
+def test_version_and_status_strings(pkg):
+    assert "sm_100a" in pkg.version()
+    lib = pkg._native.lib()
+    assert lib.w2a16_status_string(0) == b"ok"
+    assert lib.w2a16_status_string(1) == b"unsupported shape"
+    assert lib.w2a16_status_string(99) == b"unknown status"
+
+
+def test_argument_errors_return_status(pkg):
+    lib = pkg._native.lib()
+    fake = ctypes.c_void_p(0x1000)
+    # K not a multiple of 128 -> shape error, before any launch
+    st = lib.w2a16_moe_gemv_tab(fake, 64, fake, fake, None, 8, fake, None, fake, 8, 1, 8, 64, 8, 8, 2,
+                                1, 0, 1, None, None)
+    assert st == 1
+    # N not a multiple of 4
+    st = lib.w2a16_moe_gemv_tab(fake, 128, fake, fake, None, 8, fake, None, fake, 6, 1, 6, 128, 6, 6, 2,
+                                1, 0, 1, None, None)
+    assert st == 1
+    # missing tables
+    st = lib.w2a16_moe_gemv_tab(fake, 128, None, None, None, 8, fake, None, fake, 8, 1, 8, 128, 8, 8, 2,
+                                1, 0, 1, None, None)
+    assert st == 4
+    # R == 0 is a no-op success
+    st = lib.w2a16_moe_gemv_tab(fake, 128, fake, fake, None, 8, fake, None, fake, 8, 0, 8, 128, 8, 8, 2,
+                                1, 0, 1, None, None)
+    assert st == 0
+    # decode layer: workspace too small
+    st = lib.w2a16_moe_decode_layer_slots(fake, 1, 256, 256, 2, fake, fake, fake, 4, fake, 4096, fake, 256,
+                                          None, 0, fake, 4096, fake, 256, None, 0, 0, 1.0, fake, fake, 16,
+                                          None, None)
+    assert st == 5
+    # decode layer: H not a multiple of 128
+    st = lib.w2a16_moe_decode_layer_slots(fake, 1, 200, 256, 2, fake, fake, fake, 4, fake, 4096, fake, 256,
+                                          None, 0, fake, 4096, fake, 256, None, 0, 0, 1.0, fake, fake, 1 << 20,
+                                          None, None)
+    assert st == 1
+    # slot form: misaligned arena base
+    st = lib.w2a16_moe_gemv_slots(fake, 128, fake, 4, ctypes.c_void_p(0x1004), 64, fake, 64, None, 0, fake, None,
+                                  fake, 8, 1, 8, 128, 1, 0, 1, None, None)
+    assert st == 2
+    # int8: bad group
+    st = lib.w2a16_int8_gemv(fake, 256, fake, fake, 100, 128, 1, 256, 64, fake, 64, fake, 1 << 20, None)
+    assert st == 1
+    # relayout: K not a multiple of 16
+    assert lib.w2a16_to_word_ncontig(fake, fake, 1, 8, 24, None) == 1
+    # gather: row bytes not a multiple of 16
+    assert lib.w2a16_gather_rows_tab(fake, fake, 2, fake, 24, None) == 2
+
+
+def test_workspace_sizes(pkg):
+    lib = pkg._native.lib()
+    assert lib.w2a16_moe_layer_workspace_bytes(1, 4096, 1536, 8) >= 8 * 1536 * 4
+    assert lib.w2a16_int8_workspace_bytes(1, 4096, 4096) >= 16 * 4096 * 4

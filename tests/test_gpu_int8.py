@@ -1,0 +1,27 @@
+"""GPU parity of the INT8 dense projection GEMV against the CPU oracle (scripts/requant_int8.py
+dequant rule). Bar: max relative error <= 1e-2 on bf16 outputs."""
+import pytest
+import torch
+
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 4096, 4096), (3, 1024, 512), (5, 384, 128)])
+def test_int8_per_channel(pkg, dev, M, K, N):
+    qw, sc = pkg.synth.make_int8_dense(K, N, seed=M, device=dev, gen_device="cpu")
+    x = pkg.synth.make_activation(M, K, seed=M, device=dev, gen_device="cpu")
+    y = pkg.int8_gemv(x, qw, sc)
+    ref = O.int8_gemv(x.cpu(), qw.cpu(), sc.cpu())
+    assert O.max_rel_err(y.float().cpu(), ref) < 1e-2
+
+
+def test_int8_grouped_scales_and_repeat(pkg, golden, dev):
+    """The reference packing with g128 scales (pack_int8_gptq), called twice (ticket counters reset)."""
+    qw, sc = golden["int8_qw"].to(dev), golden["int8_sc"].to(dev)
+    x = torch.randn(2, qw.shape[0] * 4, generator=torch.Generator().manual_seed(1)).to(torch.bfloat16)
+    ref = O.int8_gemv(x, golden["int8_qw"], golden["int8_sc"])
+    for _ in range(2):
+        y = pkg.int8_gemv(x.to(dev), qw, sc)
+        assert O.max_rel_err(y.float().cpu(), ref) < 1e-2

@@ -1,0 +1,121 @@
+"""The CPU oracle against golden vectors produced by the reference's own code
+(tests/golden/make_golden.py) and against the reference's known-answer checks."""
+import torch
+
+import oracle as O
+
+# the reference's GEMV bar (series-0002:2231-2232) and bf16 output rounding
+TOL_GEMV = 1e-2
+
+
+def test_relayout_bit_exact(golden):
+    assert torch.equal(O.to_word_ncontig(golden["relayout_in"]), golden["relayout_out"])
+
+
+def test_word_and_byte_packing_bit_exact(golden):
+    q = golden["zp_words_vals"]
+    assert torch.equal(O.pack_words_along_k(q), golden["zp_words"])
+    assert torch.equal(O.pack_2bit_along_last(q), golden["zp_bytes"])
+
+
+def test_to_word_ncontig_known_answer():
+    """series-0002:1989-2010: bit-exact, every value at bits 2*(k%16) of word k//16, invertible."""
+    gen = torch.Generator().manual_seed(7)
+    for e, n, k in ((3, 64, 256), (2, 640, 2560), (1, 16, 64)):
+        q = torch.randint(0, 4, (e, n, k), generator=gen)
+        byte = O.pack_2bit_along_last(q)
+        word = O.to_word_ncontig(byte)
+        assert word.dtype == torch.int32 and word.shape == (e, k // 16, n) and word.is_contiguous()
+        assert torch.equal(word, O.pack_words_along_k(q).transpose(1, 2).contiguous())
+        for kk in (0, 1, 15, 16, 17, k - 1):
+            assert torch.equal((word[:, kk // 16, :] >> (2 * (kk % 16))) & 3, q[:, :, kk].to(torch.int32))
+        back = word.view(torch.uint8).view(e, k // 16, n, 4).permute(0, 2, 1, 3).reshape(e, n, k // 4)
+        assert torch.equal(back, byte)
+
+
+def test_unpack_known_answer():
+    """series-0002:2013-2081 / tools/test_group_layout.py:20-38: unpack of words is bit-exact."""
+    gen = torch.Generator().manual_seed(7)
+    for k, n, gs in ((2560, 640, 128), (640, 2560, 128), (256, 64, 64)):
+        vals = torch.randint(0, 4, (k, n), dtype=torch.int32, generator=gen)
+        sc = (torch.rand(k // gs, n, generator=gen) * 0.02 + 0.001).float()
+        words = O.pack_words_along_k(vals.T.contiguous()).T.contiguous()     # [K/16, N]
+        assert torch.equal(O.unpack_words(words), vals)
+        ref = (vals.float() - 2) * sc.repeat_interleave(gs, dim=0)
+        assert torch.equal(O.dequant(words, sc, group=gs), ref)
+
+
+def test_gemv_matches_reference_triton(golden):
+    for s in ("f16", "bf16"):
+        g = lambda k: golden[f"tab_{s}_{k}"]
+        o13 = O.gemv_tab(g("x13"), g("w13"), g("s13"), g("ids"), g("rw"), 3, False)
+        o2 = O.gemv_tab(g("x2"), g("w2"), g("s2"), g("ids"), g("rw"), 1, True)
+        assert O.max_rel_err(g("o13").float(), o13) < TOL_GEMV
+        assert O.max_rel_err(g("o2").float(), o2) < TOL_GEMV
+        assert O.norm_rel_err(g("o13").float(), o13) < 5e-3
+
+
+def test_byte_gemv_matches_reference_triton(golden):
+    ob = O.gemv_byte_tab(golden["byte_x"], golden["byte_q"], golden["byte_s"], golden["byte_ids"])
+    assert O.max_rel_err(golden["byte_out"], ob) < 1e-5
+
+
+def test_per_group_zero_points_match_reference_helpers(golden):
+    """make_int2_experts(has_zp=True) (series-0002:1936-1954): loader bytes + qzeros -> word layout ->
+    oracle dequant reproduces the reference's bf16 dequantized weights exactly."""
+    for w in ("w1", "w2"):
+        words = O.to_word_ncontig(golden[f"zp_{w}_q"])
+        sc = golden[f"zp_{w}_s"].transpose(1, 2).contiguous()
+        zn = O.zeros_to_ncontig(golden[f"zp_{w}_zp"])
+        deq = O.dequant(words, sc, zn)
+        assert torch.equal(deq.to(torch.bfloat16), golden[f"zp_{w}_ref"].transpose(1, 2))
+
+
+def test_moe_layer_matches_reference_torch_moe(golden):
+    """torch_moe (series-0002:1957-1973, bf16 math, softmax without renormalisation) vs the fp32 oracle."""
+    topk = int(golden["zp_topk"])
+    words13 = O.to_word_ncontig(golden["zp_w1_q"]); s13 = golden["zp_w1_s"].transpose(1, 2).contiguous()
+    words2 = O.to_word_ncontig(golden["zp_w2_q"]); s2 = golden["zp_w2_s"].transpose(1, 2).contiguous()
+    z13 = O.zeros_to_ncontig(golden["zp_w1_zp"]); z2 = O.zeros_to_ncontig(golden["zp_w2_zp"])
+    ids, w = O.route_topk(golden["zp_score"].float(), topk, renormalize=False)
+    y = O.moe_layer(golden["zp_a"], words13, s13, words2, s2, ids, w, z13=z13, z2=z2)
+    assert O.max_rel_err(golden["zp_moe"].float(), y) < 2e-2      # TOL atol 1e-3 / rtol 2e-2 (:1916)
+
+
+def test_int8_formula_matches_reference(golden):
+    """unpack_int8_gptq (scripts/requant_int8.py:53-63) == oracle unpack/dequant; GEMV consistent."""
+    qw, qz, sc = golden["int8_qw"], golden["int8_qz"], golden["int8_sc"]
+    assert (qz == 0x7F7F7F7F).all()                        # symmetric: stored zero - 1 = 127
+    q = O.int8_unpack(qw).float()
+    W = (q - 128.0) * sc.float().repeat_interleave(128, dim=0)        # [K, N]
+    assert torch.equal(W.T.contiguous(), golden["int8_deq"])
+    x = torch.randn(2, qw.shape[0] * 4, generator=torch.Generator().manual_seed(3))
+    y = O.int8_gemv(x, qw, sc)
+    assert O.max_rel_err(y, x @ golden["int8_deq"].T) < 1e-5
+
+
+def test_int8_pack_roundtrip():
+    gen = torch.Generator().manual_seed(11)
+    q = torch.randint(0, 256, (256, 64), generator=gen)
+    assert torch.equal(O.int8_unpack(O.int8_pack(q)), q.to(torch.int32))
+
+
+def test_zero_point_relayout_roundtrip():
+    gen = torch.Generator().manual_seed(2)
+    zp = torch.randint(0, 4, (3, 64, 4), generator=gen)           # [E, N, K/g]
+    qz = O.pack_zeros(zp)                                         # [E, N/4, K/g]
+    nc = O.zeros_to_ncontig(qz)                                   # [E, K/g, N/4]
+    assert torch.equal(O.unpack_zeros_nc(nc), zp.transpose(1, 2).to(torch.int32))
+
+
+def test_slot_masking_semantics():
+    gen = torch.Generator().manual_seed(4)
+    E, K, N = 4, 128, 32
+    w = torch.randint(-(2 ** 31), 2 ** 31, (E, K // 16, N), dtype=torch.int32, generator=gen)
+    s = torch.rand(E, K // 128, N, generator=gen).half()
+    a = torch.randn(1, K, generator=gen).to(torch.bfloat16)
+    ids = torch.tensor([0, 3, 1], dtype=torch.int32)
+    slots = torch.tensor([2, -1, 0, 1], dtype=torch.int32)
+    o = O.gemv_tab(a, w, s, ids, None, 3, False, slots=slots)
+    assert torch.equal(o[2], torch.zeros(N))                     # expert 1 not resident
+    assert torch.allclose(o[0], O.gemv_tab(a, w, s, torch.tensor([2], dtype=torch.int32), None, 1, False)[0])
