@@ -135,6 +135,35 @@ int w2a16_moe_decode_layer_slots(const void* x, int M, int H, int I, int top_k,
                                  unsigned int* err, void* stream);
 
 /*
+ * No counterpart in the reference: this entry point exists only in this library.
+ *
+ * The decode layer over a slot table (same arguments and result as w2a16_moe_decode_layer_slots) for
+ * callers that cannot allocate device memory and so cannot hand in a workspace: a host that reaches
+ * this call while its stream is being captured into a CUDA graph (cudaMalloc is not allowed during a
+ * global-mode capture), or a serving process whose device memory is fully reserved by its own pool at
+ * start-up. It calls no cudaMalloc, cudaFree or allocating library routine. Its workspace is a fixed
+ * array of W2A16_NOALLOC_SCRATCH_BYTES bytes inside the library that every GPU loading the library
+ * holds until the process exits; layers needing more (w2a16_moe_layer_workspace_bytes(M, H, I, top_k)
+ * > W2A16_NOALLOC_SCRATCH_BYTES, e.g. M * top_k * I above ~262,000) return W2A16_ERR_WORKSPACE.
+ * The first call on a device looks up that array's device address for the calling thread's current
+ * device (which must own `stream`); make that first call before any stream capture. All calls share
+ * the one array: calls that overlap on the GPU (different streams, or concurrent graph replays) race
+ * and must not be issued.
+ */
+#define W2A16_NOALLOC_SCRATCH_BYTES (1u << 20)
+int w2a16_moe_decode_layer_slots_noalloc(const void* x, int M, int H, int I, int top_k,
+                                         const int32_t* topk_ids, const float* topk_w,
+                                         const int32_t* slots, int num_experts,
+                                         const void* codes13, int64_t codes13_slot_bytes,
+                                         const void* scales13, int64_t scales13_slot_bytes,
+                                         const void* zeros13, int64_t zeros13_slot_bytes,
+                                         const void* codes2, int64_t codes2_slot_bytes,
+                                         const void* scales2, int64_t scales2_slot_bytes,
+                                         const void* zeros2, int64_t zeros2_slot_bytes,
+                                         int scale_bf16, float routed_scaling_factor, void* y,
+                                         unsigned int* err, void* stream);
+
+/*
  * Loader relayout, bit-exact: uint8 [E, N, K/4] (value k at bits 2*(k%4) of byte k/4) ->
  * int32 [E, K/16, N]. Replaces to_word_ncontig() — gemv/moe_gemv_int2_tab.py:100-109, applied in
  * process_weights_after_loading (patches/ncontig_gemv.py:169-204).

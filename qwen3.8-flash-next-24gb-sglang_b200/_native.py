@@ -34,6 +34,10 @@ SIGNATURES = {
                                              c_vp, c_i64, c_vp, c_i64, c_vp, c_i64,
                                              c_vp, c_i64, c_vp, c_i64, c_vp, c_i64,
                                              c_i32, c_f32, c_vp, c_vp, c_sz, c_vp, c_vp]),
+    "w2a16_moe_decode_layer_slots_noalloc": (c_i32, [c_vp, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp, c_vp, c_i32,
+                                                     c_vp, c_i64, c_vp, c_i64, c_vp, c_i64,
+                                                     c_vp, c_i64, c_vp, c_i64, c_vp, c_i64,
+                                                     c_i32, c_f32, c_vp, c_vp, c_vp]),
     "w2a16_to_word_ncontig": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_i32, c_vp]),
     "w2a16_gather_rows_tab": (c_i32, [c_vp, c_vp, c_i32, c_vp, c_i64, c_vp]),
     "w2a16_int8_gemv": (c_i32, [c_vp, c_i64, c_vp, c_vp, c_i32, c_i32, c_i32, c_i32, c_i32, c_vp, c_i64,
