@@ -142,15 +142,15 @@ int w2a16_moe_decode_layer_slots(const void* x, int M, int H, int I, int top_k,
  * this call while its stream is being captured into a CUDA graph (cudaMalloc is not allowed during a
  * global-mode capture), or a serving process whose device memory is fully reserved by its own pool at
  * start-up. It calls no cudaMalloc, cudaFree or allocating library routine. Its workspace is a fixed
- * array of W2A16_NOALLOC_SCRATCH_BYTES bytes inside the library that every GPU loading the library
+ * array of W2A16_NOALLOC_SCRATCH_BYTES (4 MiB) inside the library that every GPU loading the library
  * holds until the process exits; layers needing more (w2a16_moe_layer_workspace_bytes(M, H, I, top_k)
- * > W2A16_NOALLOC_SCRATCH_BYTES, e.g. M * top_k * I above ~262,000) return W2A16_ERR_WORKSPACE.
+ * > W2A16_NOALLOC_SCRATCH_BYTES; at I=1536, top-8 that is M > 17) return W2A16_ERR_WORKSPACE.
  * The first call on a device looks up that array's device address for the calling thread's current
  * device (which must own `stream`); make that first call before any stream capture. All calls share
  * the one array: calls that overlap on the GPU (different streams, or concurrent graph replays) race
  * and must not be issued.
  */
-#define W2A16_NOALLOC_SCRATCH_BYTES (1u << 20)
+#define W2A16_NOALLOC_SCRATCH_BYTES (4u << 20)
 int w2a16_moe_decode_layer_slots_noalloc(const void* x, int M, int H, int I, int top_k,
                                          const int32_t* topk_ids, const float* topk_w,
                                          const int32_t* slots, int num_experts,

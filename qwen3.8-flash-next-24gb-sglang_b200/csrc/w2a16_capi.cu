@@ -114,6 +114,8 @@ int w2a16_moe_decode_layer_slots(const void* x, int M, int H, int I, int top_k, 
   if (!a16(codes13) || !a16(scales13) || !a16(codes2) || !a16(scales2)) return W2A16_ERR_ALIGN;
   if (codes13_slot_bytes % 16 || scales13_slot_bytes % 16 || codes2_slot_bytes % 16 || scales2_slot_bytes % 16)
     return W2A16_ERR_ALIGN;
+  if (zeros13 && (!a16(zeros13) || !a16(zeros2) || zeros13_slot_bytes % 16 || zeros2_slot_bytes % 16))
+    return W2A16_ERR_ALIGN;
   LayerArgs a{};
   a.x = x; a.M = M; a.H = H; a.I = I; a.top_k = top_k; a.ids = topk_ids; a.topk_w = topk_w;
   a.map13 = slot_map(slots, num_experts, codes13, codes13_slot_bytes, scales13, scales13_slot_bytes, zeros13,

@@ -43,7 +43,6 @@ struct LayerArgs {
   cudaStream_t stream;
 };
 size_t layer_workspace_bytes(int M, int H, int I, int top_k);
-int decode_layer_two_pass(const LayerArgs& a);
 int decode_layer_fused(const LayerArgs& a);
 
 // INT8 dense GEMV (w2a16_int8.cu).

@@ -1,40 +1,650 @@
-// Decode MoE layer: gate_up GEMV + SiLU*mul, down GEMV * routed weight, sum over top-k
-// (the composite of patches/ncontig_gemv.py:218-238).
+// Decode MoE layer in one cooperative kernel: gate_up GEMV + SiLU*mul, down GEMV * routed weight,
+// sum over the top-k experts of each token (the composite of patches/ncontig_gemv.py:218-238).
+//
+// Phase 1 (gate_up). Work items are (row r, block of 32 h-columns, 2 groups of K): 32 lanes = 2 groups
+// x 16 column quads, quads 0-7 over the 32 gate columns and 8-15 over the matching 32 up columns, so a
+// warp reads two 128-byte runs per word row. The R * I/32 * ceil(G1/2) items are cut into one
+// contiguous, equal-sized range per CTA; a CTA's 16 warps share its range round-robin and leave one
+// 64-float partial per item in shared memory. Once the range is done the CTA sums the partials of each
+// h-block it touched in item order (deterministic) and writes (gate, up) to one of two part slots in
+// the workspace: slot 0 when the block starts in this CTA, slot 1 when it started in the previous CTA
+// (a range is at least one block long, so no block spans more than two CTAs); a block wholly inside the
+// range also zeroes its slot 1.
+//
+// One grid barrier (bounded wait), then phase 2 (down). Work units are (token m, block of 32 output
+// columns): top_k rows x ceil(G2/4) K-parts = items of 4 groups x 8 column quads. Units are dealt
+// round-robin to CTAs; their code data were already prefetched into the warps' staging buffers while
+// phase 1 finished. The CTA builds the h tables of its units' rows, h = silu(g0 + g1) * (u0 + u1) from
+// the part slots, computes the items, and reduces each unit's top_k x K-part partials in fixed order in
+// shared memory into y. No atomics beyond the barrier, no ticket chains.
+//
+// Every lane streams its own item data (8 x 16-byte code vectors, 8 bytes of scales, the word holding
+// its zero-point byte) into a per-warp ring of kStages buffers with cp.async, so the next items are in
+// flight while the current one is reduced.
 #include "w2a16_kernels.h"
 
 namespace w2a16 {
+namespace {
 
-// Workspace layout (bytes): [0, 256): control words (error flags, counters); then h fp32 [R, I].
+constexpr int kThreads = 512;
+constexpr int kWarps = kThreads / 32;
+constexpr int kStages = 2;
+constexpr unsigned kSpinLimit = 1u << 22;                    // polls before a wait gives up
+constexpr int kStageBytes = 4096 + 256 + 64;                 // codes + scales + zero-point windows
+
+struct Geo {
+  int M, H, I, top_k, R;
+  int G1, G2;          // groups along K of gate_up (H/128) and down (I/128)
+  int nb1, kp1;        // h-blocks per row (I/32), items per h-block (ceil(G1/2))
+  int nb2, kp2;        // output blocks per token (H/32), K-parts per row (ceil(G2/4))
+  int n1;              // phase-1 items
+  int u2, s2;          // phase-2 units (M * nb2), items per unit (top_k * kp2)
+  int grid;            // CTAs
+  int max_range;       // max phase-1 items per CTA
+  int max_units;       // max phase-2 units per CTA
+};
+
+Geo make_geo(int M, int H, int I, int top_k, int grid_cap) {
+  Geo g{};
+  g.M = M; g.H = H; g.I = I; g.top_k = top_k; g.R = M * top_k;
+  g.G1 = H / kGroup; g.G2 = I / kGroup;
+  g.nb1 = I / 32; g.kp1 = (g.G1 + 1) / 2;
+  g.nb2 = H / 32; g.kp2 = (g.G2 + 3) / 4;
+  g.n1 = g.R * g.nb1 * g.kp1;
+  g.u2 = M * g.nb2; g.s2 = top_k * g.kp2;
+  const int nblocks = g.R * g.nb1;                  // a CTA range must cover at least one h-block
+  g.grid = grid_cap < nblocks ? grid_cap : nblocks;
+  if (g.grid < 1) g.grid = 1;
+  g.max_range = (g.n1 + g.grid - 1) / g.grid;
+  g.max_units = (g.u2 + g.grid - 1) / g.grid;
+  return g;
+}
+
+__host__ __device__ __forceinline__ size_t token_table_bytes(int K) {
+  return ((size_t)(K / 16) * kXRegs * 4 + (size_t)(K / kGroup) * 8 + 15) & ~size_t(15);
+}
+
+struct SmemPlan {
+  size_t tabs, stages, mail1, mail2, rows, split, bars, total;
+};
+
+// Per routed row, resolved once per CTA: expert code / scale / zero-point bases of gate_up and down.
+struct RowPtr {
+  const uint32_t* w[2];
+  const char* s[2];
+  const uint8_t* z[2];
+  int ok[2];
+};
+
+SmemPlan smem_plan(const Geo& g) {
+  SmemPlan s{};
+  const size_t t1 = (size_t)g.M * token_table_bytes(g.H);
+  const size_t t2 = (size_t)g.max_units * g.top_k * token_table_bytes(g.I);
+  s.tabs = t1 > t2 ? t1 : t2;
+  s.stages = (size_t)kWarps * kStages * kStageBytes;
+  s.mail1 = (size_t)g.max_range * 64 * 4;
+  s.mail2 = (size_t)g.max_units * g.s2 * 32 * 4;
+  s.rows = ((size_t)g.R * sizeof(RowPtr) + 15) & ~size_t(15);
+  s.split = ((size_t)g.R * g.nb1 + 15) & ~size_t(15);
+  s.bars = (size_t)kWarps * kStages * 8;
+  s.total = s.tabs + s.stages + s.mail1 + s.mail2 + s.rows + s.split + s.bars;
+  return s;
+}
+
+struct FusedParams {
+  const __nv_bfloat16* x;
+  const int32_t* ids;
+  const float* topk_w;
+  ExpertMap map13, map2;
+  int scale_bf16;
+  float rsf;
+  __nv_bfloat16* y;
+  Geo geo;
+  size_t off_stages, off_mail1, off_mail2, off_rows, off_split, off_bars;
+  unsigned* bar_count;   // grid barrier
+  unsigned* bar_gen;
+  float* hfin;           // [R][I] h of h-blocks computed wholly inside one CTA
+  float* hpart;          // [2 sides][R][2 (gate, up)][I] partial sums of h-blocks split across two CTAs
+  unsigned* err;
+};
+
+__device__ __forceinline__ XTable table_at(unsigned char* base, int K) {
+  XTable t;
+  t.pairs = reinterpret_cast<uint32_t*>(base);
+  t.m64x = reinterpret_cast<int*>(base + (size_t)(K / 16) * kXRegs * 4);
+  t.scl = reinterpret_cast<float*>(t.m64x + K / kGroup);
+  return t;
+}
+
+__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// ----------------------------------------------------------------------------- bulk-copy staging
+// Each warp streams its items through a ring of kStages shared-memory buffers with cp.async.bulk (the
+// TMA engine): one 128-byte copy per (word row, column run), completion counted on one mbarrier per
+// buffer. The copies bypass the load/store pipeline, so the x / id / h loads of the kernel never queue
+// behind the weight stream.
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_tx(uint32_t bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, unsigned parity) {
+  unsigned ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for the phase with the given parity (error bit 1 if it never completes).
+__device__ __forceinline__ void mbar_wait(uint32_t bar, unsigned parity, unsigned* err) {
+  unsigned it = 0;
+  while (!mbar_try(bar, parity)) {
+    if (++it > kSpinLimit) {
+      flag_error(err, 2u);
+      return;
+    }
+  }
+}
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, unsigned bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
+// Stage buffer layout: codes [32 word rows x 128 B] (gate_up: 16 rows x 256 B = gate run | up run),
+// then scales [4 x 64 B], then zero-point windows [4 x 16 B].
+constexpr int kCodeBytes = 4096;
+constexpr int kScaleOff = kCodeBytes;
+constexpr int kZeroOff = kCodeBytes + 256;
+// One entry of a warp's work list.
+struct Work {
+  int kind;   // 0 none, 1 gate_up, 2 down
+  int r, b, kp;
+  int slot;   // mailbox index within the CTA
+  int unit;   // phase 2: unit slot within the CTA
+  int jr;     // phase 2: row index within the token
+};
+
+struct WarpList {
+  int a;      // CTA's phase-1 range start
+  int n1w;    // phase-1 items of this warp
+  int nu;     // phase-2 units of this CTA
+  int n2w;    // phase-2 items of this warp per unit
+  __device__ int total() const { return n1w + nu * n2w; }
+};
+
+__device__ __forceinline__ WarpList warp_list(const Geo& g, int cta, int warp) {
+  WarpList L;
+  const long long a = (long long)cta * g.n1 / g.grid, b = (long long)(cta + 1) * g.n1 / g.grid;
+  L.a = (int)a;
+  const int range = (int)(b - a);
+  L.n1w = range > warp ? (range - warp + kWarps - 1) / kWarps : 0;
+  L.nu = cta < g.u2 ? (g.u2 - cta + g.grid - 1) / g.grid : 0;
+  L.n2w = g.s2 > warp ? (g.s2 - warp + kWarps - 1) / kWarps : 0;
+  return L;
+}
+
+__device__ __forceinline__ Work work_at(const Geo& g, const WarpList& L, int cta, int warp, int t) {
+  Work w{};
+  if (t < L.n1w) {
+    const int i = L.a + warp + kWarps * t;
+    const int per_row = g.nb1 * g.kp1;
+    w.kind = 1;
+    w.r = i / per_row;
+    const int rem = i - w.r * per_row;
+    w.b = rem / g.kp1;
+    w.kp = rem - w.b * g.kp1;
+    w.slot = i - L.a;
+    return w;
+  }
+  const int t2 = t - L.n1w;
+  if (L.n2w == 0 || t2 >= L.nu * L.n2w) return w;
+  const int q = t2 / L.n2w, k = t2 - q * L.n2w;
+  const int u = cta + g.grid * q, j = warp + kWarps * k;
+  const int m = u / g.nb2;
+  w.kind = 2;
+  w.b = u - m * g.nb2;
+  w.jr = j / g.kp2;
+  w.kp = j - w.jr * g.kp2;
+  w.r = m * g.top_k + w.jr;
+  w.unit = q;
+  w.slot = q * g.s2 + j;
+  return w;
+}
+
+// Issue the bulk copies of work item w into stage buffer `st` (lane j issues copy j; lane 0 first
+// announces the byte count on the buffer's mbarrier). Rows of a non-resident expert, groups past K and
+// list entries past the end copy nothing, and their phase completes on the arrival alone.
+__device__ __forceinline__ void issue_work(const FusedParams& p, const Work& w, int lane, unsigned char* st,
+                                           uint32_t bar, const RowPtr* rows) {
+  const Geo& g = p.geo;
+  const int mi = w.kind - 1;
+  const bool live = w.kind != 0 && rows[w.r].ok[mi];
+  const int G = w.kind == 1 ? g.G1 : g.G2;
+  const int gpi = w.kind == 1 ? 2 : 4;                       // groups per item
+  const int g0 = w.kp * gpi;
+  const int ng = live ? (G - g0 < gpi ? G - g0 : gpi) : 0;   // valid groups
+  const int runs = w.kind == 1 ? 2 : 1;                      // column runs per word row (gate, up)
+  // copies: ng*8*runs code runs (128 B), ng*runs scale runs (64 B), ng*runs zero windows (16 B)
+  const bool hz = live && rows[w.r].z[mi] != nullptr;
+  const unsigned bytes = (unsigned)(ng * runs) * (8u * 128u + 64u + (hz ? 16u : 0u));
+  if (lane == 0) mbar_arrive_tx(bar, bytes);
+  __syncwarp();
+  if (!live || ng == 0) return;
+  const RowPtr& rp = rows[w.r];
+  const int N = w.kind == 1 ? 2 * g.I : g.H;
+  const uint32_t sdst = smem_u32(st);
+  const int ncode = ng * 8 * runs;
+  for (int c = lane; c < ncode + 2 * ng * runs; c += 32) {
+    if (c < ncode) {
+      int gi, k, side;
+      if (runs == 2) { gi = c >> 4; k = (c >> 1) & 7; side = c & 1; }
+      else { gi = c >> 3; k = c & 7; side = 0; }
+      const int col = (side ? g.I : 0) + w.b * 32;
+      const uint32_t* src = rp.w[mi] + (int64_t)(8 * (g0 + gi) + k) * N + col;
+      const uint32_t dst = sdst + (uint32_t)(((8 * gi + k) * runs + side) * 128);
+      bulk_g2s(dst, src, 128u, bar);
+    } else {
+      const int c2 = c - ncode;                              // scale runs then zero windows
+      const int which = c2 / (ng * runs), idx = c2 - which * (ng * runs);
+      const int gi = idx / runs, side = idx - gi * runs;
+      const int col = (side ? g.I : 0) + w.b * 32;
+      if (which == 0) {
+        bulk_g2s(sdst + kScaleOff + (gi * runs + side) * 64, rp.s[mi] + ((int64_t)(g0 + gi) * N + col) * 2, 64u, bar);
+      } else if (hz) {
+        const int64_t zoff = (int64_t)(g0 + gi) * (N / 4) + col / 4;
+        bulk_g2s(sdst + kZeroOff + (gi * runs + side) * 16, rp.z[mi] + (zoff & ~int64_t(15)), 16u, bar);
+      }
+    }
+  }
+}
+
+// 4 columns x 1 group of this lane against a pair table; codes, scales and zero points from the stage
+// buffer. gi = the lane's group within the item, qq = its 16-byte column unit within a word row.
+__device__ __forceinline__ void dot_stage(const unsigned char* st, int row_bytes, int gi, int qq, int run, int q8,
+                                          const XTable& tb, int gl, bool sbf, bool has_z, int zsh, float (&v)[4]) {
+  int acc[4][4];
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[c][j] = 0;
+  const unsigned char* rows = st + (size_t)(8 * gi) * row_bytes + qq * 16;
+#pragma unroll 2
+  for (int k = 0; k < 8; ++k) {
+    const uint4 w = *reinterpret_cast<const uint4*>(rows + k * row_bytes);
+    const uint4* xp = reinterpret_cast<const uint4*>(tb.pairs + (gl * 8 + k) * kXRegs);
+    const uint4 xa = xp[0], xb = xp[1];
+    const uint32_t xr[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+    word_dot(w.x, xr, acc[0]);
+    word_dot(w.y, xr, acc[1]);
+    word_dot(w.z, xr, acc[2]);
+    word_dot(w.w, xr, acc[3]);
+  }
+  const uint2 sr = *reinterpret_cast<const uint2*>(st + kScaleOff + run * 64 + q8 * 8);
+  float s[4];
+  if (sbf) {
+    const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&sr.x);
+    const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&sr.y);
+    s[0] = __low2float(a); s[1] = __high2float(a); s[2] = __low2float(b); s[3] = __high2float(b);
+  } else {
+    const __half2 a = *reinterpret_cast<const __half2*>(&sr.x);
+    const __half2 b = *reinterpret_cast<const __half2*>(&sr.y);
+    s[0] = __low2float(a); s[1] = __high2float(a); s[2] = __low2float(b); s[3] = __high2float(b);
+  }
+  const uint32_t zbyte = has_z ? (uint32_t)st[kZeroOff + run * 16 + zsh + q8] : 0u;
+  const int m64x = tb.m64x[gl];
+  const float scl = tb.scl[gl];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const int zp = has_z ? (int)((zbyte >> (2 * c)) & 3u) : 2;
+    const int T = combine_classes(acc[c]) + zp * m64x;
+    v[c] = (float)T * (s[c] * scl);
+  }
+}
+
+// h-block blk (items [blk*kp1, (blk+1)*kp1)) is split when a CTA range boundary falls strictly inside it.
+__device__ __forceinline__ bool block_split(const Geo& g, int blk) {
+  const long long lo = (long long)blk * g.kp1, hi = lo + g.kp1;
+  long long c = lo * g.grid / g.n1;
+  for (int k = 0; k < 3; ++k, ++c) {
+    const long long a = c * g.n1 / g.grid;
+    if (a > lo && a < hi) return true;
+  }
+  return false;
+}
+
+// All CTAs arrive; thread 0 of each CTA calls this. Gives up after kSpinLimit polls (error bit 1).
+__device__ void grid_barrier(unsigned* count, unsigned* gen, unsigned ncta, unsigned* err) {
+  const unsigned g0 = ld_acquire(gen);
+  __threadfence();
+  if (atomicAdd(count, 1u) == ncta - 1) {
+    *count = 0u;
+    __threadfence();
+    atomicAdd(gen, 1u);
+  } else {
+    unsigned it = 0;
+    while (ld_acquire(gen) == g0) {
+      if (++it > kSpinLimit) {
+        flag_error(err, 2u);
+        break;
+      }
+      __nanosleep(it < 32 ? 32 : 128);
+    }
+  }
+  __threadfence();
+}
+
+__device__ __forceinline__ void process_work(const FusedParams& p, const Work& w, int lane, const unsigned char* st,
+                                             unsigned char* smem, float* mail1, float* mail2, const RowPtr* rows) {
+  const Geo& g = p.geo;
+  const bool k1 = w.kind == 1;
+  const int mi = w.kind - 1;
+  const RowPtr& rp = rows[w.r];
+  const int G = k1 ? g.G1 : g.G2;
+  const XTable tb = k1 ? table_at(smem + (size_t)(w.r / g.top_k) * token_table_bytes(g.H), g.H)
+                       : table_at(smem + (size_t)(w.unit * g.top_k + w.jr) * token_table_bytes(g.I), g.I);
+  // lane -> (group within the item, column unit, run, quad within the run)
+  const int gi = k1 ? (lane >> 4) : (lane >> 3);
+  const int q = k1 ? (lane & 15) : (lane & 7);
+  const int run_side = k1 ? (q >= 8 ? 1 : 0) : 0;
+  const int q8 = k1 ? (q & 7) : q;
+  const int runs = k1 ? 2 : 1;
+  const int gl = k1 ? w.kp * 2 + gi : w.kp * 4 + gi;        // group index in the activation table
+  float v[4] = {0.f, 0.f, 0.f, 0.f};
+  if (rp.ok[mi] && w.kp * (k1 ? 2 : 4) + gi < G) {
+    const int col = (run_side ? g.I : 0) + w.b * 32;
+    const int N = k1 ? 2 * g.I : g.H;
+    const int zsh = (int)((((int64_t)gl * (N / 4) + col / 4)) & 15);
+    dot_stage(st, runs * 128, gi, q, gi * runs + run_side, q8, tb, gl, p.scale_bf16 != 0, rp.z[mi] != nullptr,
+              zsh, v);
+  }
+  if (k1) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c) v[c] += __shfl_xor_sync(0xffffffffu, v[c], 16);
+    if (lane < 16)
+      *reinterpret_cast<float4*>(mail1 + (size_t)w.slot * 64 + lane * 4) = make_float4(v[0], v[1], v[2], v[3]);
+  } else {
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      v[c] += __shfl_xor_sync(0xffffffffu, v[c], 8);
+      v[c] += __shfl_xor_sync(0xffffffffu, v[c], 16);
+    }
+    const float wr = p.topk_w[w.r];
+    if (lane < 8)
+      *reinterpret_cast<float4*>(mail2 + (size_t)w.slot * 32 + lane * 4) =
+          make_float4(v[0] * wr, v[1] * wr, v[2] * wr, v[3] * wr);
+  }
+}
+
+// Phase switch, entered by every warp of the CTA once its gate_up items are done: sum the CTA's
+// h-block partials, publish them, grid barrier, then build the h tables of this CTA's down units.
+__device__ __forceinline__ void phase_switch(const FusedParams& p, int cta, int warp, int lane, unsigned char* smem,
+                                             const float* mail1, const unsigned char* split) {
+  const Geo& g = p.geo;
+  const WarpList L = warp_list(g, cta, warp);
+  __syncthreads();
+  // h-blocks of this CTA's range: fixed-order sums; whole blocks publish h, split blocks their side's
+  // (gate, up) partial sums
+  {
+    const long long a = L.a, b = (long long)(cta + 1) * g.n1 / g.grid;
+    if (b > a) {
+      const int blk0 = (int)(a / g.kp1), blk1 = (int)((b - 1) / g.kp1);
+      for (int blk = blk0 + warp; blk <= blk1; blk += kWarps) {
+        const long long i0 = (long long)blk * g.kp1, i1 = i0 + g.kp1;
+        const long long lo = i0 > a ? i0 : a, hi = i1 < b ? i1 : b;
+        float gs = 0.f, us = 0.f;
+        for (long long i = lo; i < hi; ++i) {
+          gs += mail1[(size_t)(i - a) * 64 + lane];
+          us += mail1[(size_t)(i - a) * 64 + 32 + lane];
+        }
+        const int r = blk / g.nb1, hb = blk - r * g.nb1;
+        const size_t col = (size_t)hb * 32 + lane;
+        if (i0 >= a && i1 <= b) {
+          p.hfin[(size_t)r * g.I + col] = silu(gs) * us;
+        } else {
+          const int side = i0 < a ? 1 : 0;
+          float* hp = p.hpart + ((size_t)(side * g.R + r) * 2) * g.I + col;
+          hp[0] = gs;
+          hp[g.I] = us;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) grid_barrier(p.bar_count, p.bar_gen, gridDim.x, p.err);
+  __syncthreads();
+
+  // ---------------------------------------------------------------- phase 2: down items
+  // h tables of this CTA's units, one warp per (unit, row, group), loads issued in batches
+  const int per_unit = g.top_k * g.G2;
+  const int ntab = L.nu * per_unit;
+  constexpr int kHB = 6;
+  for (int k0 = warp; k0 < ntab; k0 += kHB * kWarps) {
+    float hv[kHB][4];
+#pragma unroll
+    for (int j = 0; j < kHB; ++j) {
+      const int k = k0 + j * kWarps;
+      hv[j][0] = hv[j][1] = hv[j][2] = hv[j][3] = 0.f;
+      if (k < ntab) {
+        const int q = k / per_unit, rem = k - q * per_unit;
+        const int jr = rem / g.G2, gg = rem - jr * g.G2;
+        const int m = (cta + g.grid * q) / g.nb2;
+        const int r = m * g.top_k + jr;
+        const int col = gg * kGroup + 4 * lane;
+        if (!split[r * g.nb1 + col / 32]) {
+          const float4 h4 = __ldcg(reinterpret_cast<const float4*>(p.hfin + (size_t)r * g.I + col));
+          hv[j][0] = h4.x; hv[j][1] = h4.y; hv[j][2] = h4.z; hv[j][3] = h4.w;
+        } else {
+          const float* p0 = p.hpart + ((size_t)r * 2) * g.I + col;
+          const float* p1 = p.hpart + ((size_t)(g.R + r) * 2) * g.I + col;
+          const float4 g0 = __ldcg(reinterpret_cast<const float4*>(p0));
+          const float4 u0 = __ldcg(reinterpret_cast<const float4*>(p0 + g.I));
+          const float4 g1 = __ldcg(reinterpret_cast<const float4*>(p1));
+          const float4 u1 = __ldcg(reinterpret_cast<const float4*>(p1 + g.I));
+          hv[j][0] = silu(g0.x + g1.x) * (u0.x + u1.x);
+          hv[j][1] = silu(g0.y + g1.y) * (u0.y + u1.y);
+          hv[j][2] = silu(g0.z + g1.z) * (u0.z + u1.z);
+          hv[j][3] = silu(g0.w + g1.w) * (u0.w + u1.w);
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kHB; ++j) {
+      const int k = k0 + j * kWarps;
+      if (k < ntab) {
+        const int q = k / per_unit, rem = k - q * per_unit;
+        const int jr = rem / g.G2, gg = rem - jr * g.G2;
+        prep_group_regs(hv[j], gg, table_at(smem + (size_t)(q * g.top_k + jr) * token_table_bytes(g.I), g.I),
+                        lane);
+      }
+    }
+  }
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(kThreads, 1) fused_layer_kernel(FusedParams p) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const Geo& g = p.geo;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int cta = blockIdx.x;
+  unsigned char* stages = smem + p.off_stages + (size_t)warp * kStages * kStageBytes;
+  float* mail1 = reinterpret_cast<float*>(smem + p.off_mail1);
+  float* mail2 = reinterpret_cast<float*>(smem + p.off_mail2);
+  RowPtr* rows = reinterpret_cast<RowPtr*>(smem + p.off_rows);
+  unsigned char* split = smem + p.off_split;
+  const uint32_t bars = smem_u32(smem + p.off_bars) + (uint32_t)(warp * kStages * 8);
+  if (lane < kStages) mbar_init(bars + lane * 8, 1);
+  asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+
+  const WarpList L = warp_list(g, cta, warp);
+  const int total = L.total();
+  const int nxt = g.M * g.G1;
+
+  // activation values of this warp's first table groups, loaded before the weight stream starts
+  constexpr int kXPre = 4;
+  float xv[kXPre][4];
+#pragma unroll
+  for (int j = 0; j < kXPre; ++j) {
+    const int t = warp + j * kWarps;
+    if (t < nxt) {
+      const int m = t / g.G1, gi = t - m * g.G1;
+      const __nv_bfloat162* src =
+          reinterpret_cast<const __nv_bfloat162*>(p.x + (int64_t)m * g.H + gi * kGroup + 4 * lane);
+      const float2 a0 = __bfloat1622float2(src[0]), a1 = __bfloat1622float2(src[1]);
+      xv[j][0] = a0.x; xv[j][1] = a0.y; xv[j][2] = a1.x; xv[j][3] = a1.y;
+    } else {
+      xv[j][0] = xv[j][1] = xv[j][2] = xv[j][3] = 0.f;
+    }
+  }
+  // expert bases of every routed row, resolved once per CTA; h-blocks split by a CTA range boundary
+  for (int r = threadIdx.x; r < g.R; r += kThreads) {
+    RowPtr rp;
+    const int e = p.ids[r];
+    rp.ok[0] = p.map13.resolve(e, rp.w[0], rp.s[0], rp.z[0], p.err);
+    rp.ok[1] = p.map2.resolve(e, rp.w[1], rp.s[1], rp.z[1], p.err);
+    rows[r] = rp;
+  }
+  for (int k = threadIdx.x; k < g.R * g.nb1; k += kThreads) split[k] = 0;
+  __syncthreads();
+  for (int c = 1 + threadIdx.x; c < g.grid; c += kThreads) {
+    const long long ac = (long long)c * g.n1 / g.grid;
+    if (ac % g.kp1) split[ac / g.kp1] = 1;
+  }
+  // One loop over this warp's work list with a single call site for issuing and one for processing an
+  // item, so the loop body stays small enough for the instruction cache. t < 0 only issues the first
+  // items, t == 0 builds the activation tables, t == n1w (the warp's first down item) switches phase.
+  bool p1done = false;
+  for (int t = -kStages;; ++t) {
+    if (t == 0) {
+#pragma unroll
+      for (int j = 0; j < kXPre; ++j) {
+        const int tt = warp + j * kWarps;
+        if (tt < nxt) {
+          const int m = tt / g.G1, gi = tt - m * g.G1;
+          prep_group_regs(xv[j], gi, table_at(smem + (size_t)m * token_table_bytes(g.H), g.H), lane);
+        }
+      }
+      for (int tt = warp + kXPre * kWarps; tt < nxt; tt += kWarps) {
+        const int m = tt / g.G1, gi = tt - m * g.G1;
+        const __nv_bfloat16* src = p.x + (int64_t)m * g.H + gi * kGroup + 4 * lane;
+        const float v[4] = {__bfloat162float(src[0]), __bfloat162float(src[1]), __bfloat162float(src[2]),
+                            __bfloat162float(src[3])};
+        prep_group_regs(v, gi, table_at(smem + (size_t)m * token_table_bytes(g.H), g.H), lane);
+      }
+      __syncthreads();
+    }
+    if (t >= 0 && t == L.n1w && !p1done) {
+      phase_switch(p, cta, warp, lane, smem, mail1, split);
+      p1done = true;
+    }
+    if (t >= 0 && t >= total) break;
+    if (t >= 0) {
+      mbar_wait(bars + (t % kStages) * 8, (unsigned)(t / kStages) & 1u, p.err);
+      process_work(p, work_at(g, L, cta, warp, t), lane, stages + (t % kStages) * kStageBytes, smem, mail1, mail2,
+                   rows);
+      __syncwarp();
+    }
+    {
+      const int s2 = (t + kStages) % kStages;
+      issue_work(p, work_at(g, L, cta, warp, t + kStages), lane, stages + s2 * kStageBytes, bars + s2 * 8, rows);
+    }
+  }
+  __syncthreads();
+
+  // y of each unit: fixed-order sum of its top_k x K-part partials
+  for (int q = warp; q < L.nu; q += kWarps) {
+    const int u = cta + g.grid * q, m = u / g.nb2, b = u - m * g.nb2;
+    float acc = 0.f;
+    for (int j = 0; j < g.s2; ++j) acc += mail2[((size_t)q * g.s2 + j) * 32 + lane];
+    p.y[(int64_t)m * g.H + b * 32 + lane] = __float2bfloat16(acc * p.rsf);
+  }
+}
+
+}  // namespace
+
+// Workspace: 256 bytes of control words (grid barrier count and generation, zero-filled before the
+// first call; the barrier leaves the count at zero), then h [R][I] fp32 and the split-block partial
+// sums [2][R][2][I] fp32.
 size_t layer_workspace_bytes(int M, int H, int I, int top_k) {
   (void)H;
-  const size_t R = (size_t)M * (size_t)top_k;
-  return 256 + R * (size_t)I * 4;
+  if (M <= 0 || I <= 0 || top_k <= 0) return 256;
+  return 256 + (size_t)M * top_k * 5 * (size_t)I * 4;
 }
 
-int decode_layer_two_pass(const LayerArgs& a) {
+static int launch_fused(const LayerArgs& a, int M, const void* x, const int32_t* ids, const float* w, void* y,
+                        int grid_cap) {
+  const Geo g = make_geo(M, a.H, a.I, a.top_k, grid_cap);
+  const SmemPlan sp = smem_plan(g);
+  FusedParams p{};
+  p.x = static_cast<const __nv_bfloat16*>(x); p.ids = ids; p.topk_w = w;
+  p.map13 = a.map13; p.map2 = a.map2; p.scale_bf16 = a.scale_bf16; p.rsf = a.routed_scaling;
+  p.y = static_cast<__nv_bfloat16*>(y); p.geo = g; p.err = a.err;
+  p.off_stages = sp.tabs;
+  p.off_mail1 = sp.tabs + sp.stages;
+  p.off_mail2 = p.off_mail1 + sp.mail1;
+  p.off_rows = p.off_mail2 + sp.mail2;
+  p.off_split = p.off_rows + sp.rows;
+  p.off_bars = p.off_split + sp.split;
+  unsigned* ctl = static_cast<unsigned*>(a.workspace);
+  p.bar_count = ctl;
+  p.bar_gen = ctl + 1;
+  p.hfin = reinterpret_cast<float*>(static_cast<char*>(a.workspace) + 256);
+  p.hpart = p.hfin + (size_t)g.R * a.I;
+
+  if (cudaFuncSetAttribute(fused_layer_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sp.total) !=
+      cudaSuccess)
+    return kErrLaunch;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(g.grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = sp.total;
+  cfg.stream = a.stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, fused_layer_kernel, p) == cudaSuccess ? kOk : kErrLaunch;
+}
+
+int decode_layer_fused(const LayerArgs& a) {
   if (a.M <= 0) return kOk;
-  if (a.H % kGroup != 0 || a.I % kGroup != 0 || a.H % 4 != 0 || a.top_k <= 0) return kErrShape;
+  if (a.H % kGroup != 0 || a.I % kGroup != 0 || a.top_k <= 0) return kErrShape;
   if (!a.x || !a.ids || !a.topk_w || !a.y) return kErrArg;
   if (!a.workspace || a.workspace_bytes < layer_workspace_bytes(a.M, a.H, a.I, a.top_k)) return kErrWorkspace;
-  const int R = a.M * a.top_k;
-  float* h = reinterpret_cast<float*>(static_cast<char*>(a.workspace) + 256);
+  if (reinterpret_cast<uintptr_t>(a.workspace) & 255u) return kErrAlign;
 
-  GemvArgs g{};
-  g.a = a.x; g.stride_am = a.H; g.map = a.map13; g.ids = a.ids; g.topk_w = a.topk_w;
-  g.out = nullptr; g.stride_om = 0; g.R = R; g.N = 2 * a.I; g.K = a.H; g.top_k = a.top_k;
-  g.stride_ww = 2 * a.I; g.stride_sg = 2 * a.I; g.stride_zg = (2 * a.I) / 4;
-  g.mul_routed_weight = 0; g.scale_bf16 = a.scale_bf16; g.err = a.err; g.stream = a.stream;
-  int st = gemv_gateup_silu(g, a.I, h, a.I);
-  if (st != kOk) return st;
-
-  GemvArgs d{};
-  d.a = h; d.stride_am = a.I; d.map = a.map2; d.ids = a.ids; d.topk_w = a.topk_w;
-  d.out = a.y; d.stride_om = a.H; d.R = R; d.N = a.H; d.K = a.I; d.top_k = a.top_k;
-  d.stride_ww = a.H; d.stride_sg = a.H; d.stride_zg = a.H / 4;
-  d.mul_routed_weight = 1; d.scale_bf16 = a.scale_bf16; d.err = a.err; d.stream = a.stream;
-  return gemv_down_sum(d, a.M, a.routed_scaling);
+  static thread_local int cached_dev = -1, cached_cap = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return kErrDevice;
+  if (dev != cached_dev) {
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return kErrDevice;
+    cached_cap = sms;              // one CTA per SM: the staging buffers take most of shared memory
+    cached_dev = dev;
+  }
+  // tokens per launch: as many as the shared-memory plan allows
+  int mmax = a.M;
+  while (mmax > 1 && smem_plan(make_geo(mmax, a.H, a.I, a.top_k, cached_cap)).total > 227 * 1024) --mmax;
+  if (smem_plan(make_geo(mmax, a.H, a.I, a.top_k, cached_cap)).total > 227 * 1024) return kErrShape;
+  for (int m0 = 0; m0 < a.M; m0 += mmax) {
+    const int mc = a.M - m0 < mmax ? a.M - m0 : mmax;
+    const int st = launch_fused(a, mc, static_cast<const __nv_bfloat16*>(a.x) + (size_t)m0 * a.H,
+                                a.ids + (size_t)m0 * a.top_k, a.topk_w + (size_t)m0 * a.top_k,
+                                static_cast<__nv_bfloat16*>(a.y) + (size_t)m0 * a.H, cached_cap);
+    if (st != kOk) return st;
+  }
+  return kOk;
 }
-
-int decode_layer_fused(const LayerArgs& a) { return decode_layer_two_pass(a); }
 
 }  // namespace w2a16

@@ -16,12 +16,14 @@ pytestmark = pytest.mark.gpu
 TOL = 1e-2
 
 
-def _call_noalloc(pkg, x, ids, w, arena, y, M=None):
+def _call_noalloc(pkg, x, ids, w, arena, y, M=None, H=None, I=None):
     lib = pkg._native.lib()
     esz = arena.scales13.element_size()
     M = x.shape[0] if M is None else M
+    H = arena.H if H is None else H
+    I = arena.I if I is None else I
     return lib.w2a16_moe_decode_layer_slots_noalloc(
-        x.data_ptr(), M, arena.H, arena.I, ids.shape[1], ids.data_ptr(), w.data_ptr(), arena.slots.data_ptr(),
+        x.data_ptr(), M, H, I, ids.shape[1], ids.data_ptr(), w.data_ptr(), arena.slots.data_ptr(),
         arena.E, arena.codes13.data_ptr(), arena.codes13.stride(0) * 4, arena.scales13.data_ptr(),
         arena.scales13.stride(0) * esz, arena.zeros13.data_ptr(), arena.zeros13.stride(0),
         arena.codes2.data_ptr(), arena.codes2.stride(0) * 4, arena.scales2.data_ptr(),
@@ -51,5 +53,10 @@ def test_noalloc_entry_rejects_oversized_layers(pkg, dev):
     ids = torch.zeros(1, 8, dtype=torch.int32, device=dev)
     w = torch.zeros(1, 8, dtype=torch.float32, device=dev)
     y = torch.empty(1, 256, dtype=torch.bfloat16, device=dev)
-    # M * top_k * I * 4 bytes of activations exceed the 1 MiB scratch: refused before any launch
-    assert _call_noalloc(pkg, x, ids, w, arena, y, M=64) == 5
+    # the smallest token count whose workspace exceeds the 4 MiB scratch is refused before any launch or
+    # memory access
+    lib = pkg._native.lib()
+    M = 1
+    while lib.w2a16_moe_layer_workspace_bytes(M, 4096, 1536, 8) <= 4 << 20:
+        M += 1
+    assert _call_noalloc(pkg, x, ids, w, arena, y, M=M, H=4096, I=1536) == 5
