@@ -18,9 +18,12 @@
 // the part slots, computes the items, and reduces each unit's top_k x K-part partials in fixed order in
 // shared memory into y. No atomics beyond the barrier, no ticket chains.
 //
-// Every lane streams its own item data (8 x 16-byte code vectors, 8 bytes of scales, the word holding
-// its zero-point byte) into a per-warp ring of kStages buffers with cp.async, so the next items are in
-// flight while the current one is reduced.
+// Weight stream. At launch every CTA asks L2 to fetch its 1/grid share of each routed expert's code,
+// scale and zero-point arrays (cp.async.bulk.prefetch.L2, gate_up first, then down), so HBM streams the
+// whole layer at full rate from the first microsecond. Each lane then loads its own item data straight
+// into registers with 16-byte non-allocating loads -- 8 word rows of its 4 columns, 4 scales and one
+// zero-point byte -- one item ahead of the one it is reducing; those loads hit L2 or merge with the
+// prefetch in flight, and no shared-memory staging or copy engine sits on the path.
 #include "w2a16_kernels.h"
 
 namespace w2a16 {
@@ -28,9 +31,7 @@ namespace {
 
 constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
-constexpr int kStages = 2;
 constexpr unsigned kSpinLimit = 1u << 22;                    // polls before a wait gives up
-constexpr int kStageBytes = 4096 + 256 + 64;                 // codes + scales + zero-point windows
 
 struct Geo {
   int M, H, I, top_k, R;
@@ -65,7 +66,7 @@ __host__ __device__ __forceinline__ size_t token_table_bytes(int K) {
 }
 
 struct SmemPlan {
-  size_t tabs, stages, mail1, mail2, rows, split, bars, total;
+  size_t tabs, mail1, mail2, rows, split, total;
 };
 
 // Per routed row, resolved once per CTA: expert code / scale / zero-point bases of gate_up and down.
@@ -81,13 +82,11 @@ SmemPlan smem_plan(const Geo& g) {
   const size_t t1 = (size_t)g.M * token_table_bytes(g.H);
   const size_t t2 = (size_t)g.max_units * g.top_k * token_table_bytes(g.I);
   s.tabs = t1 > t2 ? t1 : t2;
-  s.stages = (size_t)kWarps * kStages * kStageBytes;
   s.mail1 = (size_t)g.max_range * 64 * 4;
   s.mail2 = (size_t)g.max_units * g.s2 * 32 * 4;
   s.rows = ((size_t)g.R * sizeof(RowPtr) + 15) & ~size_t(15);
   s.split = ((size_t)g.R * g.nb1 + 15) & ~size_t(15);
-  s.bars = (size_t)kWarps * kStages * 8;
-  s.total = s.tabs + s.stages + s.mail1 + s.mail2 + s.rows + s.split + s.bars;
+  s.total = s.tabs + s.mail1 + s.mail2 + s.rows + s.split;
   return s;
 }
 
@@ -100,7 +99,7 @@ struct FusedParams {
   float rsf;
   __nv_bfloat16* y;
   Geo geo;
-  size_t off_stages, off_mail1, off_mail2, off_rows, off_split, off_bars;
+  size_t off_mail1, off_mail2, off_rows, off_split;
   unsigned* bar_count;   // grid barrier
   unsigned* bar_gen;
   float* hfin;           // [R][I] h of h-blocks computed wholly inside one CTA
@@ -122,50 +121,6 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
   return v;
 }
 
-// ----------------------------------------------------------------------------- bulk-copy staging
-// Each warp streams its items through a ring of kStages shared-memory buffers with cp.async.bulk (the
-// TMA engine): one 128-byte copy per (word row, column run), completion counted on one mbarrier per
-// buffer. The copies bypass the load/store pipeline, so the x / id / h loads of the kernel never queue
-// behind the weight stream.
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ void mbar_init(uint32_t bar, unsigned count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_tx(uint32_t bar, unsigned bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ bool mbar_try(uint32_t bar, unsigned parity) {
-  unsigned ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Bounded wait for the phase with the given parity (error bit 1 if it never completes).
-__device__ __forceinline__ void mbar_wait(uint32_t bar, unsigned parity, unsigned* err) {
-  unsigned it = 0;
-  while (!mbar_try(bar, parity)) {
-    if (++it > kSpinLimit) {
-      flag_error(err, 2u);
-      return;
-    }
-  }
-}
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, unsigned bytes, uint32_t bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
-               "l"(src), "r"(bytes), "r"(bar)
-               : "memory");
-}
-
-// Stage buffer layout: codes [32 word rows x 128 B] (gate_up: 16 rows x 256 B = gate run | up run),
-// then scales [4 x 64 B], then zero-point windows [4 x 16 B].
-constexpr int kCodeBytes = 4096;
-constexpr int kScaleOff = kCodeBytes;
-constexpr int kZeroOff = kCodeBytes + 256;
 // One entry of a warp's work list.
 struct Work {
   int kind;   // 0 none, 1 gate_up, 2 down
@@ -222,105 +177,105 @@ __device__ __forceinline__ Work work_at(const Geo& g, const WarpList& L, int cta
   return w;
 }
 
-// Issue the bulk copies of work item w into stage buffer `st` (lane j issues copy j; lane 0 first
-// announces the byte count on the buffer's mbarrier). Rows of a non-resident expert, groups past K and
-// list entries past the end copy nothing, and their phase completes on the arrival alone.
-__device__ __forceinline__ void issue_work(const FusedParams& p, const Work& w, int lane, unsigned char* st,
-                                           uint32_t bar, const RowPtr* rows) {
-  const Geo& g = p.geo;
-  const int mi = w.kind - 1;
-  const bool live = w.kind != 0 && rows[w.r].ok[mi];
-  const int G = w.kind == 1 ? g.G1 : g.G2;
-  const int gpi = w.kind == 1 ? 2 : 4;                       // groups per item
-  const int g0 = w.kp * gpi;
-  const int ng = live ? (G - g0 < gpi ? G - g0 : gpi) : 0;   // valid groups
-  const int runs = w.kind == 1 ? 2 : 1;                      // column runs per word row (gate, up)
-  // copies: ng*8*runs code runs (128 B), ng*runs scale runs (64 B), ng*runs zero windows (16 B)
-  const bool hz = live && rows[w.r].z[mi] != nullptr;
-  const unsigned bytes = (unsigned)(ng * runs) * (8u * 128u + 64u + (hz ? 16u : 0u));
-  if (lane == 0) mbar_arrive_tx(bar, bytes);
-  __syncwarp();
-  if (!live || ng == 0) return;
-  const RowPtr& rp = rows[w.r];
-  const int N = w.kind == 1 ? 2 * g.I : g.H;
-  const uint32_t sdst = smem_u32(st);
-  const int ncode = ng * 8 * runs;
-  for (int c = lane; c < ncode + 2 * ng * runs; c += 32) {
-    if (c < ncode) {
-      int gi, k, side;
-      if (runs == 2) { gi = c >> 4; k = (c >> 1) & 7; side = c & 1; }
-      else { gi = c >> 3; k = c & 7; side = 0; }
-      const int col = (side ? g.I : 0) + w.b * 32;
-      const uint32_t* src = rp.w[mi] + (int64_t)(8 * (g0 + gi) + k) * N + col;
-      const uint32_t dst = sdst + (uint32_t)(((8 * gi + k) * runs + side) * 128);
-      bulk_g2s(dst, src, 128u, bar);
-    } else {
-      const int c2 = c - ncode;                              // scale runs then zero windows
-      const int which = c2 / (ng * runs), idx = c2 - which * (ng * runs);
-      const int gi = idx / runs, side = idx - gi * runs;
-      const int col = (side ? g.I : 0) + w.b * 32;
-      if (which == 0) {
-        bulk_g2s(sdst + kScaleOff + (gi * runs + side) * 64, rp.s[mi] + ((int64_t)(g0 + gi) * N + col) * 2, 64u, bar);
-      } else if (hz) {
-        const int64_t zoff = (int64_t)(g0 + gi) * (N / 4) + col / 4;
-        bulk_g2s(sdst + kZeroOff + (gi * runs + side) * 16, rp.z[mi] + (zoff & ~int64_t(15)), 16u, bar);
-      }
-    }
-  }
+// Lane -> (group within the item, first of its 4 columns, group index along K). Gate_up items: lanes
+// 0-15 take group 2kp, 16-31 group 2kp+1, quads 0-7 over the 32 gate columns and 8-15 over the matching
+// up columns. Down items: 4 groups x 8 column quads.
+struct LaneMap {
+  int col, gl;
+  bool valid;
+};
+
+__device__ __forceinline__ LaneMap lane_map(const Geo& g, const Work& w, int lane, const RowPtr* rows) {
+  LaneMap lm{};
+  if (w.kind == 0) return lm;
+  const bool k1 = w.kind == 1;
+  const int gi = k1 ? (lane >> 4) : (lane >> 3);
+  const int q = k1 ? (lane & 15) : (lane & 7);
+  const int q8 = k1 ? (q & 7) : q;
+  lm.col = (k1 && q >= 8 ? g.I : 0) + w.b * 32 + q8 * 4;
+  lm.gl = k1 ? w.kp * 2 + gi : w.kp * 4 + gi;
+  lm.valid = rows[w.r].ok[w.kind - 1] && lm.gl < (k1 ? g.G1 : g.G2);
+  return lm;
 }
 
-// 4 columns x 1 group of this lane against a pair table; codes, scales and zero points from the stage
-// buffer. gi = the lane's group within the item, qq = its 16-byte column unit within a word row.
-__device__ __forceinline__ void dot_stage(const unsigned char* st, int row_bytes, int gi, int qq, int run, int q8,
-                                          const XTable& tb, int gl, bool sbf, bool has_z, int zsh, float (&v)[4]) {
+// One lane's share of an item, held in registers.
+struct ItemRegs {
+  uint4 w[8];    // word rows 8*gl .. 8*gl+7, columns col .. col+3
+  uint2 s;       // the 4 scales
+  uint32_t z;    // zero-point byte of the 4 columns
+};
+
+__device__ __forceinline__ uint4 ldg_stream16(const void* ptr) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];\n"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(ptr));
+  return v;
+}
+__device__ __forceinline__ uint2 ldg_stream8(const void* ptr) {
+  uint2 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];\n" : "=r"(v.x), "=r"(v.y) : "l"(ptr));
+  return v;
+}
+__device__ __forceinline__ uint32_t ldg_stream1(const void* ptr) {
+  unsigned short v;
+  asm volatile("ld.global.nc.L1::no_allocate.u8 %0, [%1];\n" : "=h"(v) : "l"(ptr));
+  return v;
+}
+
+// Issue the loads of this lane's share of item w (nothing for list entries past the end, rows of a
+// non-resident expert or groups past K).
+__device__ __forceinline__ void load_item(const FusedParams& p, const Work& w, int lane, const RowPtr* rows,
+                                          ItemRegs& it) {
+  const Geo& g = p.geo;
+  const LaneMap lm = lane_map(g, w, lane, rows);
+  if (!lm.valid) return;
+  const int mi = w.kind - 1;
+  const RowPtr& rp = rows[w.r];
+  const int64_t N = w.kind == 1 ? 2 * g.I : g.H;
+  const uint32_t* wp = rp.w[mi] + (int64_t)(8 * lm.gl) * N + lm.col;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) it.w[k] = ldg_stream16(wp + (int64_t)k * N);
+  it.s = ldg_stream8(rp.s[mi] + ((int64_t)lm.gl * N + lm.col) * 2);
+  it.z = rp.z[mi] != nullptr ? ldg_stream1(rp.z[mi] + (int64_t)lm.gl * (N / 4) + lm.col / 4) : 0u;
+}
+
+// 4 columns x 1 group of this lane from its registers against an activation table.
+__device__ __forceinline__ void dot_regs(const ItemRegs& it, const XTable& tb, int gl, bool sbf, bool has_z,
+                                         float (&v)[4]) {
   int acc[4][4];
 #pragma unroll
   for (int c = 0; c < 4; ++c)
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[c][j] = 0;
-  const unsigned char* rows = st + (size_t)(8 * gi) * row_bytes + qq * 16;
-#pragma unroll 2
+#pragma unroll
   for (int k = 0; k < 8; ++k) {
-    const uint4 w = *reinterpret_cast<const uint4*>(rows + k * row_bytes);
     const uint4* xp = reinterpret_cast<const uint4*>(tb.pairs + (gl * 8 + k) * kXRegs);
     const uint4 xa = xp[0], xb = xp[1];
     const uint32_t xr[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-    word_dot(w.x, xr, acc[0]);
-    word_dot(w.y, xr, acc[1]);
-    word_dot(w.z, xr, acc[2]);
-    word_dot(w.w, xr, acc[3]);
+    word_dot(it.w[k].x, xr, acc[0]);
+    word_dot(it.w[k].y, xr, acc[1]);
+    word_dot(it.w[k].z, xr, acc[2]);
+    word_dot(it.w[k].w, xr, acc[3]);
   }
-  const uint2 sr = *reinterpret_cast<const uint2*>(st + kScaleOff + run * 64 + q8 * 8);
   float s[4];
   if (sbf) {
-    const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&sr.x);
-    const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&sr.y);
+    const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&it.s.x);
+    const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&it.s.y);
     s[0] = __low2float(a); s[1] = __high2float(a); s[2] = __low2float(b); s[3] = __high2float(b);
   } else {
-    const __half2 a = *reinterpret_cast<const __half2*>(&sr.x);
-    const __half2 b = *reinterpret_cast<const __half2*>(&sr.y);
+    const __half2 a = *reinterpret_cast<const __half2*>(&it.s.x);
+    const __half2 b = *reinterpret_cast<const __half2*>(&it.s.y);
     s[0] = __low2float(a); s[1] = __high2float(a); s[2] = __low2float(b); s[3] = __high2float(b);
   }
-  const uint32_t zbyte = has_z ? (uint32_t)st[kZeroOff + run * 16 + zsh + q8] : 0u;
   const int m64x = tb.m64x[gl];
   const float scl = tb.scl[gl];
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
-    const int zp = has_z ? (int)((zbyte >> (2 * c)) & 3u) : 2;
+    const int zp = has_z ? (int)((it.z >> (2 * c)) & 3u) : 2;
     const int T = combine_classes(acc[c]) + zp * m64x;
     v[c] = (float)T * (s[c] * scl);
   }
-}
-
-// h-block blk (items [blk*kp1, (blk+1)*kp1)) is split when a CTA range boundary falls strictly inside it.
-__device__ __forceinline__ bool block_split(const Geo& g, int blk) {
-  const long long lo = (long long)blk * g.kp1, hi = lo + g.kp1;
-  long long c = lo * g.grid / g.n1;
-  for (int k = 0; k < 3; ++k, ++c) {
-    const long long a = c * g.n1 / g.grid;
-    if (a > lo && a < hi) return true;
-  }
-  return false;
 }
 
 // All CTAs arrive; thread 0 of each CTA calls this. Gives up after kSpinLimit polls (error bit 1).
@@ -344,30 +299,17 @@ __device__ void grid_barrier(unsigned* count, unsigned* gen, unsigned ncta, unsi
   __threadfence();
 }
 
-__device__ __forceinline__ void process_work(const FusedParams& p, const Work& w, int lane, const unsigned char* st,
+__device__ __forceinline__ void process_work(const FusedParams& p, const Work& w, int lane, const ItemRegs& it,
                                              unsigned char* smem, float* mail1, float* mail2, const RowPtr* rows) {
   const Geo& g = p.geo;
   const bool k1 = w.kind == 1;
   const int mi = w.kind - 1;
   const RowPtr& rp = rows[w.r];
-  const int G = k1 ? g.G1 : g.G2;
   const XTable tb = k1 ? table_at(smem + (size_t)(w.r / g.top_k) * token_table_bytes(g.H), g.H)
                        : table_at(smem + (size_t)(w.unit * g.top_k + w.jr) * token_table_bytes(g.I), g.I);
-  // lane -> (group within the item, column unit, run, quad within the run)
-  const int gi = k1 ? (lane >> 4) : (lane >> 3);
-  const int q = k1 ? (lane & 15) : (lane & 7);
-  const int run_side = k1 ? (q >= 8 ? 1 : 0) : 0;
-  const int q8 = k1 ? (q & 7) : q;
-  const int runs = k1 ? 2 : 1;
-  const int gl = k1 ? w.kp * 2 + gi : w.kp * 4 + gi;        // group index in the activation table
+  const LaneMap lm = lane_map(g, w, lane, rows);
   float v[4] = {0.f, 0.f, 0.f, 0.f};
-  if (rp.ok[mi] && w.kp * (k1 ? 2 : 4) + gi < G) {
-    const int col = (run_side ? g.I : 0) + w.b * 32;
-    const int N = k1 ? 2 * g.I : g.H;
-    const int zsh = (int)((((int64_t)gl * (N / 4) + col / 4)) & 15);
-    dot_stage(st, runs * 128, gi, q, gi * runs + run_side, q8, tb, gl, p.scale_bf16 != 0, rp.z[mi] != nullptr,
-              zsh, v);
-  }
+  if (lm.valid) dot_regs(it, tb, lm.gl, p.scale_bf16 != 0, rp.z[mi] != nullptr, v);
   if (k1) {
 #pragma unroll
     for (int c = 0; c < 4; ++c) v[c] += __shfl_xor_sync(0xffffffffu, v[c], 16);
@@ -428,7 +370,7 @@ __device__ __forceinline__ void phase_switch(const FusedParams& p, int cta, int 
   // h tables of this CTA's units, one warp per (unit, row, group), loads issued in batches
   const int per_unit = g.top_k * g.G2;
   const int ntab = L.nu * per_unit;
-  constexpr int kHB = 6;
+  constexpr int kHB = 3;
   for (int k0 = warp; k0 < ntab; k0 += kHB * kWarps) {
     float hv[kHB][4];
 #pragma unroll
@@ -477,20 +419,37 @@ __global__ void __launch_bounds__(kThreads, 1) fused_layer_kernel(FusedParams p)
   const Geo& g = p.geo;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int cta = blockIdx.x;
-  unsigned char* stages = smem + p.off_stages + (size_t)warp * kStages * kStageBytes;
   float* mail1 = reinterpret_cast<float*>(smem + p.off_mail1);
   float* mail2 = reinterpret_cast<float*>(smem + p.off_mail2);
   RowPtr* rows = reinterpret_cast<RowPtr*>(smem + p.off_rows);
   unsigned char* split = smem + p.off_split;
-  const uint32_t bars = smem_u32(smem + p.off_bars) + (uint32_t)(warp * kStages * 8);
-  if (lane < kStages) mbar_init(bars + lane * 8, 1);
-  asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+
+  // Start the whole layer's weight stream: this CTA's 1/grid share of every routed row's six arrays.
+  // A prefetch is only a hint, so arrays whose base is not 16-byte aligned are left to the loads.
+  for (int idx = threadIdx.x; idx < g.R * 6; idx += kThreads) {
+    const int r = idx / 6, arr = idx - r * 6, ph = arr / 3, kind = arr - ph * 3;
+    const ExpertMap& mp = ph == 0 ? p.map13 : p.map2;
+    const uint32_t* wb = nullptr;
+    const char* sb = nullptr;
+    const uint8_t* zb = nullptr;
+    if (!mp.resolve(p.ids[r], wb, sb, zb, nullptr)) continue;
+    const int64_t K = ph == 0 ? g.H : g.I, N = ph == 0 ? 2 * g.I : g.H;
+    const char* base = kind == 0 ? reinterpret_cast<const char*>(wb)
+                                 : (kind == 1 ? sb : reinterpret_cast<const char*>(zb));
+    const int64_t bytes = kind == 0 ? (K / 16) * N * 4 : (kind == 1 ? (K / kGroup) * N * 2 : (K / kGroup) * (N / 4));
+    if (base == nullptr || (reinterpret_cast<uintptr_t>(base) & 15u)) continue;
+    const int64_t chunk = ((bytes + g.grid - 1) / g.grid + 15) & ~int64_t(15);
+    const int64_t start = (int64_t)cta * chunk;
+    const int64_t len = (start < bytes ? (bytes - start < chunk ? bytes - start : chunk) : 0) & ~int64_t(15);
+    if (len > 0)
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(base + start), "r"((unsigned)len) : "memory");
+  }
 
   const WarpList L = warp_list(g, cta, warp);
   const int total = L.total();
   const int nxt = g.M * g.G1;
 
-  // activation values of this warp's first table groups, loaded before the weight stream starts
+  // activation values of this warp's first table groups
   constexpr int kXPre = 4;
   float xv[kXPre][4];
 #pragma unroll
@@ -520,44 +479,45 @@ __global__ void __launch_bounds__(kThreads, 1) fused_layer_kernel(FusedParams p)
     const long long ac = (long long)c * g.n1 / g.grid;
     if (ac % g.kp1) split[ac / g.kp1] = 1;
   }
-  // One loop over this warp's work list with a single call site for issuing and one for processing an
-  // item, so the loop body stays small enough for the instruction cache. t < 0 only issues the first
-  // items, t == 0 builds the activation tables, t == n1w (the warp's first down item) switches phase.
-  bool p1done = false;
-  for (int t = -kStages;; ++t) {
-    if (t == 0) {
+
+  // first item of this warp in flight while the activation tables are built
+  ItemRegs cur, nxt_it;
+  Work wn = work_at(g, L, cta, warp, 0);
+  load_item(p, wn, lane, rows, nxt_it);
 #pragma unroll
-      for (int j = 0; j < kXPre; ++j) {
-        const int tt = warp + j * kWarps;
-        if (tt < nxt) {
-          const int m = tt / g.G1, gi = tt - m * g.G1;
-          prep_group_regs(xv[j], gi, table_at(smem + (size_t)m * token_table_bytes(g.H), g.H), lane);
-        }
-      }
-      for (int tt = warp + kXPre * kWarps; tt < nxt; tt += kWarps) {
-        const int m = tt / g.G1, gi = tt - m * g.G1;
-        const __nv_bfloat16* src = p.x + (int64_t)m * g.H + gi * kGroup + 4 * lane;
-        const float v[4] = {__bfloat162float(src[0]), __bfloat162float(src[1]), __bfloat162float(src[2]),
-                            __bfloat162float(src[3])};
-        prep_group_regs(v, gi, table_at(smem + (size_t)m * token_table_bytes(g.H), g.H), lane);
-      }
-      __syncthreads();
+  for (int j = 0; j < kXPre; ++j) {
+    const int tt = warp + j * kWarps;
+    if (tt < nxt) {
+      const int m = tt / g.G1, gi = tt - m * g.G1;
+      prep_group_regs(xv[j], gi, table_at(smem + (size_t)m * token_table_bytes(g.H), g.H), lane);
     }
-    if (t >= 0 && t == L.n1w && !p1done) {
+  }
+  for (int tt = warp + kXPre * kWarps; tt < nxt; tt += kWarps) {
+    const int m = tt / g.G1, gi = tt - m * g.G1;
+    const __nv_bfloat16* src = p.x + (int64_t)m * g.H + gi * kGroup + 4 * lane;
+    const float v[4] = {__bfloat162float(src[0]), __bfloat162float(src[1]), __bfloat162float(src[2]),
+                        __bfloat162float(src[3])};
+    prep_group_regs(v, gi, table_at(smem + (size_t)m * token_table_bytes(g.H), g.H), lane);
+  }
+  __syncthreads();
+
+  // One loop over this warp's work list: take the item whose loads are in flight, issue the next one's,
+  // reduce. t == n1w (the warp's first down item) switches phase, with that item already loading.
+  bool p1done = false;
+  for (int t = 0;; ++t) {
+    if (t == L.n1w && !p1done) {
       phase_switch(p, cta, warp, lane, smem, mail1, split);
       p1done = true;
     }
-    if (t >= 0 && t >= total) break;
-    if (t >= 0) {
-      mbar_wait(bars + (t % kStages) * 8, (unsigned)(t / kStages) & 1u, p.err);
-      process_work(p, work_at(g, L, cta, warp, t), lane, stages + (t % kStages) * kStageBytes, smem, mail1, mail2,
-                   rows);
-      __syncwarp();
+    if (t >= total) break;
+    const Work wc = wn;
+    cur = nxt_it;
+    if (t + 1 < total) {
+      wn = work_at(g, L, cta, warp, t + 1);
+      load_item(p, wn, lane, rows, nxt_it);
     }
-    {
-      const int s2 = (t + kStages) % kStages;
-      issue_work(p, work_at(g, L, cta, warp, t + kStages), lane, stages + s2 * kStageBytes, bars + s2 * 8, rows);
-    }
+    process_work(p, wc, lane, cur, smem, mail1, mail2, rows);
+    __syncwarp();
   }
   __syncthreads();
 
@@ -589,12 +549,10 @@ static int launch_fused(const LayerArgs& a, int M, const void* x, const int32_t*
   p.x = static_cast<const __nv_bfloat16*>(x); p.ids = ids; p.topk_w = w;
   p.map13 = a.map13; p.map2 = a.map2; p.scale_bf16 = a.scale_bf16; p.rsf = a.routed_scaling;
   p.y = static_cast<__nv_bfloat16*>(y); p.geo = g; p.err = a.err;
-  p.off_stages = sp.tabs;
-  p.off_mail1 = sp.tabs + sp.stages;
+  p.off_mail1 = sp.tabs;
   p.off_mail2 = p.off_mail1 + sp.mail1;
   p.off_rows = p.off_mail2 + sp.mail2;
   p.off_split = p.off_rows + sp.rows;
-  p.off_bars = p.off_split + sp.split;
   unsigned* ctl = static_cast<unsigned*>(a.workspace);
   p.bar_count = ctl;
   p.bar_gen = ctl + 1;
@@ -630,7 +588,7 @@ int decode_layer_fused(const LayerArgs& a) {
   if (dev != cached_dev) {
     int sms = 0;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return kErrDevice;
-    cached_cap = sms;              // one CTA per SM: the staging buffers take most of shared memory
+    cached_cap = sms;              // one CTA of 512 threads per SM
     cached_dev = dev;
   }
   // tokens per launch: as many as the shared-memory plan allows
