@@ -22,8 +22,10 @@
  *   w = (q - zp) * s.
  *
  * Device-side error word (`err`, optional, uint32 in device memory): bit 0 is set when an expert id
- * lies outside [0, num_experts); such rows contribute zero. Bit 1 is set when a bounded wait inside
- * a kernel gave up. The library never traps or aborts.
+ * lies outside [0, num_experts), or when an arena slot id is 2^20 or larger; such rows contribute
+ * zero. Bit 1 is set when a bounded wait inside a kernel gave up. Bit 2 is set when the decode layer's
+ * shared-memory ring is not 128-byte aligned (its copies are then skipped). The library never traps or
+ * aborts.
  */
 #ifndef W2A16_MOE_H
 #define W2A16_MOE_H
@@ -144,7 +146,7 @@ int w2a16_moe_decode_layer_slots(const void* x, int M, int H, int I, int top_k,
  * start-up. It calls no cudaMalloc, cudaFree or allocating library routine. Its workspace is a fixed
  * array of W2A16_NOALLOC_SCRATCH_BYTES (4 MiB) inside the library that every GPU loading the library
  * holds until the process exits; layers needing more (w2a16_moe_layer_workspace_bytes(M, H, I, top_k)
- * > W2A16_NOALLOC_SCRATCH_BYTES; at I=1536, top-8 that is M > 17) return W2A16_ERR_WORKSPACE.
+ * > W2A16_NOALLOC_SCRATCH_BYTES; at I=1536, top-8 that is M > 15) return W2A16_ERR_WORKSPACE.
  * The first call on a device looks up that array's device address for the calling thread's current
  * device (which must own `stream`); make that first call before any stream capture. All calls share
  * the one array: calls that overlap on the GPU (different streams, or concurrent graph replays) race

@@ -40,7 +40,8 @@ enum Status : int {
   kErrDevice = 6,
 };
 
-// Device-side error word: bit 0 = an expert id outside [0, E), bit 1 = a grid wait gave up.
+// Device-side error word: bit 0 = an expert id outside [0, E) (or an arena slot id >= 2^20), bit 1 =
+// a bounded wait gave up, bit 2 = a misaligned shared-memory ring (copies skipped).
 __device__ __forceinline__ void flag_error(unsigned* err, unsigned bit) {
   if (err) atomicOr(err, bit);
 }
@@ -90,6 +91,20 @@ __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return
 template <>
 __device__ __forceinline__ float to_f32<float>(float v) { return v; }
 
+// Exact power-of-two helpers: the frexp exponent E of a positive finite m (m = f * 2^E, f in [0.5, 1)),
+// read from the float's exponent field, and 2^k built the same way; both fall back to the library
+// functions only outside the normal range.
+__device__ __forceinline__ int frexp_exponent(float m) {
+  const int be = (int)((__float_as_uint(m) >> 23) & 0xFFu);
+  if (be != 0) return be - 126;
+  int E = 0;
+  frexpf(m, &E);
+  return E;
+}
+__device__ __forceinline__ float pow2f(int k) {
+  return (k >= -126 && k <= 127) ? __uint_as_float((unsigned)(k + 127) << 23) : ldexpf(1.f, k);
+}
+
 // One warp converts one 128-value group of an activation row (src points at the group's first
 // element). Lane l owns elements 4l .. 4l+3.
 template <typename T>
@@ -101,10 +116,8 @@ __device__ __forceinline__ void prep_group_warp(const T* __restrict__ src, int g
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   // mx = f * 2^E with f in [0.5, 1) -> x / 2^(E-15) lies in (-32768, 32768)
-  int E = 0;
-  if (mx > 0.f) frexpf(mx, &E);
-  const int e = E - 15;
-  const float inv = ldexpf(1.f, -e);
+  const int e = (mx > 0.f ? frexp_exponent(mx) : 0) - 15;
+  const float inv = pow2f(-e);
   int s = 0;
   uint16_t* half = reinterpret_cast<uint16_t*>(tab.pairs);
 #pragma unroll
@@ -122,7 +135,63 @@ __device__ __forceinline__ void prep_group_warp(const T* __restrict__ src, int g
   for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
   if (lane == 0) {
     tab.m64x[g] = -64 * s;
-    tab.scl[g] = ldexpf(1.f, e - 6);
+    tab.scl[g] = pow2f(e - 6);
+  }
+}
+
+// NG groups at once, with their lane reductions interleaved (the same conversion as prep_group_regs):
+// lane l holds elements 4l .. 4l+3 of group gl[j] in v[j]; group j goes to the table of a K-long row
+// that starts toff[j] bytes after `base` (pairs, then m64x, then scl); groups with gl[j] < 0 are
+// skipped. Lane pairs (2i, 2i+1) hold the two 16-bit halves of the same packed register, so even lanes
+// store whole words.
+template <int NG>
+__device__ __forceinline__ void prep_groups(const float (&v)[NG][4], const int (&gl)[NG], const int (&toff)[NG],
+                                            unsigned char* base, int K, int lane) {
+  float mx[NG];
+#pragma unroll
+  for (int j = 0; j < NG; ++j)
+    mx[j] = fmaxf(fmaxf(fabsf(v[j][0]), fabsf(v[j][1])), fmaxf(fabsf(v[j][2]), fabsf(v[j][3])));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int j = 0; j < NG; ++j) mx[j] = fmaxf(mx[j], __shfl_xor_sync(0xffffffffu, mx[j], o));
+  int e[NG], s[NG], q[NG][4];
+#pragma unroll
+  for (int j = 0; j < NG; ++j) {
+    e[j] = (mx[j] > 0.f ? frexp_exponent(mx[j]) : 0) - 15;
+    const float inv = pow2f(-e[j]);
+    s[j] = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      q[j][i] = max(-32767, min(32767, __float2int_rn(v[j][i] * inv)));
+      s[j] += q[j][i];
+    }
+  }
+  // element 4l+i of the group: word row l/4, register 2i + (l%4)/2, half l%2
+#pragma unroll
+  for (int j = 0; j < NG; ++j) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int other = __shfl_xor_sync(0xffffffffu, q[j][i], 1);
+      if (gl[j] >= 0 && (lane & 1) == 0) {
+        const uint32_t word = (uint32_t)(q[j][i] & 0xFFFF) | ((uint32_t)other << 16);
+        reinterpret_cast<uint32_t*>(base + toff[j])[(gl[j] * 8 + (lane >> 2)) * kXRegs + 2 * i + ((lane & 3) >> 1)] =
+            word;
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int j = 0; j < NG; ++j) s[j] += __shfl_xor_sync(0xffffffffu, s[j], o);
+  if (lane == 0) {
+#pragma unroll
+    for (int j = 0; j < NG; ++j)
+      if (gl[j] >= 0) {
+        int* m64x = reinterpret_cast<int*>(base + toff[j] + (size_t)(K / 16) * kXRegs * 4);
+        m64x[gl[j]] = -64 * s[j];
+        reinterpret_cast<float*>(m64x + K / kGroup)[gl[j]] = pow2f(e[j] - 6);
+      }
   }
 }
 
@@ -131,10 +200,8 @@ __device__ __forceinline__ void prep_group_regs(const float (&v)[4], int gl, XTa
   float mx = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  int E = 0;
-  if (mx > 0.f) frexpf(mx, &E);
-  const int e = E - 15;
-  const float inv = ldexpf(1.f, -e);
+  const int e = (mx > 0.f ? frexp_exponent(mx) : 0) - 15;
+  const float inv = pow2f(-e);
   int s = 0;
   uint16_t* half = reinterpret_cast<uint16_t*>(tab.pairs);
 #pragma unroll
@@ -150,7 +217,7 @@ __device__ __forceinline__ void prep_group_regs(const float (&v)[4], int gl, XTa
   for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
   if (lane == 0) {
     tab.m64x[gl] = -64 * s;
-    tab.scl[gl] = ldexpf(1.f, e - 6);
+    tab.scl[gl] = pow2f(e - 6);
   }
 }
 
@@ -162,10 +229,8 @@ __device__ __forceinline__ void prep_group_warp_l2(const float* __restrict__ src
   float mx = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  int E = 0;
-  if (mx > 0.f) frexpf(mx, &E);
-  const int e = E - 15;
-  const float inv = ldexpf(1.f, -e);
+  const int e = (mx > 0.f ? frexp_exponent(mx) : 0) - 15;
+  const float inv = pow2f(-e);
   int s = 0;
   uint16_t* half = reinterpret_cast<uint16_t*>(tab.pairs);
 #pragma unroll
@@ -181,7 +246,7 @@ __device__ __forceinline__ void prep_group_warp_l2(const float* __restrict__ src
   for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
   if (lane == 0) {
     tab.m64x[gl] = -64 * s;
-    tab.scl[gl] = ldexpf(1.f, e - 6);
+    tab.scl[gl] = pow2f(e - 6);
   }
 }
 

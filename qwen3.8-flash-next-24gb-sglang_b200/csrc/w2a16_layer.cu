@@ -24,13 +24,27 @@
 // into registers with 16-byte non-allocating loads -- 8 word rows of its 4 columns, 4 scales and one
 // zero-point byte -- one item ahead of the one it is reducing; those loads hit L2 or merge with the
 // prefetch in flight, and no shared-memory staging or copy engine sits on the path.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "w2a16_kernels.h"
 
 namespace w2a16 {
 namespace {
 
-constexpr int kThreads = 512;
+constexpr int kThreads = 512;                                // reducing warps (both modes)
 constexpr int kWarps = kThreads / 32;
+constexpr int kProducers = 4;                                // producer warps (copy-engine mode)
+constexpr int kTmaThreads = kThreads + 32 * kProducers;
+// Copy-engine mode: one stage of the shared-memory ring holds one item -- codes at 0 (4 KB: 16 word rows
+// x [32 gate | 32 up] columns, or 32 word rows x 32 columns), scales at 4096 (256 B), zero-point windows
+// at 4352 (64 B); every offset a multiple of 128 bytes, as tensor copies require.
+constexpr int kStageBytes = 4480;
+constexpr int kScaleOff = 4096;
+constexpr int kZeroOff = 4352;
+constexpr int kMinStages = 16, kMaxStages = 48;             // multiples of kProducers
+constexpr int kSlotExtent = 1 << 20;                         // slot ids the arena tensor maps accept
+
 constexpr unsigned kSpinLimit = 1u << 22;                    // polls before a wait gives up
 
 struct Geo {
@@ -75,6 +89,7 @@ struct RowPtr {
   const char* s[2];
   const uint8_t* z[2];
   int ok[2];
+  int slot;      // arena slot of the row's expert (copy-engine mode)
 };
 
 SmemPlan smem_plan(const Geo& g) {
@@ -91,6 +106,11 @@ SmemPlan smem_plan(const Geo& g) {
 }
 
 struct FusedParams {
+  // copy-engine mode: tensor maps over the slot arena -- gate_up codes / scales / zero points (4-D:
+  // column within half, half, row, slot) and down codes / scales / zero points (3-D: column, row, slot)
+  CUtensorMap tm[6];
+  int nstage;
+  size_t off_stages, off_bars;
   const __nv_bfloat16* x;
   const int32_t* ids;
   const float* topk_w;
@@ -99,9 +119,9 @@ struct FusedParams {
   float rsf;
   __nv_bfloat16* y;
   Geo geo;
-  size_t off_mail1, off_mail2, off_rows, off_split;
-  unsigned* bar_count;   // grid barrier
-  unsigned* bar_gen;
+  size_t off_tabs, off_mail1, off_mail2, off_rows, off_split;
+  unsigned* bar_count;   // grid barrier: arrivals (zero between calls)
+  unsigned* bar_gen;     // grid barrier: generation, 128 bytes further
   float* hfin;           // [R][I] h of h-blocks computed wholly inside one CTA
   float* hpart;          // [2 sides][R][2 (gate, up)][I] partial sums of h-blocks split across two CTAs
   unsigned* err;
@@ -115,11 +135,9 @@ __device__ __forceinline__ XTable table_at(unsigned char* base, int K) {
   return t;
 }
 
-__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
+// Barrier of the 512 reducing threads only (the producer warp of copy-engine mode never joins).
+__device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;\n" ::"n"(kThreads) : "memory"); }
+
 
 // One entry of a warp's work list.
 struct Work {
@@ -128,10 +146,12 @@ struct Work {
   int slot;   // mailbox index within the CTA
   int unit;   // phase 2: unit slot within the CTA
   int jr;     // phase 2: row index within the token
+  int seq;    // position in the CTA's item order (copy-engine ring)
 };
 
 struct WarpList {
   int a;      // CTA's phase-1 range start
+  int range;  // CTA's phase-1 items
   int n1w;    // phase-1 items of this warp
   int nu;     // phase-2 units of this CTA
   int n2w;    // phase-2 items of this warp per unit
@@ -143,6 +163,7 @@ __device__ __forceinline__ WarpList warp_list(const Geo& g, int cta, int warp) {
   const long long a = (long long)cta * g.n1 / g.grid, b = (long long)(cta + 1) * g.n1 / g.grid;
   L.a = (int)a;
   const int range = (int)(b - a);
+  L.range = range;
   L.n1w = range > warp ? (range - warp + kWarps - 1) / kWarps : 0;
   L.nu = cta < g.u2 ? (g.u2 - cta + g.grid - 1) / g.grid : 0;
   L.n2w = g.s2 > warp ? (g.s2 - warp + kWarps - 1) / kWarps : 0;
@@ -160,6 +181,7 @@ __device__ __forceinline__ Work work_at(const Geo& g, const WarpList& L, int cta
     w.b = rem / g.kp1;
     w.kp = rem - w.b * g.kp1;
     w.slot = i - L.a;
+    w.seq = warp + kWarps * t;
     return w;
   }
   const int t2 = t - L.n1w;
@@ -174,6 +196,7 @@ __device__ __forceinline__ Work work_at(const Geo& g, const WarpList& L, int cta
   w.r = m * g.top_k + w.jr;
   w.unit = q;
   w.slot = q * g.s2 + j;
+  w.seq = L.range + q * g.s2 + j;
   return w;
 }
 
@@ -278,38 +301,218 @@ __device__ __forceinline__ void dot_regs(const ItemRegs& it, const XTable& tb, i
   }
 }
 
-// All CTAs arrive; thread 0 of each CTA calls this. Gives up after kSpinLimit polls (error bit 1).
-__device__ void grid_barrier(unsigned* count, unsigned* gen, unsigned ncta, unsigned* err) {
-  const unsigned g0 = ld_acquire(gen);
-  __threadfence();
-  if (atomicAdd(count, 1u) == ncta - 1) {
-    *count = 0u;
-    __threadfence();
-    atomicAdd(gen, 1u);
-  } else {
-    unsigned it = 0;
-    while (ld_acquire(gen) == g0) {
-      if (++it > kSpinLimit) {
-        flag_error(err, 2u);
-        break;
-      }
-      __nanosleep(it < 32 ? 32 : 128);
+// ----------------------------------------------------------------------------- copy-engine mode
+__device__ __forceinline__ uint32_t smem_u32(const void* ptr) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(ptr));
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_tx(uint32_t bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, unsigned parity) {
+  unsigned ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for the phase of the given parity (non-blocking polls, optionally with a short sleep
+// between them); error bit 1 when it never completes.
+__device__ __forceinline__ void mbar_wait(uint32_t bar, unsigned parity, unsigned* err, bool nap = false) {
+  unsigned it = 0;
+  while (!mbar_try(bar, parity)) {
+    if (++it > kSpinLimit) {
+      flag_error(err, 2u);
+      return;
     }
+    if (nap) __nanosleep(20);
   }
-  __threadfence();
+}
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];\n" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
+      "%5}], [%6];\n" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
+      : "memory");
 }
 
+__device__ __forceinline__ void st_volatile_shared(int* ptr, int v) {
+  asm volatile("st.volatile.shared.s32 [%0], %1;\n" ::"r"(smem_u32(ptr)), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_volatile_shared(const int* ptr) {
+  int v;
+  asm volatile("ld.volatile.shared.s32 %0, [%1];\n" : "=r"(v) : "r"(smem_u32(ptr)) : "memory");
+  return v;
+}
+// Bounded wait until the producer has armed stage `st` for item `seq` (error bit 1 when it never does).
+__device__ __forceinline__ void wait_tag(const int* tags, int st, int seq, unsigned* err) {
+  unsigned it = 0;
+  while (ld_volatile_shared(tags + st) != seq) {
+    if (++it > kSpinLimit) {
+      flag_error(err, 2u);
+      return;
+    }
+  }
+}
+
+// Item i of the CTA's order: its phase-1 range first, then (unit, item within unit) of phase 2.
+__device__ __forceinline__ Work cta_item(const Geo& g, const WarpList& L, int cta, int i) {
+  Work w{};
+  if (i < L.range) {
+    const int ii = L.a + i;
+    const int per_row = g.nb1 * g.kp1;
+    w.kind = 1;
+    w.r = ii / per_row;
+    const int rem = ii - w.r * per_row;
+    w.b = rem / g.kp1;
+    w.kp = rem - w.b * g.kp1;
+    return w;
+  }
+  const int i2 = i - L.range;
+  const int q = i2 / g.s2, j = i2 - q * g.s2;
+  const int u = cta + g.grid * q, m = u / g.nb2;
+  w.kind = 2;
+  w.b = u - m * g.nb2;
+  w.jr = j / g.kp2;
+  w.kp = j - w.jr * g.kp2;
+  w.r = m * g.top_k + w.jr;
+  return w;
+}
+
+// The producers: lane 0 of producer warp pr streams items pr, pr + kProducers, ... of the CTA's order
+// through the ring (one issuing thread sustains only about a quarter of an SM's share of HBM bandwidth:
+// each arm-and-copy sequence has a long latency, so several threads issue side by side). The stage count
+// is a multiple of kProducers, so every stage has a single producer. Each item is one tensor copy of
+// codes (4 KB), one of scales and one of zero-point windows, completing on the stage's `full` barrier; a
+// stage is refilled once the warp that reduced it arrived on its `empty` barrier. Items of a
+// non-resident expert complete their phase on the arrival alone.
+__device__ void produce(const FusedParams& p, const WarpList& L, int cta, const RowPtr* rows, unsigned char* stages,
+                        uint32_t bars, int* tags, int pr) {
+  const Geo& g = p.geo;
+  const int ns = p.nstage;
+  const int n = L.range + L.nu * g.s2;
+  const bool hz = p.map13.has_zeros != 0;
+  const bool aligned = (smem_u32(stages) & 127u) == 0;        // tensor copies land on 128-byte boundaries
+  if (!aligned) flag_error(p.err, 4u);
+  for (int i = pr; i < n; i += kProducers) {
+    const int st = i % ns;
+    const uint32_t full = bars + st * 8, empty = bars + (ns + st) * 8;
+    if (i >= ns) mbar_wait(empty, (unsigned)(i / ns - 1) & 1u, p.err, true);
+    // Tag the stage with the item it now holds. A warp waits for its item's tag before it waits on the
+    // stage's `full` phase: a stage is refilled by another warp's item, and without the tag a warp that
+    // runs ahead could take the still-pending previous fill's phase parity for its own.
+    st_volatile_shared(tags + st, i);
+    const Work w = cta_item(g, L, cta, i);
+    const RowPtr& rp = rows[w.r];
+    if (!aligned || !rp.ok[w.kind - 1] || rp.slot < 0 || rp.slot >= kSlotExtent) {
+      mbar_arrive(full);
+      continue;
+    }
+    const uint32_t dst = smem_u32(stages + (size_t)st * kStageBytes);
+    mbar_arrive_tx(full, (unsigned)(kScaleOff + 256 + (hz ? 64 : 0)));
+    const int zx = (8 * w.b) & ~15;                          // 16-byte aligned zero-point window
+    if (w.kind == 1) {
+      tma_load_4d(dst, &p.tm[0], w.b * 32, 0, 16 * w.kp, rp.slot, full);
+      tma_load_4d(dst + kScaleOff, &p.tm[1], w.b * 32, 0, 2 * w.kp, rp.slot, full);
+      if (hz) tma_load_4d(dst + kZeroOff, &p.tm[2], zx, 0, 2 * w.kp, rp.slot, full);
+    } else {
+      tma_load_3d(dst, &p.tm[3], w.b * 32, 32 * w.kp, rp.slot, full);
+      tma_load_3d(dst + kScaleOff, &p.tm[4], w.b * 32, 4 * w.kp, rp.slot, full);
+      if (hz) tma_load_3d(dst + kZeroOff, &p.tm[5], zx, 4 * w.kp, rp.slot, full);
+    }
+  }
+  // every copy has landed before the producer leaves (the reducing warps wait on the same phases)
+  for (int st = pr; st < ns && st < n; st += kProducers) {
+    const int last = st + ((n - 1 - st) / ns) * ns;
+    mbar_wait(bars + st * 8, (unsigned)(last / ns) & 1u, p.err, true);
+  }
+}
+
+// 4 columns x 1 group of this lane from a ring stage. Gate_up stages hold 256-byte word rows (32 gate |
+// 32 up columns), scales [group][half][32] and zero windows [group][half][16 B]; down stages 128-byte
+// rows, scales [group][32] and windows [group][16 B].
+__device__ __forceinline__ void dot_stage(const unsigned char* st, const Work& w, int lane, const XTable& tb, int gl,
+                                          bool sbf, bool has_z, float (&v)[4]) {
+  const bool k1 = w.kind == 1;
+  const int gi = k1 ? (lane >> 4) : (lane >> 3);
+  const int q = k1 ? (lane & 15) : (lane & 7);
+  const int side = k1 && q >= 8 ? 1 : 0;
+  const int q8 = k1 ? (q & 7) : q;
+  const int row_bytes = k1 ? 256 : 128;
+  const int sub = k1 ? gi * 2 + side : gi;                   // (group, half) index of scales / windows
+  const unsigned char* code = st + (size_t)(8 * gi) * row_bytes + side * 128 + q8 * 16;
+  int acc[4][4];
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[c][j] = 0;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const uint4 wd = *reinterpret_cast<const uint4*>(code + k * row_bytes);
+    const uint4* xp = reinterpret_cast<const uint4*>(tb.pairs + (gl * 8 + k) * kXRegs);
+    const uint4 xa = xp[0], xb = xp[1];
+    const uint32_t xr[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+    word_dot(wd.x, xr, acc[0]);
+    word_dot(wd.y, xr, acc[1]);
+    word_dot(wd.z, xr, acc[2]);
+    word_dot(wd.w, xr, acc[3]);
+  }
+  const uint2 sr = *reinterpret_cast<const uint2*>(st + kScaleOff + (sub * 32 + q8 * 4) * 2);
+  float s[4];
+  if (sbf) {
+    const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&sr.x);
+    const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&sr.y);
+    s[0] = __low2float(a); s[1] = __high2float(a); s[2] = __low2float(b); s[3] = __high2float(b);
+  } else {
+    const __half2 a = *reinterpret_cast<const __half2*>(&sr.x);
+    const __half2 b = *reinterpret_cast<const __half2*>(&sr.y);
+    s[0] = __low2float(a); s[1] = __high2float(a); s[2] = __low2float(b); s[3] = __high2float(b);
+  }
+  const uint32_t zbyte = has_z ? (uint32_t)st[kZeroOff + sub * 16 + ((8 * w.b) & 15) + q8] : 0u;
+  const int m64x = tb.m64x[gl];
+  const float scl = tb.scl[gl];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const int zp = has_z ? (int)((zbyte >> (2 * c)) & 3u) : 2;
+    const int T = combine_classes(acc[c]) + zp * m64x;
+    v[c] = (float)T * (s[c] * scl);
+  }
+}
+
+
+template <bool kTma>
 __device__ __forceinline__ void process_work(const FusedParams& p, const Work& w, int lane, const ItemRegs& it,
-                                             unsigned char* smem, float* mail1, float* mail2, const RowPtr* rows) {
+                                             const unsigned char* stage, unsigned char* smem, float* mail1,
+                                             float* mail2, const RowPtr* rows) {
   const Geo& g = p.geo;
   const bool k1 = w.kind == 1;
   const int mi = w.kind - 1;
   const RowPtr& rp = rows[w.r];
-  const XTable tb = k1 ? table_at(smem + (size_t)(w.r / g.top_k) * token_table_bytes(g.H), g.H)
-                       : table_at(smem + (size_t)(w.unit * g.top_k + w.jr) * token_table_bytes(g.I), g.I);
+  unsigned char* tabs = smem + p.off_tabs;
+  const XTable tb = k1 ? table_at(tabs + (size_t)(w.r / g.top_k) * token_table_bytes(g.H), g.H)
+                       : table_at(tabs + (size_t)(w.unit * g.top_k + w.jr) * token_table_bytes(g.I), g.I);
   const LaneMap lm = lane_map(g, w, lane, rows);
   float v[4] = {0.f, 0.f, 0.f, 0.f};
-  if (lm.valid) dot_regs(it, tb, lm.gl, p.scale_bf16 != 0, rp.z[mi] != nullptr, v);
+  if (lm.valid) {
+    if (kTma) dot_stage(stage, w, lane, tb, lm.gl, p.scale_bf16 != 0, rp.z[mi] != nullptr, v);
+    else dot_regs(it, tb, lm.gl, p.scale_bf16 != 0, rp.z[mi] != nullptr, v);
+  }
   if (k1) {
 #pragma unroll
     for (int c = 0; c < 4; ++c) v[c] += __shfl_xor_sync(0xffffffffu, v[c], 16);
@@ -328,15 +531,45 @@ __device__ __forceinline__ void process_work(const FusedParams& p, const Work& w
   }
 }
 
-// Phase switch, entered by every warp of the CTA once its gate_up items are done: sum the CTA's
-// h-block partials, publish them, grid barrier, then build the h tables of this CTA's down units.
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* ptr) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(ptr) : "memory");
+  return v;
+}
+
+// All CTAs arrive; thread 0 of each CTA calls this. The arrival count and the generation word sit on
+// different 128-byte lines, so the pollers of the generation never queue the arrivals' atomics. Gives
+// up after kSpinLimit polls (error bit 1).
+__device__ void grid_barrier(unsigned* count, unsigned* gen, unsigned ncta, unsigned* err) {
+  const unsigned g0 = ld_acquire_u32(gen);
+  __threadfence();
+  if (atomicAdd(count, 1u) == ncta - 1) {
+    *count = 0u;
+    __threadfence();
+    atomicAdd(gen, 1u);
+  } else {
+    unsigned it = 0;
+    while (ld_acquire_u32(gen) == g0) {
+      if (++it > kSpinLimit) {
+        flag_error(err, 2u);
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  __threadfence();
+}
+
+// Phase switch, entered by every warp of the CTA once its gate_up items are done: sum the CTA's h-block
+// partials in item order and publish them (whole blocks as h, blocks split by a CTA range boundary as
+// their side's (gate, up) partial sums), grid barrier, then build the activation tables of this CTA's
+// down units from h: every warp loads all its groups' h values at once, then converts them together.
+template <int kHB>
 __device__ __forceinline__ void phase_switch(const FusedParams& p, int cta, int warp, int lane, unsigned char* smem,
                                              const float* mail1, const unsigned char* split) {
   const Geo& g = p.geo;
   const WarpList L = warp_list(g, cta, warp);
-  __syncthreads();
-  // h-blocks of this CTA's range: fixed-order sums; whole blocks publish h, split blocks their side's
-  // (gate, up) partial sums
+  csync();
   {
     const long long a = L.a, b = (long long)(cta + 1) * g.n1 / g.grid;
     if (b > a) {
@@ -362,27 +595,30 @@ __device__ __forceinline__ void phase_switch(const FusedParams& p, int cta, int 
       }
     }
   }
-  __syncthreads();
+  csync();
   if (threadIdx.x == 0) grid_barrier(p.bar_count, p.bar_gen, gridDim.x, p.err);
-  __syncthreads();
+  csync();
 
-  // ---------------------------------------------------------------- phase 2: down items
-  // h tables of this CTA's units, one warp per (unit, row, group), loads issued in batches
   const int per_unit = g.top_k * g.G2;
   const int ntab = L.nu * per_unit;
-  constexpr int kHB = 3;
+  unsigned char* tabs = smem + p.off_tabs;
   for (int k0 = warp; k0 < ntab; k0 += kHB * kWarps) {
     float hv[kHB][4];
+    int gl[kHB], toff[kHB];
 #pragma unroll
     for (int j = 0; j < kHB; ++j) {
       const int k = k0 + j * kWarps;
       hv[j][0] = hv[j][1] = hv[j][2] = hv[j][3] = 0.f;
+      gl[j] = -1;
+      toff[j] = 0;
       if (k < ntab) {
         const int q = k / per_unit, rem = k - q * per_unit;
         const int jr = rem / g.G2, gg = rem - jr * g.G2;
         const int m = (cta + g.grid * q) / g.nb2;
         const int r = m * g.top_k + jr;
         const int col = gg * kGroup + 4 * lane;
+        gl[j] = gg;
+        toff[j] = (q * g.top_k + jr) * (int)token_table_bytes(g.I);
         if (!split[r * g.nb1 + col / 32]) {
           const float4 h4 = __ldcg(reinterpret_cast<const float4*>(p.hfin + (size_t)r * g.I + col));
           hv[j][0] = h4.x; hv[j][1] = h4.y; hv[j][2] = h4.z; hv[j][3] = h4.w;
@@ -400,22 +636,16 @@ __device__ __forceinline__ void phase_switch(const FusedParams& p, int cta, int 
         }
       }
     }
-#pragma unroll
-    for (int j = 0; j < kHB; ++j) {
-      const int k = k0 + j * kWarps;
-      if (k < ntab) {
-        const int q = k / per_unit, rem = k - q * per_unit;
-        const int jr = rem / g.G2, gg = rem - jr * g.G2;
-        prep_group_regs(hv[j], gg, table_at(smem + (size_t)(q * g.top_k + jr) * token_table_bytes(g.I), g.I),
-                        lane);
-      }
-    }
+    prep_groups<kHB>(hv, gl, toff, tabs, g.I, lane);
   }
-  __syncthreads();
+  csync();
 }
 
-__global__ void __launch_bounds__(kThreads, 1) fused_layer_kernel(FusedParams p) {
-  extern __shared__ __align__(16) unsigned char smem[];
+// kTma = false: register mode (any expert map), 512 threads; every lane loads its item data itself.
+// kTma = true: copy-engine mode (slot arenas), 512 reducing threads + one producer warp.
+template <bool kTma>
+__global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_kernel(const __grid_constant__ FusedParams p) {
+  extern __shared__ __align__(128) unsigned char smem[];
   const Geo& g = p.geo;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int cta = blockIdx.x;
@@ -423,29 +653,39 @@ __global__ void __launch_bounds__(kThreads, 1) fused_layer_kernel(FusedParams p)
   float* mail2 = reinterpret_cast<float*>(smem + p.off_mail2);
   RowPtr* rows = reinterpret_cast<RowPtr*>(smem + p.off_rows);
   unsigned char* split = smem + p.off_split;
+  unsigned char* stages = kTma ? smem + p.off_stages : nullptr;
+  const uint32_t bars = kTma ? smem_u32(smem + p.off_bars) : 0u;
+  int* tags = kTma ? reinterpret_cast<int*>(smem + p.off_bars + 16 * (size_t)p.nstage) : nullptr;
 
-  // Start the whole layer's weight stream: this CTA's 1/grid share of every routed row's six arrays.
-  // A prefetch is only a hint, so arrays whose base is not 16-byte aligned are left to the loads.
-  for (int idx = threadIdx.x; idx < g.R * 6; idx += kThreads) {
-    const int r = idx / 6, arr = idx - r * 6, ph = arr / 3, kind = arr - ph * 3;
-    const ExpertMap& mp = ph == 0 ? p.map13 : p.map2;
-    const uint32_t* wb = nullptr;
-    const char* sb = nullptr;
-    const uint8_t* zb = nullptr;
-    if (!mp.resolve(p.ids[r], wb, sb, zb, nullptr)) continue;
-    const int64_t K = ph == 0 ? g.H : g.I, N = ph == 0 ? 2 * g.I : g.H;
-    const char* base = kind == 0 ? reinterpret_cast<const char*>(wb)
-                                 : (kind == 1 ? sb : reinterpret_cast<const char*>(zb));
-    const int64_t bytes = kind == 0 ? (K / 16) * N * 4 : (kind == 1 ? (K / kGroup) * N * 2 : (K / kGroup) * (N / 4));
-    if (base == nullptr || (reinterpret_cast<uintptr_t>(base) & 15u)) continue;
-    const int64_t chunk = ((bytes + g.grid - 1) / g.grid + 15) & ~int64_t(15);
-    const int64_t start = (int64_t)cta * chunk;
-    const int64_t len = (start < bytes ? (bytes - start < chunk ? bytes - start : chunk) : 0) & ~int64_t(15);
-    if (len > 0)
-      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(base + start), "r"((unsigned)len) : "memory");
+  if (!kTma) {
+    // Start the whole layer's weight stream: this CTA's 1/grid share of every routed row's six arrays.
+    // A prefetch is only a hint, so arrays whose base is not 16-byte aligned are left to the loads.
+    for (int idx = threadIdx.x; idx < g.R * 6; idx += blockDim.x) {
+      const int r = idx / 6, arr = idx - r * 6, ph = arr / 3, kind = arr - ph * 3;
+      const ExpertMap& mp = ph == 0 ? p.map13 : p.map2;
+      const uint32_t* wb = nullptr;
+      const char* sb = nullptr;
+      const uint8_t* zb = nullptr;
+      if (!mp.resolve(p.ids[r], wb, sb, zb, nullptr)) continue;
+      const int64_t K = ph == 0 ? g.H : g.I, N = ph == 0 ? 2 * g.I : g.H;
+      const char* base = kind == 0 ? reinterpret_cast<const char*>(wb)
+                                   : (kind == 1 ? sb : reinterpret_cast<const char*>(zb));
+      const int64_t bytes =
+          kind == 0 ? (K / 16) * N * 4 : (kind == 1 ? (K / kGroup) * N * 2 : (K / kGroup) * (N / 4));
+      if (base == nullptr || (reinterpret_cast<uintptr_t>(base) & 15u)) continue;
+      const int64_t chunk = ((bytes + g.grid - 1) / g.grid + 15) & ~int64_t(15);
+      const int64_t start = (int64_t)cta * chunk;
+      const int64_t len = (start < bytes ? (bytes - start < chunk ? bytes - start : chunk) : 0) & ~int64_t(15);
+      if (len > 0)
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(base + start), "r"((unsigned)len) : "memory");
+    }
+  } else if (threadIdx.x < 2 * p.nstage) {
+    mbar_init(bars + threadIdx.x * 8, 1);                     // full[0..ns), then empty[0..ns)
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    if (threadIdx.x < p.nstage) tags[threadIdx.x] = -1;
   }
 
-  const WarpList L = warp_list(g, cta, warp);
+  const WarpList L = warp_list(g, cta, warp < kWarps ? warp : 0);
   const int total = L.total();
   const int nxt = g.M * g.G1;
 
@@ -455,7 +695,7 @@ __global__ void __launch_bounds__(kThreads, 1) fused_layer_kernel(FusedParams p)
 #pragma unroll
   for (int j = 0; j < kXPre; ++j) {
     const int t = warp + j * kWarps;
-    if (t < nxt) {
+    if (warp < kWarps && t < nxt) {
       const int m = t / g.G1, gi = t - m * g.G1;
       const __nv_bfloat162* src =
           reinterpret_cast<const __nv_bfloat162*>(p.x + (int64_t)m * g.H + gi * kGroup + 4 * lane);
@@ -466,60 +706,81 @@ __global__ void __launch_bounds__(kThreads, 1) fused_layer_kernel(FusedParams p)
     }
   }
   // expert bases of every routed row, resolved once per CTA; h-blocks split by a CTA range boundary
-  for (int r = threadIdx.x; r < g.R; r += kThreads) {
+  for (int r = threadIdx.x; r < g.R; r += blockDim.x) {
     RowPtr rp;
     const int e = p.ids[r];
     rp.ok[0] = p.map13.resolve(e, rp.w[0], rp.s[0], rp.z[0], p.err);
     rp.ok[1] = p.map2.resolve(e, rp.w[1], rp.s[1], rp.z[1], p.err);
+    rp.slot = (p.map13.slots != nullptr && e >= 0 && e < p.map13.E) ? p.map13.slots[e] : -1;
+    if (kTma && rp.slot >= kSlotExtent) flag_error(p.err, 1u);
     rows[r] = rp;
   }
-  for (int k = threadIdx.x; k < g.R * g.nb1; k += kThreads) split[k] = 0;
+  for (int k = threadIdx.x; k < g.R * g.nb1; k += blockDim.x) split[k] = 0;
   __syncthreads();
-  for (int c = 1 + threadIdx.x; c < g.grid; c += kThreads) {
+  for (int c = 1 + threadIdx.x; c < g.grid && threadIdx.x < kThreads; c += kThreads) {  // read after csync()
     const long long ac = (long long)c * g.n1 / g.grid;
     if (ac % g.kp1) split[ac / g.kp1] = 1;
   }
+  if (kTma && warp >= kWarps) {
+    if (lane == 0) produce(p, warp_list(g, cta, 0), cta, rows, stages, bars, tags, warp - kWarps);
+    return;
+  }
 
-  // first item of this warp in flight while the activation tables are built
+  // register mode: this warp's first item in flight while the activation tables are built
   ItemRegs cur, nxt_it;
   Work wn = work_at(g, L, cta, warp, 0);
-  load_item(p, wn, lane, rows, nxt_it);
+  if (!kTma) load_item(p, wn, lane, rows, nxt_it);
+  {
+    int gl[kXPre], toff[kXPre];
 #pragma unroll
-  for (int j = 0; j < kXPre; ++j) {
-    const int tt = warp + j * kWarps;
-    if (tt < nxt) {
-      const int m = tt / g.G1, gi = tt - m * g.G1;
-      prep_group_regs(xv[j], gi, table_at(smem + (size_t)m * token_table_bytes(g.H), g.H), lane);
+    for (int j = 0; j < kXPre; ++j) {
+      const int tt = warp + j * kWarps;
+      const int m = tt / g.G1;
+      gl[j] = tt < nxt ? tt - m * g.G1 : -1;
+      toff[j] = tt < nxt ? m * (int)token_table_bytes(g.H) : 0;
     }
+    prep_groups<kXPre>(xv, gl, toff, smem + p.off_tabs, g.H, lane);
   }
   for (int tt = warp + kXPre * kWarps; tt < nxt; tt += kWarps) {
     const int m = tt / g.G1, gi = tt - m * g.G1;
     const __nv_bfloat16* src = p.x + (int64_t)m * g.H + gi * kGroup + 4 * lane;
     const float v[4] = {__bfloat162float(src[0]), __bfloat162float(src[1]), __bfloat162float(src[2]),
                         __bfloat162float(src[3])};
-    prep_group_regs(v, gi, table_at(smem + (size_t)m * token_table_bytes(g.H), g.H), lane);
+    prep_group_regs(v, gi, table_at(smem + p.off_tabs + (size_t)m * token_table_bytes(g.H), g.H), lane);
   }
-  __syncthreads();
+  csync();
 
-  // One loop over this warp's work list: take the item whose loads are in flight, issue the next one's,
-  // reduce. t == n1w (the warp's first down item) switches phase, with that item already loading.
+  // One loop over this warp's work list. Register mode: take the item whose loads are in flight, issue
+  // the next one's, reduce. Copy-engine mode: wait for the item's ring stage, reduce, release the stage.
+  // t == n1w (the warp's first down item) switches phase.
   bool p1done = false;
   for (int t = 0;; ++t) {
     if (t == L.n1w && !p1done) {
-      phase_switch(p, cta, warp, lane, smem, mail1, split);
+      phase_switch<kTma ? 6 : 2>(p, cta, warp, lane, smem, mail1, split);
       p1done = true;
     }
     if (t >= total) break;
-    const Work wc = wn;
-    cur = nxt_it;
-    if (t + 1 < total) {
-      wn = work_at(g, L, cta, warp, t + 1);
-      load_item(p, wn, lane, rows, nxt_it);
+    if (kTma) {
+      const Work w = work_at(g, L, cta, warp, t);
+      const int st = w.seq % p.nstage;
+      if (lane == 0) wait_tag(tags, st, w.seq, p.err);
+      __syncwarp();
+      mbar_wait(bars + st * 8, (unsigned)(w.seq / p.nstage) & 1u, p.err);
+      process_work<true>(p, w, lane, cur, stages + (size_t)st * kStageBytes, smem, mail1, mail2, rows);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bars + (p.nstage + st) * 8);
+    } else {
+      const Work wc = wn;
+      cur = nxt_it;
+      if (t + 1 < total) {
+        wn = work_at(g, L, cta, warp, t + 1);
+        load_item(p, wn, lane, rows, nxt_it);
+      }
+      process_work<false>(p, wc, lane, cur, nullptr, smem, mail1, mail2, rows);
+      __syncwarp();
     }
-    process_work(p, wc, lane, cur, smem, mail1, mail2, rows);
-    __syncwarp();
   }
-  __syncthreads();
+  csync();
 
   // y of each unit: fixed-order sum of its top_k x K-part partials
   for (int q = warp; q < L.nu; q += kWarps) {
@@ -532,48 +793,171 @@ __global__ void __launch_bounds__(kThreads, 1) fused_layer_kernel(FusedParams p)
 
 }  // namespace
 
-// Workspace: 256 bytes of control words (grid barrier count and generation, zero-filled before the
-// first call; the barrier leaves the count at zero), then h [R][I] fp32 and the split-block partial
-// sums [2][R][2][I] fp32.
+// Workspace: 256 bytes of control words (grid barrier arrivals at 0 and generation at 128, zero-filled
+// before the first call; the barrier leaves the arrivals at zero), then h [R][I] fp32 and the
+// split-block partial sums [2][R][2][I] fp32.
 size_t layer_workspace_bytes(int M, int H, int I, int top_k) {
   (void)H;
   if (M <= 0 || I <= 0 || top_k <= 0) return 256;
   return 256 + (size_t)M * top_k * 5 * (size_t)I * 4;
 }
 
-static int launch_fused(const LayerArgs& a, int M, const void* x, const int32_t* ids, const float* w, void* y,
-                        int grid_cap) {
+namespace {
+
+// ----------------------------------------------------------------------------- host side
+// Shared-memory plan of copy-engine mode: the ring first (offset 0, so every stage is 128-byte aligned),
+// then the plan of register mode, then 2 * nstage mbarriers and nstage stage tags. Returns 0 stages when
+// fewer than kMinStages fit.
+struct TmaPlan {
+  int nstage;
+  size_t stages, rest, total;
+};
+TmaPlan tma_plan(const Geo& g) {
+  TmaPlan t{};
+  const size_t cap = 227 * 1024;
+  t.rest = smem_plan(g).total;
+  const size_t fixed = t.rest + 2 * kMaxStages * 8 + kMaxStages * 4;
+  int ns = fixed < cap ? (int)((cap - fixed) / kStageBytes) : 0;
+  if (ns > kMaxStages) ns = kMaxStages;
+  ns -= ns % kProducers;
+  t.nstage = ns >= kMinStages ? ns : 0;
+  t.stages = (size_t)t.nstage * kStageBytes;
+  t.total = t.stages + t.rest + 2 * (size_t)t.nstage * 8 + (size_t)t.nstage * 4;
+  return t;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<PFN_cuTensorMapEncodeTiled_v12000>(nullptr);
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  }();
+  return fn;
+}
+
+// One tensor map over a slot arena: dims / strides innermost first, the last dimension the slot.
+bool encode_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* base, const cuuint64_t* dims,
+                const cuuint64_t* strides, const cuuint32_t* box) {
+  const cuuint32_t es[4] = {1, 1, 1, 1};
+  return tensor_map_encoder()(m, dt, (cuuint32_t)rank, const_cast<void*>(base), dims, strides, box, es,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The six arena maps; cached per thread on everything they depend on (the arena never moves between
+// decode steps, so steady-state calls encode nothing).
+bool arena_maps(const LayerArgs& a, CUtensorMap (&tm)[6]) {
+  struct Key {
+    const void* b[6];
+    int64_t st[6];
+    int H, I;
+    bool operator==(const Key& o) const {
+      for (int k = 0; k < 6; ++k)
+        if (b[k] != o.b[k] || st[k] != o.st[k]) return false;
+      return H == o.H && I == o.I;
+    }
+  };
+  static thread_local Key last{};
+  static thread_local bool have = false;
+  static thread_local CUtensorMap cache[6];
+  const Key k{{a.map13.wbase, a.map13.sbase, a.map13.zbase, a.map2.wbase, a.map2.sbase, a.map2.zbase},
+              {a.map13.wstride, a.map13.sstride, a.map13.zstride, a.map2.wstride, a.map2.sstride, a.map2.zstride},
+              a.H, a.I};
+  if (!(have && last == k)) {
+    have = false;
+    if (!tensor_map_encoder()) return false;
+    const cuuint64_t I = (cuuint64_t)a.I, H = (cuuint64_t)a.H, S = kSlotExtent;
+    const bool hz = a.map13.has_zeros != 0;
+    {  // gate_up: (column within half, half, row, slot)
+      const cuuint64_t dc[4] = {I, 2, H / 16, S}, sc[3] = {I * 4, 2 * I * 4, (cuuint64_t)a.map13.wstride};
+      const cuuint32_t bc[4] = {32, 2, 16, 1};
+      const cuuint64_t ds[4] = {I, 2, H / kGroup, S}, ss[3] = {I * 2, 2 * I * 2, (cuuint64_t)a.map13.sstride};
+      const cuuint32_t bs[4] = {32, 2, 2, 1};
+      if (!encode_map(&cache[0], CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, a.map13.wbase, dc, sc, bc)) return false;
+      if (!encode_map(&cache[1], CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, a.map13.sbase, ds, ss, bs)) return false;
+      if (hz) {
+        const cuuint64_t dz[4] = {I / 4, 2, H / kGroup, S}, sz[3] = {I / 4, I / 2, (cuuint64_t)a.map13.zstride};
+        const cuuint32_t bz[4] = {16, 2, 2, 1};
+        if (!encode_map(&cache[2], CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, a.map13.zbase, dz, sz, bz)) return false;
+      }
+    }
+    {  // down: (column, row, slot)
+      const cuuint64_t dc[3] = {H, I / 16, S}, sc[2] = {H * 4, (cuuint64_t)a.map2.wstride};
+      const cuuint32_t bc[3] = {32, 32, 1};
+      const cuuint64_t ds[3] = {H, I / kGroup, S}, ss[2] = {H * 2, (cuuint64_t)a.map2.sstride};
+      const cuuint32_t bs[3] = {32, 4, 1};
+      if (!encode_map(&cache[3], CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, a.map2.wbase, dc, sc, bc)) return false;
+      if (!encode_map(&cache[4], CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, a.map2.sbase, ds, ss, bs)) return false;
+      if (hz) {
+        const cuuint64_t dz[3] = {H / 4, I / kGroup, S}, sz[2] = {H / 4, (cuuint64_t)a.map2.zstride};
+        const cuuint32_t bz[3] = {16, 4, 1};
+        if (!encode_map(&cache[5], CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, a.map2.zbase, dz, sz, bz)) return false;
+      }
+    }
+    last = k;
+    have = true;
+  }
+  for (int k2 = 0; k2 < 6; ++k2) tm[k2] = cache[k2];
+  return true;
+}
+
+// Copy-engine mode needs a slot arena, 16-byte strides in every map (H and I multiples of 64) and the
+// driver's tensor-map encoder.
+bool tma_eligible(const LayerArgs& a) {
+  if (a.map13.slots == nullptr || a.map2.slots == nullptr) return false;
+  if (a.H % 64 != 0 || a.I % 64 != 0) return false;
+  return tensor_map_encoder() != nullptr;
+}
+
+int launch_fused(const LayerArgs& a, int M, const void* x, const int32_t* ids, const float* w, void* y,
+                        int grid_cap, bool tma) {
   const Geo g = make_geo(M, a.H, a.I, a.top_k, grid_cap);
   const SmemPlan sp = smem_plan(g);
   FusedParams p{};
   p.x = static_cast<const __nv_bfloat16*>(x); p.ids = ids; p.topk_w = w;
   p.map13 = a.map13; p.map2 = a.map2; p.scale_bf16 = a.scale_bf16; p.rsf = a.routed_scaling;
   p.y = static_cast<__nv_bfloat16*>(y); p.geo = g; p.err = a.err;
-  p.off_mail1 = sp.tabs;
+  size_t base = 0, total = sp.total;
+  if (tma) {
+    const TmaPlan tp = tma_plan(g);
+    if (tp.nstage == 0 || !arena_maps(a, p.tm)) return kErrShape;
+    p.nstage = tp.nstage;
+    p.off_stages = 0;
+    base = tp.stages;
+    p.off_bars = tp.stages + tp.rest;
+    total = tp.total;
+  }
+  p.off_tabs = base;
+  p.off_mail1 = base + sp.tabs;
   p.off_mail2 = p.off_mail1 + sp.mail1;
   p.off_rows = p.off_mail2 + sp.mail2;
   p.off_split = p.off_rows + sp.rows;
   unsigned* ctl = static_cast<unsigned*>(a.workspace);
   p.bar_count = ctl;
-  p.bar_gen = ctl + 1;
+  p.bar_gen = ctl + 32;
   p.hfin = reinterpret_cast<float*>(static_cast<char*>(a.workspace) + 256);
   p.hpart = p.hfin + (size_t)g.R * a.I;
 
-  if (cudaFuncSetAttribute(fused_layer_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sp.total) !=
-      cudaSuccess)
+  auto kern = tma ? fused_layer_kernel<true> : fused_layer_kernel<false>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)total) != cudaSuccess)
     return kErrLaunch;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(g.grid);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = sp.total;
+  cfg.blockDim = dim3(tma ? kTmaThreads : kThreads);
+  cfg.dynamicSmemBytes = total;
   cfg.stream = a.stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, fused_layer_kernel, p) == cudaSuccess ? kOk : kErrLaunch;
+  return cudaLaunchKernelEx(&cfg, kern, p) == cudaSuccess ? kOk : kErrLaunch;
 }
+
+}  // namespace
 
 int decode_layer_fused(const LayerArgs& a) {
   if (a.M <= 0) return kOk;
@@ -588,18 +972,24 @@ int decode_layer_fused(const LayerArgs& a) {
   if (dev != cached_dev) {
     int sms = 0;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return kErrDevice;
-    cached_cap = sms;              // one CTA of 512 threads per SM
+    cached_cap = sms;              // one CTA per SM
     cached_dev = dev;
   }
-  // tokens per launch: as many as the shared-memory plan allows
+  // tokens per launch: as many as the shared-memory plan allows (copy-engine mode also keeps a ring of
+  // at least kMinStages stages)
+  const bool tma = tma_eligible(a);
+  auto fits = [&](int m) {
+    const Geo g = make_geo(m, a.H, a.I, a.top_k, cached_cap);
+    return tma ? tma_plan(g).nstage > 0 : smem_plan(g).total <= 227 * 1024;
+  };
   int mmax = a.M;
-  while (mmax > 1 && smem_plan(make_geo(mmax, a.H, a.I, a.top_k, cached_cap)).total > 227 * 1024) --mmax;
-  if (smem_plan(make_geo(mmax, a.H, a.I, a.top_k, cached_cap)).total > 227 * 1024) return kErrShape;
+  while (mmax > 1 && !fits(mmax)) --mmax;
+  if (!fits(mmax)) return kErrShape;
   for (int m0 = 0; m0 < a.M; m0 += mmax) {
     const int mc = a.M - m0 < mmax ? a.M - m0 : mmax;
     const int st = launch_fused(a, mc, static_cast<const __nv_bfloat16*>(a.x) + (size_t)m0 * a.H,
                                 a.ids + (size_t)m0 * a.top_k, a.topk_w + (size_t)m0 * a.top_k,
-                                static_cast<__nv_bfloat16*>(a.y) + (size_t)m0 * a.H, cached_cap);
+                                static_cast<__nv_bfloat16*>(a.y) + (size_t)m0 * a.H, cached_cap, tma);
     if (st != kOk) return st;
   }
   return kOk;
