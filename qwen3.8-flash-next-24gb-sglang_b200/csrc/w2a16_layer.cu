@@ -46,6 +46,7 @@ constexpr int kMinStages = 16, kMaxStages = 48;             // multiples of kPro
 constexpr int kSlotExtent = 1 << 20;                         // slot ids the arena tensor maps accept
 
 constexpr unsigned kSpinLimit = 1u << 22;                    // polls before a wait gives up
+constexpr unsigned kWaitLimit = 1u << 17;                    // suspending mbarrier tries before a wait gives up
 
 struct Geo {
   int M, H, I, top_k, R;
@@ -80,7 +81,7 @@ __host__ __device__ __forceinline__ size_t token_table_bytes(int K) {
 }
 
 struct SmemPlan {
-  size_t tabs, mail1, mail2, rows, split, total;
+  size_t tabs, mail1, mail2, rows, hstage, misc, total;
 };
 
 // Per routed row, resolved once per CTA: expert code / scale / zero-point bases of gate_up and down.
@@ -100,8 +101,9 @@ SmemPlan smem_plan(const Geo& g) {
   s.mail1 = (size_t)g.max_range * 64 * 4;
   s.mail2 = (size_t)g.max_units * g.s2 * 32 * 4;
   s.rows = ((size_t)g.R * sizeof(RowPtr) + 15) & ~size_t(15);
-  s.split = ((size_t)g.R * g.nb1 + 15) & ~size_t(15);
-  s.total = s.tabs + s.mail1 + s.mail2 + s.rows + s.split;
+  s.hstage = (size_t)g.max_units * g.top_k * g.I * 4;           // h rows of the down units (bulk copies)
+  s.misc = 64;                                                  // mbarrier, head counter, generation
+  s.total = s.tabs + s.mail1 + s.mail2 + s.rows + s.hstage + s.misc;
   return s;
 }
 
@@ -119,11 +121,12 @@ struct FusedParams {
   float rsf;
   __nv_bfloat16* y;
   Geo geo;
-  size_t off_tabs, off_mail1, off_mail2, off_rows, off_split;
+  size_t off_tabs, off_mail1, off_mail2, off_rows, off_hstage, off_misc;
   unsigned* bar_count;   // grid barrier: arrivals (zero between calls)
   unsigned* bar_gen;     // grid barrier: generation, 128 bytes further
   float* hfin;           // [R][I] h of h-blocks computed wholly inside one CTA
-  float* hpart;          // [2 sides][R][2 (gate, up)][I] partial sums of h-blocks split across two CTAs
+  unsigned* hflags;      // [grid] generation + 1 once the CTA published the partial of its first h-block
+  float* hpart;          // [R][2 (gate, up)][I] partial sums of the tails of h-blocks split across two CTAs
   unsigned* err;
 };
 
@@ -317,22 +320,23 @@ __device__ __forceinline__ void mbar_arrive_tx(uint32_t bar, unsigned bytes) {
 __device__ __forceinline__ bool mbar_try(uint32_t bar, unsigned parity) {
   unsigned ok;
   asm volatile(
-      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 10000;\n selp.u32 %0, 1, 0, p;\n}\n"
       : "=r"(ok)
       : "r"(bar), "r"(parity)
       : "memory");
   return ok != 0;
 }
-// Bounded wait for the phase of the given parity (non-blocking polls, optionally with a short sleep
-// between them); error bit 1 when it never completes.
-__device__ __forceinline__ void mbar_wait(uint32_t bar, unsigned parity, unsigned* err, bool nap = false) {
+// Bounded wait for the phase of the given parity: try_wait suspends the thread in hardware until the
+// phase completes or a system time limit passes, so a waiter costs the copy engine no polling traffic.
+// Exactly one thread should wait; the others meet it at a warp or CTA barrier. Error bit 1 when the
+// phase never completes.
+__device__ __forceinline__ void mbar_wait(uint32_t bar, unsigned parity, unsigned* err) {
   unsigned it = 0;
-  while (!mbar_try(bar, parity)) {
-    if (++it > kSpinLimit) {
+  while (!mbar_try(bar, parity)) {                           // each try suspends for at most ~10 us
+    if (++it > kWaitLimit) {
       flag_error(err, 2u);
       return;
     }
-    if (nap) __nanosleep(20);
   }
 }
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2,
@@ -413,7 +417,7 @@ __device__ void produce(const FusedParams& p, const WarpList& L, int cta, const 
   for (int i = pr; i < n; i += kProducers) {
     const int st = i % ns;
     const uint32_t full = bars + st * 8, empty = bars + (ns + st) * 8;
-    if (i >= ns) mbar_wait(empty, (unsigned)(i / ns - 1) & 1u, p.err, true);
+    if (i >= ns) mbar_wait(empty, (unsigned)(i / ns - 1) & 1u, p.err);
     // Tag the stage with the item it now holds. A warp waits for its item's tag before it waits on the
     // stage's `full` phase: a stage is refilled by another warp's item, and without the tag a warp that
     // runs ahead could take the still-pending previous fill's phase parity for its own.
@@ -440,7 +444,7 @@ __device__ void produce(const FusedParams& p, const WarpList& L, int cta, const 
   // every copy has landed before the producer leaves (the reducing warps wait on the same phases)
   for (int st = pr; st < ns && st < n; st += kProducers) {
     const int last = st + ((n - 1 - st) / ns) * ns;
-    mbar_wait(bars + st * 8, (unsigned)(last / ns) & 1u, p.err, true);
+    mbar_wait(bars + st * 8, (unsigned)(last / ns) & 1u, p.err);
   }
 }
 
@@ -560,13 +564,58 @@ __device__ void grid_barrier(unsigned* count, unsigned* gen, unsigned ncta, unsi
   __threadfence();
 }
 
-// Phase switch, entered by every warp of the CTA once its gate_up items are done: sum the CTA's h-block
-// partials in item order and publish them (whole blocks as h, blocks split by a CTA range boundary as
-// their side's (gate, up) partial sums), grid barrier, then build the activation tables of this CTA's
-// down units from h: every warp loads all its groups' h values at once, then converts them together.
+__device__ __forceinline__ void st_release_u32(unsigned* ptr, unsigned v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;\n" ::"l"(ptr), "r"(v) : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, unsigned bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
+// Items [0, head_k) of a CTA's range are the tail of an h-block that began in the previous CTA. Once
+// they are reduced (round 0 of the item loop), the warp that completes them sums their partials and
+// publishes the (gate, up) tail sums with a flag, so the previous CTA can finish that block before the
+// grid barrier.
+__device__ void publish_head(const FusedParams& p, const WarpList& L, int cta, int lane, const float* mail1, int head_k,
+                             unsigned epoch) {
+  const Geo& g = p.geo;
+  const int blk = L.a / g.kp1;
+  const int r = blk / g.nb1, hb = blk - r * g.nb1;
+  const size_t col = (size_t)hb * 32 + lane;
+  __syncwarp();                                               // lane 0's acquire of the count covers the warp
+  float gs = 0.f, us = 0.f;
+  for (int i = 0; i < head_k; ++i) {
+    gs += mail1[(size_t)i * 64 + lane];
+    us += mail1[(size_t)i * 64 + 32 + lane];
+  }
+  p.hpart[((size_t)r * 2) * g.I + col] = gs;
+  p.hpart[((size_t)r * 2 + 1) * g.I + col] = us;
+  __threadfence();
+  __syncwarp();
+  if (lane == 0) st_release_u32(p.hflags + cta, epoch);
+}
+
+// Count one reduced head item; the warp that reduces the last of them publishes the tail sums.
+__device__ __forceinline__ void head_item_done(const FusedParams& p, const WarpList& L, int cta, int lane,
+                                               const float* mail1, int head_k, unsigned epoch, unsigned* counter) {
+  unsigned last = 0u;
+  if (lane == 0) {
+    __threadfence_block();
+    last = atomicAdd(counter, 1u) == (unsigned)head_k - 1u;
+    __threadfence_block();
+  }
+  if (__shfl_sync(0xffffffffu, last, 0)) publish_head(p, L, cta, lane, mail1, head_k, epoch);
+}
+
+// Phase switch, entered by every warp of the CTA once its gate_up items are done. (1) h of every h-block
+// this CTA finishes, in item order: whole blocks from its own partials; the block it shares with the next
+// CTA from its head part plus the tail sums that CTA published (bounded wait on its flag); the block it
+// shares with the previous CTA is finished there. (2) Grid barrier: h is complete. (3) One bulk copy per
+// h row of this CTA's down units into shared memory, then every warp converts its groups from there.
 template <int kHB>
 __device__ __forceinline__ void phase_switch(const FusedParams& p, int cta, int warp, int lane, unsigned char* smem,
-                                             const float* mail1, const unsigned char* split) {
+                                             const float* mail1, unsigned epoch, uint32_t hbar) {
   const Geo& g = p.geo;
   const WarpList L = warp_list(g, cta, warp);
   csync();
@@ -576,29 +625,52 @@ __device__ __forceinline__ void phase_switch(const FusedParams& p, int cta, int 
       const int blk0 = (int)(a / g.kp1), blk1 = (int)((b - 1) / g.kp1);
       for (int blk = blk0 + warp; blk <= blk1; blk += kWarps) {
         const long long i0 = (long long)blk * g.kp1, i1 = i0 + g.kp1;
-        const long long lo = i0 > a ? i0 : a, hi = i1 < b ? i1 : b;
+        if (i0 < a) continue;                                 // finished by the previous CTA
+        const long long hi = i1 < b ? i1 : b;
         float gs = 0.f, us = 0.f;
-        for (long long i = lo; i < hi; ++i) {
+        for (long long i = i0; i < hi; ++i) {
           gs += mail1[(size_t)(i - a) * 64 + lane];
           us += mail1[(size_t)(i - a) * 64 + 32 + lane];
         }
         const int r = blk / g.nb1, hb = blk - r * g.nb1;
         const size_t col = (size_t)hb * 32 + lane;
-        if (i0 >= a && i1 <= b) {
-          p.hfin[(size_t)r * g.I + col] = silu(gs) * us;
-        } else {
-          const int side = i0 < a ? 1 : 0;
-          float* hp = p.hpart + ((size_t)(side * g.R + r) * 2) * g.I + col;
-          hp[0] = gs;
-          hp[g.I] = us;
+        if (i1 > b) {                                         // tail published by the next CTA
+          if (lane == 0) {
+            unsigned it = 0;
+            while (ld_acquire_u32(p.hflags + cta + 1) != epoch) {
+              if (++it > kSpinLimit) {
+                flag_error(p.err, 2u);
+                break;
+              }
+              __nanosleep(32);
+            }
+          }
+          __syncwarp();
+          gs += __ldcg(p.hpart + ((size_t)r * 2) * g.I + col);
+          us += __ldcg(p.hpart + ((size_t)r * 2 + 1) * g.I + col);
         }
+        p.hfin[(size_t)r * g.I + col] = silu(gs) * us;
       }
+      __threadfence();
     }
   }
   csync();
   if (threadIdx.x == 0) grid_barrier(p.bar_count, p.bar_gen, gridDim.x, p.err);
   csync();
 
+  // (3) h rows of the down units -> shared memory (row slot q * top_k + jr), then the tables
+  float* hst = reinterpret_cast<float*>(smem + p.off_hstage);
+  const int nrows = L.nu * g.top_k;
+  const unsigned row_bytes = (unsigned)g.I * 4u;
+  if (threadIdx.x == 0) mbar_arrive_tx(hbar, row_bytes * (unsigned)nrows);
+  if (threadIdx.x < nrows) {
+    const int q = threadIdx.x / g.top_k, jr = threadIdx.x - q * g.top_k;
+    const int m = (cta + g.grid * q) / g.nb2;
+    asm volatile("fence.proxy.async.global;\n" ::: "memory");  // h was written through the generic proxy
+    bulk_g2s(smem_u32(hst + (size_t)threadIdx.x * g.I), p.hfin + (size_t)(m * g.top_k + jr) * g.I, row_bytes, hbar);
+  }
+  if (threadIdx.x == 0) mbar_wait(hbar, 0u, p.err);
+  csync();
   const int per_unit = g.top_k * g.G2;
   const int ntab = L.nu * per_unit;
   unsigned char* tabs = smem + p.off_tabs;
@@ -612,28 +684,11 @@ __device__ __forceinline__ void phase_switch(const FusedParams& p, int cta, int 
       gl[j] = -1;
       toff[j] = 0;
       if (k < ntab) {
-        const int q = k / per_unit, rem = k - q * per_unit;
-        const int jr = rem / g.G2, gg = rem - jr * g.G2;
-        const int m = (cta + g.grid * q) / g.nb2;
-        const int r = m * g.top_k + jr;
-        const int col = gg * kGroup + 4 * lane;
+        const int row = k / g.G2, gg = k - row * g.G2;         // row slot = q * top_k + jr
+        const float4 h4 = *reinterpret_cast<const float4*>(hst + (size_t)row * g.I + gg * kGroup + 4 * lane);
+        hv[j][0] = h4.x; hv[j][1] = h4.y; hv[j][2] = h4.z; hv[j][3] = h4.w;
         gl[j] = gg;
-        toff[j] = (q * g.top_k + jr) * (int)token_table_bytes(g.I);
-        if (!split[r * g.nb1 + col / 32]) {
-          const float4 h4 = __ldcg(reinterpret_cast<const float4*>(p.hfin + (size_t)r * g.I + col));
-          hv[j][0] = h4.x; hv[j][1] = h4.y; hv[j][2] = h4.z; hv[j][3] = h4.w;
-        } else {
-          const float* p0 = p.hpart + ((size_t)r * 2) * g.I + col;
-          const float* p1 = p.hpart + ((size_t)(g.R + r) * 2) * g.I + col;
-          const float4 g0 = __ldcg(reinterpret_cast<const float4*>(p0));
-          const float4 u0 = __ldcg(reinterpret_cast<const float4*>(p0 + g.I));
-          const float4 g1 = __ldcg(reinterpret_cast<const float4*>(p1));
-          const float4 u1 = __ldcg(reinterpret_cast<const float4*>(p1 + g.I));
-          hv[j][0] = silu(g0.x + g1.x) * (u0.x + u1.x);
-          hv[j][1] = silu(g0.y + g1.y) * (u0.y + u1.y);
-          hv[j][2] = silu(g0.z + g1.z) * (u0.z + u1.z);
-          hv[j][3] = silu(g0.w + g1.w) * (u0.w + u1.w);
-        }
+        toff[j] = row * (int)token_table_bytes(g.I);
       }
     }
     prep_groups<kHB>(hv, gl, toff, tabs, g.I, lane);
@@ -652,7 +707,9 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
   float* mail1 = reinterpret_cast<float*>(smem + p.off_mail1);
   float* mail2 = reinterpret_cast<float*>(smem + p.off_mail2);
   RowPtr* rows = reinterpret_cast<RowPtr*>(smem + p.off_rows);
-  unsigned char* split = smem + p.off_split;
+  unsigned* misc = reinterpret_cast<unsigned*>(smem + p.off_misc);  // [0,1] h-copy mbarrier, [2] head count,
+                                                                    // [3] grid barrier generation at entry
+  const uint32_t hbar = smem_u32(misc);
   unsigned char* stages = kTma ? smem + p.off_stages : nullptr;
   const uint32_t bars = kTma ? smem_u32(smem + p.off_bars) : 0u;
   int* tags = kTma ? reinterpret_cast<int*>(smem + p.off_bars + 16 * (size_t)p.nstage) : nullptr;
@@ -705,7 +762,7 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
       xv[j][0] = xv[j][1] = xv[j][2] = xv[j][3] = 0.f;
     }
   }
-  // expert bases of every routed row, resolved once per CTA; h-blocks split by a CTA range boundary
+  // expert bases of every routed row, resolved once per CTA
   for (int r = threadIdx.x; r < g.R; r += blockDim.x) {
     RowPtr rp;
     const int e = p.ids[r];
@@ -715,12 +772,13 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
     if (kTma && rp.slot >= kSlotExtent) flag_error(p.err, 1u);
     rows[r] = rp;
   }
-  for (int k = threadIdx.x; k < g.R * g.nb1; k += blockDim.x) split[k] = 0;
-  __syncthreads();
-  for (int c = 1 + threadIdx.x; c < g.grid && threadIdx.x < kThreads; c += kThreads) {  // read after csync()
-    const long long ac = (long long)c * g.n1 / g.grid;
-    if (ac % g.kp1) split[ac / g.kp1] = 1;
+  if (threadIdx.x == 0) {
+    mbar_init(hbar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    misc[2] = 0u;
+    misc[3] = ld_acquire_u32(p.bar_gen);                     // no CTA passes this call's barrier before all read it
   }
+  __syncthreads();
   if (kTma && warp >= kWarps) {
     if (lane == 0) produce(p, warp_list(g, cta, 0), cta, rows, stages, bars, tags, warp - kWarps);
     return;
@@ -753,22 +811,27 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
   // One loop over this warp's work list. Register mode: take the item whose loads are in flight, issue
   // the next one's, reduce. Copy-engine mode: wait for the item's ring stage, reduce, release the stage.
   // t == n1w (the warp's first down item) switches phase.
+  const unsigned epoch = misc[3] + 1u;
+  const int head_k = L.a % g.kp1 ? min(g.kp1 - L.a % g.kp1, L.range) : 0;   // items finishing a shared block
   bool p1done = false;
   for (int t = 0;; ++t) {
     if (t == L.n1w && !p1done) {
-      phase_switch<kTma ? 6 : 2>(p, cta, warp, lane, smem, mail1, split);
+      phase_switch<kTma ? 6 : 2>(p, cta, warp, lane, smem, mail1, epoch, hbar);
       p1done = true;
     }
     if (t >= total) break;
     if (kTma) {
       const Work w = work_at(g, L, cta, warp, t);
       const int st = w.seq % p.nstage;
-      if (lane == 0) wait_tag(tags, st, w.seq, p.err);
+      if (lane == 0) {
+        wait_tag(tags, st, w.seq, p.err);
+        mbar_wait(bars + st * 8, (unsigned)(w.seq / p.nstage) & 1u, p.err);
+      }
       __syncwarp();
-      mbar_wait(bars + st * 8, (unsigned)(w.seq / p.nstage) & 1u, p.err);
       process_work<true>(p, w, lane, cur, stages + (size_t)st * kStageBytes, smem, mail1, mail2, rows);
       __syncwarp();
       if (lane == 0) mbar_arrive(bars + (p.nstage + st) * 8);
+      if (w.kind == 1 && w.slot < head_k) head_item_done(p, L, cta, lane, mail1, head_k, epoch, misc + 2);
     } else {
       const Work wc = wn;
       cur = nxt_it;
@@ -778,6 +841,7 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
       }
       process_work<false>(p, wc, lane, cur, nullptr, smem, mail1, mail2, rows);
       __syncwarp();
+      if (wc.kind == 1 && wc.slot < head_k) head_item_done(p, L, cta, lane, mail1, head_k, epoch, misc + 2);
     }
   }
   csync();
@@ -794,12 +858,14 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
 }  // namespace
 
 // Workspace: 256 bytes of control words (grid barrier arrivals at 0 and generation at 128, zero-filled
-// before the first call; the barrier leaves the arrivals at zero), then h [R][I] fp32 and the
-// split-block partial sums [2][R][2][I] fp32.
+// before the first call; the barrier leaves the arrivals at zero), kMaxGrid hand-off flags (hold past
+// generations, never reset), then h [R][I] fp32 and the split-block tail partials [R][2][I] fp32.
+constexpr int kMaxGrid = 1024;
 size_t layer_workspace_bytes(int M, int H, int I, int top_k) {
   (void)H;
-  if (M <= 0 || I <= 0 || top_k <= 0) return 256;
-  return 256 + (size_t)M * top_k * 5 * (size_t)I * 4;
+  const size_t head = 256 + (size_t)kMaxGrid * 4;
+  if (M <= 0 || I <= 0 || top_k <= 0) return head;
+  return head + (size_t)M * top_k * 3 * (size_t)I * 4;
 }
 
 namespace {
@@ -934,11 +1000,13 @@ int launch_fused(const LayerArgs& a, int M, const void* x, const int32_t* ids, c
   p.off_mail1 = base + sp.tabs;
   p.off_mail2 = p.off_mail1 + sp.mail1;
   p.off_rows = p.off_mail2 + sp.mail2;
-  p.off_split = p.off_rows + sp.rows;
+  p.off_hstage = p.off_rows + sp.rows;
+  p.off_misc = p.off_hstage + sp.hstage;
   unsigned* ctl = static_cast<unsigned*>(a.workspace);
   p.bar_count = ctl;
   p.bar_gen = ctl + 32;
-  p.hfin = reinterpret_cast<float*>(static_cast<char*>(a.workspace) + 256);
+  p.hflags = ctl + 64;
+  p.hfin = reinterpret_cast<float*>(static_cast<char*>(a.workspace) + 256 + (size_t)kMaxGrid * 4);
   p.hpart = p.hfin + (size_t)g.R * a.I;
 
   auto kern = tma ? fused_layer_kernel<true> : fused_layer_kernel<false>;
@@ -972,7 +1040,7 @@ int decode_layer_fused(const LayerArgs& a) {
   if (dev != cached_dev) {
     int sms = 0;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return kErrDevice;
-    cached_cap = sms;              // one CTA per SM
+    cached_cap = sms < kMaxGrid ? sms : kMaxGrid;   // one CTA per SM
     cached_dev = dev;
   }
   // tokens per launch: as many as the shared-memory plan allows (copy-engine mode also keeps a ring of

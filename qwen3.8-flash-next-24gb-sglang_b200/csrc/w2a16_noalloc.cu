@@ -17,7 +17,7 @@
 
 namespace {
 
-// Zero-initialised at module load. The layer kernels need their control words zero on entry and leave
+// Zero-initialised at module load. The layer kernels need their barrier words zero on entry and leave
 // them zero on exit; the rest of the array (the SiLU*mul activations) is overwritten by every call.
 __device__ __align__(256) unsigned char g_noalloc_scratch[W2A16_NOALLOC_SCRATCH_BYTES];
 
