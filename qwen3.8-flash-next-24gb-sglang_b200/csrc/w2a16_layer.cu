@@ -541,32 +541,32 @@ __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* ptr) {
   return v;
 }
 
-// All CTAs arrive; thread 0 of each CTA calls this. The arrival count and the generation word sit on
-// different 128-byte lines, so the pollers of the generation never queue the arrivals' atomics. Gives
-// up after kSpinLimit polls (error bit 1).
-__device__ void grid_barrier(unsigned* count, unsigned* gen, unsigned ncta, unsigned* err) {
-  const unsigned g0 = ld_acquire_u32(gen);
-  __threadfence();
-  if (atomicAdd(count, 1u) == ncta - 1) {
-    *count = 0u;
-    __threadfence();
-    atomicAdd(gen, 1u);
-  } else {
-    unsigned it = 0;
-    while (ld_acquire_u32(gen) == g0) {
-      if (++it > kSpinLimit) {
-        flag_error(err, 2u);
-        break;
-      }
-      __nanosleep(64);
-    }
-  }
-  __threadfence();
-}
-
 __device__ __forceinline__ void st_release_u32(unsigned* ptr, unsigned v) {
   asm volatile("st.release.gpu.global.u32 [%0], %1;\n" ::"l"(ptr), "r"(v) : "memory");
 }
+
+// All CTAs arrive; thread 0 of each CTA calls this with `base`, the generation word it read at kernel
+// entry. The arrival count only grows, and the generation word holds the count every completed call
+// reached, so an arrival is one fire-and-forget release add and every CTA waits until the count reaches
+// base + ncta (signed distance, so the words may wrap). CTA 0 then stores that value as the new
+// generation, which the next call reads at entry; no CTA of this call reads it after its own entry, and
+// the grid size may differ from call to call. The count sits 128 bytes away from the generation. Gives
+// up after kSpinLimit polls (error bit 1).
+__device__ void grid_barrier(unsigned* count, unsigned* gen, unsigned base, unsigned ncta, unsigned* err) {
+  __threadfence();
+  asm volatile("red.release.gpu.global.add.u32 [%0], 1;\n" ::"l"(count) : "memory");
+  const unsigned target = base + ncta;
+  unsigned it = 0;
+  while ((int)(ld_acquire_u32(count) - target) < 0) {
+    if (++it > kSpinLimit) {
+      flag_error(err, 2u);
+      break;
+    }
+  }
+  if (blockIdx.x == 0) st_release_u32(gen, target);
+  __threadfence();
+}
+
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, unsigned bytes, uint32_t bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(dst),
                "l"(src), "r"(bytes), "r"(bar)
@@ -655,7 +655,7 @@ __device__ __forceinline__ void phase_switch(const FusedParams& p, int cta, int 
     }
   }
   csync();
-  if (threadIdx.x == 0) grid_barrier(p.bar_count, p.bar_gen, gridDim.x, p.err);
+  if (threadIdx.x == 0) grid_barrier(p.bar_count, p.bar_gen, epoch - 1u, gridDim.x, p.err);
   csync();
 
   // (3) h rows of the down units -> shared memory (row slot q * top_k + jr), then the tables
@@ -776,7 +776,7 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
     mbar_init(hbar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     misc[2] = 0u;
-    misc[3] = ld_acquire_u32(p.bar_gen);                     // no CTA passes this call's barrier before all read it
+    misc[3] = ld_acquire_u32(p.bar_gen);  // read by every CTA before any passes this call's barrier
   }
   __syncthreads();
   if (kTma && warp >= kWarps) {
@@ -857,9 +857,10 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
 
 }  // namespace
 
-// Workspace: 256 bytes of control words (grid barrier arrivals at 0 and generation at 128, zero-filled
-// before the first call; the barrier leaves the arrivals at zero), kMaxGrid hand-off flags (hold past
-// generations, never reset), then h [R][I] fp32 and the split-block tail partials [R][2][I] fp32.
+// Workspace: 256 bytes of control words (grid barrier arrival count at 0 and generation at 128; both
+// only grow and are equal between calls, so zero-filling before the first call is all they need),
+// kMaxGrid hand-off flags (hold past generations + 1, never reset), then h [R][I] fp32 and the
+// split-block tail partials [R][2][I] fp32.
 constexpr int kMaxGrid = 1024;
 size_t layer_workspace_bytes(int M, int H, int I, int top_k) {
   (void)H;
