@@ -151,10 +151,9 @@ __device__ __forceinline__ void prep_groups(const float (&v)[NG][4], const int (
 #pragma unroll
   for (int j = 0; j < NG; ++j)
     mx[j] = fmaxf(fmaxf(fabsf(v[j][0]), fabsf(v[j][1])), fmaxf(fabsf(v[j][2]), fabsf(v[j][3])));
+  // |x| of a non-negative float orders like its bit pattern: one integer max reduction per group
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-    for (int j = 0; j < NG; ++j) mx[j] = fmaxf(mx[j], __shfl_xor_sync(0xffffffffu, mx[j], o));
+  for (int j = 0; j < NG; ++j) mx[j] = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(mx[j])));
   int e[NG], s[NG], q[NG][4];
 #pragma unroll
   for (int j = 0; j < NG; ++j) {
@@ -181,9 +180,7 @@ __device__ __forceinline__ void prep_groups(const float (&v)[NG][4], const int (
     }
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-    for (int j = 0; j < NG; ++j) s[j] += __shfl_xor_sync(0xffffffffu, s[j], o);
+  for (int j = 0; j < NG; ++j) s[j] = __reduce_add_sync(0xffffffffu, s[j]);
   if (lane == 0) {
 #pragma unroll
     for (int j = 0; j < NG; ++j)
