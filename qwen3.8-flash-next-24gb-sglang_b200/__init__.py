@@ -19,3 +19,4 @@ from .expert_gemv import (moe_gemv_int2_tab, make_tables, make_zero_table, to_wo
 from .moe_layer import ExpertArena, moe_decode_layer, apply_gemv  # noqa: F401
 from .int8_gemv import int8_gemv  # noqa: F401
 from . import synth  # noqa: F401
+from . import expert_parallel  # noqa: F401
