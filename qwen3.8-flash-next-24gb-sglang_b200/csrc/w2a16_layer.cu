@@ -81,7 +81,7 @@ __host__ __device__ __forceinline__ size_t token_table_bytes(int K) {
 }
 
 struct SmemPlan {
-  size_t tabs, mail1, mail2, rows, hstage, misc, total;
+  size_t tabs, mail1, mail2, rows, hstage, misc, live, itab, total;
 };
 
 // Per routed row, resolved once per CTA: expert code / scale / zero-point bases of gate_up and down.
@@ -103,7 +103,9 @@ SmemPlan smem_plan(const Geo& g) {
   s.rows = ((size_t)g.R * sizeof(RowPtr) + 15) & ~size_t(15);
   s.hstage = (size_t)g.max_units * g.top_k * g.I * 4;           // h rows of the down units (bulk copies)
   s.misc = 64;                                                  // mbarrier, head counter, generation
-  s.total = s.tabs + s.mail1 + s.mail2 + s.rows + s.hstage + s.misc;
+  s.live = ((size_t)(2 * g.R + g.M + g.max_units * g.top_k) * 4 + 15) & ~size_t(15);   // LiveRows arrays
+  s.itab = (size_t)(g.max_range + g.max_units * g.s2) * 16;     // the CTA's item descriptors (producers)
+  s.total = s.tabs + s.mail1 + s.mail2 + s.rows + s.hstage + s.misc + s.live + s.itab;
   return s;
 }
 
@@ -121,7 +123,7 @@ struct FusedParams {
   float rsf;
   __nv_bfloat16* y;
   Geo geo;
-  size_t off_tabs, off_mail1, off_mail2, off_rows, off_hstage, off_misc;
+  size_t off_tabs, off_mail1, off_mail2, off_rows, off_hstage, off_misc, off_live, off_itab;
   unsigned* bar_count;   // grid barrier: arrivals (zero between calls)
   unsigned* bar_gen;     // grid barrier: generation, 128 bytes further
   float* hfin;           // [R][I] h of h-blocks computed wholly inside one CTA
@@ -150,10 +152,26 @@ struct Work {
   int unit;   // phase 2: unit slot within the CTA
   int jr;     // phase 2: row index within the token
   int seq;    // position in the CTA's item order (copy-engine ring)
+  int dead;   // phase 2: slot past the token's live rows (reduces nothing, writes a zero partial)
+};
+
+// Routed rows whose expert resolves (slot >= 0), compacted identically by every CTA in its prologue.
+// Phase-1 items and ranges run over the live rows only, so masked rows (experts not resident, or owned
+// by another GPU) cost nothing and do not unbalance the CTAs; phase-2 items of a token take its live
+// rows first and the remaining (dead) item slots of its units write zero partials.
+struct LiveRows {
+  const int* rowmap;   // [R] compact phase-1 row -> routed row
+  const int* tokrow;   // [M][top_k] j-th live row of token m, as an index within the token's top_k
+  const int* tokcnt;   // [M] live rows per token
+  const int* slotrow;  // [max_units][top_k] routed row of each h staging slot of this CTA, -1 = dead
+  int live_slots;      // staging slots holding a live row (h rows this CTA copies)
+  int n1;              // phase-1 items over the live rows
+  int grid1;           // CTAs holding phase-1 items (each range at least one h-block)
 };
 
 struct WarpList {
   int a;      // CTA's phase-1 range start
+  int b;      // CTA's phase-1 range end
   int range;  // CTA's phase-1 items
   int n1w;    // phase-1 items of this warp
   int nu;     // phase-2 units of this CTA
@@ -161,10 +179,12 @@ struct WarpList {
   __device__ int total() const { return n1w + nu * n2w; }
 };
 
-__device__ __forceinline__ WarpList warp_list(const Geo& g, int cta, int warp) {
+__device__ __forceinline__ WarpList warp_list(const Geo& g, const LiveRows& lv, int cta, int warp) {
   WarpList L;
-  const long long a = (long long)cta * g.n1 / g.grid, b = (long long)(cta + 1) * g.n1 / g.grid;
+  const long long a = cta < lv.grid1 ? (long long)cta * lv.n1 / lv.grid1 : lv.n1;
+  const long long b = cta < lv.grid1 ? (long long)(cta + 1) * lv.n1 / lv.grid1 : lv.n1;
   L.a = (int)a;
+  L.b = (int)b;
   const int range = (int)(b - a);
   L.range = range;
   L.n1w = range > warp ? (range - warp + kWarps - 1) / kWarps : 0;
@@ -173,14 +193,24 @@ __device__ __forceinline__ WarpList warp_list(const Geo& g, int cta, int warp) {
   return L;
 }
 
-__device__ __forceinline__ Work work_at(const Geo& g, const WarpList& L, int cta, int warp, int t) {
+// Phase-2 item j of unit (token m, block b) -> its live row (or a dead slot).
+__device__ __forceinline__ void unit_row(const Geo& g, const LiveRows& lv, int m, int j, Work& w) {
+  w.jr = j / g.kp2;
+  w.kp = j - w.jr * g.kp2;
+  w.dead = w.jr >= lv.tokcnt[m];
+  w.r = m * g.top_k + (w.dead ? w.jr : lv.tokrow[m * g.top_k + w.jr]);
+}
+
+__device__ __forceinline__ Work work_at(const Geo& g, const LiveRows& lv, const WarpList& L, int cta, int warp,
+                                        int t) {
   Work w{};
   if (t < L.n1w) {
     const int i = L.a + warp + kWarps * t;
     const int per_row = g.nb1 * g.kp1;
     w.kind = 1;
-    w.r = i / per_row;
-    const int rem = i - w.r * per_row;
+    const int rc = i / per_row;
+    w.r = lv.rowmap[rc];
+    const int rem = i - rc * per_row;
     w.b = rem / g.kp1;
     w.kp = rem - w.b * g.kp1;
     w.slot = i - L.a;
@@ -194,9 +224,7 @@ __device__ __forceinline__ Work work_at(const Geo& g, const WarpList& L, int cta
   const int m = u / g.nb2;
   w.kind = 2;
   w.b = u - m * g.nb2;
-  w.jr = j / g.kp2;
-  w.kp = j - w.jr * g.kp2;
-  w.r = m * g.top_k + w.jr;
+  unit_row(g, lv, m, j, w);
   w.unit = q;
   w.slot = q * g.s2 + j;
   w.seq = L.range + q * g.s2 + j;
@@ -220,7 +248,7 @@ __device__ __forceinline__ LaneMap lane_map(const Geo& g, const Work& w, int lan
   const int q8 = k1 ? (q & 7) : q;
   lm.col = (k1 && q >= 8 ? g.I : 0) + w.b * 32 + q8 * 4;
   lm.gl = k1 ? w.kp * 2 + gi : w.kp * 4 + gi;
-  lm.valid = rows[w.r].ok[w.kind - 1] && lm.gl < (k1 ? g.G1 : g.G2);
+  lm.valid = !w.dead && rows[w.r].ok[w.kind - 1] && lm.gl < (k1 ? g.G1 : g.G2);
   return lm;
 }
 
@@ -376,14 +404,15 @@ __device__ __forceinline__ void wait_tag(const int* tags, int st, int seq, unsig
 }
 
 // Item i of the CTA's order: its phase-1 range first, then (unit, item within unit) of phase 2.
-__device__ __forceinline__ Work cta_item(const Geo& g, const WarpList& L, int cta, int i) {
+__device__ __forceinline__ Work cta_item(const Geo& g, const LiveRows& lv, const WarpList& L, int cta, int i) {
   Work w{};
   if (i < L.range) {
     const int ii = L.a + i;
     const int per_row = g.nb1 * g.kp1;
     w.kind = 1;
-    w.r = ii / per_row;
-    const int rem = ii - w.r * per_row;
+    const int rc = ii / per_row;
+    w.r = lv.rowmap[rc];
+    const int rem = ii - rc * per_row;
     w.b = rem / g.kp1;
     w.kp = rem - w.b * g.kp1;
     return w;
@@ -393,9 +422,7 @@ __device__ __forceinline__ Work cta_item(const Geo& g, const WarpList& L, int ct
   const int u = cta + g.grid * q, m = u / g.nb2;
   w.kind = 2;
   w.b = u - m * g.nb2;
-  w.jr = j / g.kp2;
-  w.kp = j - w.jr * g.kp2;
-  w.r = m * g.top_k + w.jr;
+  unit_row(g, lv, m, j, w);
   return w;
 }
 
@@ -406,39 +433,41 @@ __device__ __forceinline__ Work cta_item(const Geo& g, const WarpList& L, int ct
 // codes (4 KB), one of scales and one of zero-point windows, completing on the stage's `full` barrier; a
 // stage is refilled once the warp that reduced it arrived on its `empty` barrier. Items of a
 // non-resident expert complete their phase on the arrival alone.
-__device__ void produce(const FusedParams& p, const WarpList& L, int cta, const RowPtr* rows, unsigned char* stages,
-                        uint32_t bars, int* tags, int pr) {
-  const Geo& g = p.geo;
+__device__ void produce(const FusedParams& p, int n, const int4* itab, unsigned char* stages, uint32_t bars, int* tags,
+                        int pr) {
   const int ns = p.nstage;
-  const int n = L.range + L.nu * g.s2;
   const bool hz = p.map13.has_zeros != 0;
   const bool aligned = (smem_u32(stages) & 127u) == 0;        // tensor copies land on 128-byte boundaries
   if (!aligned) flag_error(p.err, 4u);
+  int st = pr, round = 0;                                     // st = i % ns, round = i / ns
   for (int i = pr; i < n; i += kProducers) {
-    const int st = i % ns;
     const uint32_t full = bars + st * 8, empty = bars + (ns + st) * 8;
-    if (i >= ns) mbar_wait(empty, (unsigned)(i / ns - 1) & 1u, p.err);
+    if (round > 0) mbar_wait(empty, (unsigned)(round - 1) & 1u, p.err);
     // Tag the stage with the item it now holds. A warp waits for its item's tag before it waits on the
     // stage's `full` phase: a stage is refilled by another warp's item, and without the tag a warp that
     // runs ahead could take the still-pending previous fill's phase parity for its own.
     st_volatile_shared(tags + st, i);
-    const Work w = cta_item(g, L, cta, i);
-    const RowPtr& rp = rows[w.r];
-    if (!aligned || !rp.ok[w.kind - 1] || rp.slot < 0 || rp.slot >= kSlotExtent) {
+    const int4 it = itab[i];                                  // {kind (0 = nothing to copy), slot, b, kp}
+    if (!aligned || it.x == 0) {
       mbar_arrive(full);
-      continue;
-    }
-    const uint32_t dst = smem_u32(stages + (size_t)st * kStageBytes);
-    mbar_arrive_tx(full, (unsigned)(kScaleOff + 256 + (hz ? 64 : 0)));
-    const int zx = (8 * w.b) & ~15;                          // 16-byte aligned zero-point window
-    if (w.kind == 1) {
-      tma_load_4d(dst, &p.tm[0], w.b * 32, 0, 16 * w.kp, rp.slot, full);
-      tma_load_4d(dst + kScaleOff, &p.tm[1], w.b * 32, 0, 2 * w.kp, rp.slot, full);
-      if (hz) tma_load_4d(dst + kZeroOff, &p.tm[2], zx, 0, 2 * w.kp, rp.slot, full);
     } else {
-      tma_load_3d(dst, &p.tm[3], w.b * 32, 32 * w.kp, rp.slot, full);
-      tma_load_3d(dst + kScaleOff, &p.tm[4], w.b * 32, 4 * w.kp, rp.slot, full);
-      if (hz) tma_load_3d(dst + kZeroOff, &p.tm[5], zx, 4 * w.kp, rp.slot, full);
+      const uint32_t dst = smem_u32(stages + (size_t)st * kStageBytes);
+      mbar_arrive_tx(full, (unsigned)(kScaleOff + 256 + (hz ? 64 : 0)));
+      const int zx = (8 * it.z) & ~15;                        // 16-byte aligned zero-point window
+      if (it.x == 1) {
+        tma_load_4d(dst, &p.tm[0], it.z * 32, 0, 16 * it.w, it.y, full);
+        tma_load_4d(dst + kScaleOff, &p.tm[1], it.z * 32, 0, 2 * it.w, it.y, full);
+        if (hz) tma_load_4d(dst + kZeroOff, &p.tm[2], zx, 0, 2 * it.w, it.y, full);
+      } else {
+        tma_load_3d(dst, &p.tm[3], it.z * 32, 32 * it.w, it.y, full);
+        tma_load_3d(dst + kScaleOff, &p.tm[4], it.z * 32, 4 * it.w, it.y, full);
+        if (hz) tma_load_3d(dst + kZeroOff, &p.tm[5], zx, 4 * it.w, it.y, full);
+      }
+    }
+    st += kProducers;
+    if (st >= ns) {
+      st -= ns;
+      ++round;
     }
   }
   // every copy has landed before the producer leaves (the reducing warps wait on the same phases)
@@ -577,11 +606,12 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, unsigned
 // they are reduced (round 0 of the item loop), the warp that completes them sums their partials and
 // publishes the (gate, up) tail sums with a flag, so the previous CTA can finish that block before the
 // grid barrier.
-__device__ void publish_head(const FusedParams& p, const WarpList& L, int cta, int lane, const float* mail1, int head_k,
-                             unsigned epoch) {
+__device__ void publish_head(const FusedParams& p, const LiveRows& lv, const WarpList& L, int cta, int lane,
+                             const float* mail1, int head_k, unsigned epoch) {
   const Geo& g = p.geo;
   const int blk = L.a / g.kp1;
-  const int r = blk / g.nb1, hb = blk - r * g.nb1;
+  const int rc = blk / g.nb1, hb = blk - rc * g.nb1;
+  const int r = lv.rowmap[rc];
   const size_t col = (size_t)hb * 32 + lane;
   __syncwarp();                                               // lane 0's acquire of the count covers the warp
   float gs = 0.f, us = 0.f;
@@ -597,15 +627,16 @@ __device__ void publish_head(const FusedParams& p, const WarpList& L, int cta, i
 }
 
 // Count one reduced head item; the warp that reduces the last of them publishes the tail sums.
-__device__ __forceinline__ void head_item_done(const FusedParams& p, const WarpList& L, int cta, int lane,
-                                               const float* mail1, int head_k, unsigned epoch, unsigned* counter) {
+__device__ __forceinline__ void head_item_done(const FusedParams& p, const LiveRows& lv, const WarpList& L, int cta,
+                                               int lane, const float* mail1, int head_k, unsigned epoch,
+                                               unsigned* counter) {
   unsigned last = 0u;
   if (lane == 0) {
     __threadfence_block();
     last = atomicAdd(counter, 1u) == (unsigned)head_k - 1u;
     __threadfence_block();
   }
-  if (__shfl_sync(0xffffffffu, last, 0)) publish_head(p, L, cta, lane, mail1, head_k, epoch);
+  if (__shfl_sync(0xffffffffu, last, 0)) publish_head(p, lv, L, cta, lane, mail1, head_k, epoch);
 }
 
 // Phase switch, entered by every warp of the CTA once its gate_up items are done. (1) h of every h-block
@@ -614,13 +645,13 @@ __device__ __forceinline__ void head_item_done(const FusedParams& p, const WarpL
 // shares with the previous CTA is finished there. (2) Grid barrier: h is complete. (3) One bulk copy per
 // h row of this CTA's down units into shared memory, then every warp converts its groups from there.
 template <int kHB>
-__device__ __forceinline__ void phase_switch(const FusedParams& p, int cta, int warp, int lane, unsigned char* smem,
-                                             const float* mail1, unsigned epoch, uint32_t hbar) {
+__device__ __forceinline__ void phase_switch(const FusedParams& p, const LiveRows& lv, int cta, int warp, int lane,
+                                             unsigned char* smem, const float* mail1, unsigned epoch, uint32_t hbar) {
   const Geo& g = p.geo;
-  const WarpList L = warp_list(g, cta, warp);
+  const WarpList L = warp_list(g, lv, cta, warp);
   csync();
   {
-    const long long a = L.a, b = (long long)(cta + 1) * g.n1 / g.grid;
+    const long long a = L.a, b = L.b;
     if (b > a) {
       const int blk0 = (int)(a / g.kp1), blk1 = (int)((b - 1) / g.kp1);
       for (int blk = blk0 + warp; blk <= blk1; blk += kWarps) {
@@ -632,7 +663,8 @@ __device__ __forceinline__ void phase_switch(const FusedParams& p, int cta, int 
           gs += mail1[(size_t)(i - a) * 64 + lane];
           us += mail1[(size_t)(i - a) * 64 + 32 + lane];
         }
-        const int r = blk / g.nb1, hb = blk - r * g.nb1;
+        const int rc = blk / g.nb1, hb = blk - rc * g.nb1;
+        const int r = lv.rowmap[rc];
         const size_t col = (size_t)hb * 32 + lane;
         if (i1 > b) {                                         // tail published by the next CTA
           if (lane == 0) {
@@ -658,16 +690,15 @@ __device__ __forceinline__ void phase_switch(const FusedParams& p, int cta, int 
   if (threadIdx.x == 0) grid_barrier(p.bar_count, p.bar_gen, epoch - 1u, gridDim.x, p.err);
   csync();
 
-  // (3) h rows of the down units -> shared memory (row slot q * top_k + jr), then the tables
+  // (3) h rows of the down units' live rows -> shared memory (row slot q * top_k + jr), then the tables
   float* hst = reinterpret_cast<float*>(smem + p.off_hstage);
   const int nrows = L.nu * g.top_k;
   const unsigned row_bytes = (unsigned)g.I * 4u;
-  if (threadIdx.x == 0) mbar_arrive_tx(hbar, row_bytes * (unsigned)nrows);
-  if (threadIdx.x < nrows) {
-    const int q = threadIdx.x / g.top_k, jr = threadIdx.x - q * g.top_k;
-    const int m = (cta + g.grid * q) / g.nb2;
+  if (threadIdx.x == 0) mbar_arrive_tx(hbar, row_bytes * (unsigned)lv.live_slots);
+  if (threadIdx.x < nrows && lv.slotrow[threadIdx.x] >= 0) {
     asm volatile("fence.proxy.async.global;\n" ::: "memory");  // h was written through the generic proxy
-    bulk_g2s(smem_u32(hst + (size_t)threadIdx.x * g.I), p.hfin + (size_t)(m * g.top_k + jr) * g.I, row_bytes, hbar);
+    bulk_g2s(smem_u32(hst + (size_t)threadIdx.x * g.I), p.hfin + (size_t)lv.slotrow[threadIdx.x] * g.I, row_bytes,
+             hbar);
   }
   if (threadIdx.x == 0) mbar_wait(hbar, 0u, p.err);
   csync();
@@ -683,8 +714,8 @@ __device__ __forceinline__ void phase_switch(const FusedParams& p, int cta, int 
       hv[j][0] = hv[j][1] = hv[j][2] = hv[j][3] = 0.f;
       gl[j] = -1;
       toff[j] = 0;
-      if (k < ntab) {
-        const int row = k / g.G2, gg = k - row * g.G2;         // row slot = q * top_k + jr
+      const int row = k / g.G2, gg = k - row * g.G2;           // row slot = q * top_k + jr
+      if (k < ntab && lv.slotrow[row] >= 0) {
         const float4 h4 = *reinterpret_cast<const float4*>(hst + (size_t)row * g.I + gg * kGroup + 4 * lane);
         hv[j][0] = h4.x; hv[j][1] = h4.y; hv[j][2] = h4.z; hv[j][3] = h4.w;
         gl[j] = gg;
@@ -714,6 +745,8 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
   const uint32_t bars = kTma ? smem_u32(smem + p.off_bars) : 0u;
   int* tags = kTma ? reinterpret_cast<int*>(smem + p.off_bars + 16 * (size_t)p.nstage) : nullptr;
 
+  // the barrier generation of this call, loaded first (its latency overlaps the prologue)
+  const unsigned gen_entry = threadIdx.x == 0 ? ld_acquire_u32(p.bar_gen) : 0u;
   if (!kTma) {
     // Start the whole layer's weight stream: this CTA's 1/grid share of every routed row's six arrays.
     // A prefetch is only a hint, so arrays whose base is not 16-byte aligned are left to the loads.
@@ -742,8 +775,6 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
     if (threadIdx.x < p.nstage) tags[threadIdx.x] = -1;
   }
 
-  const WarpList L = warp_list(g, cta, warp < kWarps ? warp : 0);
-  const int total = L.total();
   const int nxt = g.M * g.G1;
 
   // activation values of this warp's first table groups
@@ -772,21 +803,67 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
     if (kTma && rp.slot >= kSlotExtent) flag_error(p.err, 1u);
     rows[r] = rp;
   }
+  int* rowmap = reinterpret_cast<int*>(smem + p.off_live);
+  int* tokrow = rowmap + g.R;
+  int* tokcnt = tokrow + g.R;
+  int* slotrow = tokcnt + g.M;
+  __syncthreads();
   if (threadIdx.x == 0) {
     mbar_init(hbar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     misc[2] = 0u;
-    misc[3] = ld_acquire_u32(p.bar_gen);  // read by every CTA before any passes this call's barrier
+    misc[3] = gen_entry;                   // read by every CTA before any passes this call's barrier
+    int nl = 0;                            // live rows, token by token, in routing order
+    for (int m = 0; m < g.M; ++m) {
+      int c = 0;
+      for (int j = 0; j < g.top_k; ++j) {
+        const int r = m * g.top_k + j;
+        if (rows[r].ok[0] && rows[r].ok[1]) {
+          tokrow[m * g.top_k + c++] = j;
+          rowmap[nl++] = r;
+        }
+      }
+      tokcnt[m] = c;
+    }
+    const int nblk = nl * g.nb1;
+    misc[4] = (unsigned)(nblk * g.kp1);
+    misc[5] = (unsigned)max(1, min((int)gridDim.x, nblk));
+    int ls = 0;                            // h staging slots of this CTA's down units
+    for (int q = 0; q < g.max_units; ++q) {
+      const int u = cta + g.grid * q, m = u / g.nb2;
+      for (int jr = 0; jr < g.top_k; ++jr) {
+        const bool on = u < g.u2 && jr < tokcnt[m];
+        slotrow[q * g.top_k + jr] = on ? m * g.top_k + tokrow[m * g.top_k + jr] : -1;
+        ls += on;
+      }
+    }
+    misc[6] = (unsigned)ls;
   }
   __syncthreads();
-  if (kTma && warp >= kWarps) {
-    if (lane == 0) produce(p, warp_list(g, cta, 0), cta, rows, stages, bars, tags, warp - kWarps);
-    return;
+  const LiveRows lv{rowmap, tokrow, tokcnt, slotrow, (int)misc[6], (int)misc[4], (int)misc[5]};
+  const WarpList L = warp_list(g, lv, cta, warp < kWarps ? warp : 0);
+  const int total = L.total();
+  if (kTma) {
+    // descriptors of the CTA's items in ring order, built once in parallel for the producers
+    const WarpList L0 = warp_list(g, lv, cta, 0);
+    const int n_items = L0.range + L0.nu * g.s2;
+    int4* itab = reinterpret_cast<int4*>(smem + p.off_itab);
+    for (int i = threadIdx.x; i < n_items; i += blockDim.x) {
+      const Work w = cta_item(g, lv, L0, cta, i);
+      const RowPtr& rp = rows[w.r];
+      const bool live = !w.dead && rp.ok[w.kind - 1] && rp.slot >= 0 && rp.slot < kSlotExtent;
+      itab[i] = make_int4(live ? w.kind : 0, rp.slot, w.b, w.kp);
+    }
+    __syncthreads();
+    if (warp >= kWarps) {
+      if (lane == 0) produce(p, n_items, itab, stages, bars, tags, warp - kWarps);
+      return;
+    }
   }
 
   // register mode: this warp's first item in flight while the activation tables are built
   ItemRegs cur, nxt_it;
-  Work wn = work_at(g, L, cta, warp, 0);
+  Work wn = work_at(g, lv, L, cta, warp, 0);
   if (!kTma) load_item(p, wn, lane, rows, nxt_it);
   {
     int gl[kXPre], toff[kXPre];
@@ -816,12 +893,12 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
   bool p1done = false;
   for (int t = 0;; ++t) {
     if (t == L.n1w && !p1done) {
-      phase_switch<kTma ? 6 : 2>(p, cta, warp, lane, smem, mail1, epoch, hbar);
+      phase_switch<kTma ? 6 : 2>(p, lv, cta, warp, lane, smem, mail1, epoch, hbar);
       p1done = true;
     }
     if (t >= total) break;
     if (kTma) {
-      const Work w = work_at(g, L, cta, warp, t);
+      const Work w = work_at(g, lv, L, cta, warp, t);
       const int st = w.seq % p.nstage;
       if (lane == 0) {
         wait_tag(tags, st, w.seq, p.err);
@@ -831,17 +908,17 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
       process_work<true>(p, w, lane, cur, stages + (size_t)st * kStageBytes, smem, mail1, mail2, rows);
       __syncwarp();
       if (lane == 0) mbar_arrive(bars + (p.nstage + st) * 8);
-      if (w.kind == 1 && w.slot < head_k) head_item_done(p, L, cta, lane, mail1, head_k, epoch, misc + 2);
+      if (w.kind == 1 && w.slot < head_k) head_item_done(p, lv, L, cta, lane, mail1, head_k, epoch, misc + 2);
     } else {
       const Work wc = wn;
       cur = nxt_it;
       if (t + 1 < total) {
-        wn = work_at(g, L, cta, warp, t + 1);
+        wn = work_at(g, lv, L, cta, warp, t + 1);
         load_item(p, wn, lane, rows, nxt_it);
       }
       process_work<false>(p, wc, lane, cur, nullptr, smem, mail1, mail2, rows);
       __syncwarp();
-      if (wc.kind == 1 && wc.slot < head_k) head_item_done(p, L, cta, lane, mail1, head_k, epoch, misc + 2);
+      if (wc.kind == 1 && wc.slot < head_k) head_item_done(p, lv, L, cta, lane, mail1, head_k, epoch, misc + 2);
     }
   }
   csync();
@@ -1003,6 +1080,8 @@ int launch_fused(const LayerArgs& a, int M, const void* x, const int32_t* ids, c
   p.off_rows = p.off_mail2 + sp.mail2;
   p.off_hstage = p.off_rows + sp.rows;
   p.off_misc = p.off_hstage + sp.hstage;
+  p.off_live = p.off_misc + sp.misc;
+  p.off_itab = p.off_live + sp.live;
   unsigned* ctl = static_cast<unsigned*>(a.workspace);
   p.bar_count = ctl;
   p.bar_gen = ctl + 32;
