@@ -56,6 +56,22 @@ def test_config3_m4(pkg, dev):
     assert O.max_rel_err(y.float().cpu(), oracle_layer(arena, x, ids, w)) < TOL
 
 
+@pytest.mark.parametrize("M", [16, 64])
+def test_config3_batched_tokens(pkg, dev, M):
+    """Config 3, M=16 and M=64 tokens at full size (uniform-random logits). The layer runs them in token
+    chunks through the same kernel; each token's output depends only on its own routing, so a spread of
+    tokens is checked against the oracle (dequantising 8 experts per checked token)."""
+    E, H, I, k = 256, 4096, 1536, 8
+    arena = pkg.synth.make_arena(E, H, I, seed=5, device=dev, gen_device=dev)
+    x = pkg.synth.make_activation(M, H, seed=5, device=dev, gen_device=dev)
+    ids, w = pkg.synth.route_softmax(M, E, k, seed=5, device=dev, gen_device=dev, uniform_logits=True)
+    y = pkg.moe_decode_layer(x, ids, w, arena)
+    torch.cuda.synchronize()
+    for m in sorted({0, 1, M // 2, M - 1}):
+        ref = oracle_layer(arena, x[m:m + 1], ids[m:m + 1], w[m:m + 1])
+        assert O.max_rel_err(y[m:m + 1].float().cpu(), ref) < TOL, m
+
+
 def test_config2_resident_slots_full_size(pkg, dev):
     """Config 2: S=184 of 256 experts resident at a random arena permutation, Zipf(1.1) routing,
     misses masked by slot -1. Properties: (a) oracle parity; (b) masking == zero routing weight,
