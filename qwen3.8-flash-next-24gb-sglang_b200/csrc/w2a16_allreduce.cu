@@ -1,0 +1,96 @@
+// One-shot all-reduce (sum) of a small bf16 vector across the GPUs of one node over NVLink peer memory,
+// for the expert-parallel decode step: every rank holds a partial MoE-layer output [M, H] (8 KB at M=1)
+// and needs the sum.
+//
+// Buffers: each rank owns a peer-visible buffer holding 2 parity slots x n_max bf16 and, at `flag_off`
+// bytes, `world` flag words (zero before the first call); every rank maps every other rank's buffer (the
+// caller passes a device array of the N peer addresses, e.g. from torch symmetric memory). Call e (a
+// per-rank device counter, identical on all ranks because every rank makes the same calls) uses slot e & 1:
+//   1. copy the local partial into this rank's slot;
+//   2. fence (system scope), then store e into flag[my_rank] of every peer (release);
+//   3. wait until this rank's own flags hold e from every peer (acquire, bounded);
+//   4. read slot e & 1 of all N buffers and sum them in rank order 0..N-1 in fp32 -> bf16 out (the same
+//      order on every rank, so every rank gets bit-identical sums).
+// A rank reaches step 2 of call e only after step 4 of call e-1, so once it has seen every peer's
+// call-e signal no peer still reads the slot that call e+1 will overwrite. Plain loads and stores to peer
+// memory only; no multicast.
+#include "w2a16_kernels.h"
+
+namespace w2a16 {
+namespace {
+
+constexpr unsigned kArSpinLimit = 1u << 22;
+constexpr int kArThreads = 512;
+
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+struct ArParams {
+  const __nv_bfloat16* in;
+  __nv_bfloat16* out;
+  int n, n_max, rank, world;
+  const uint64_t* bufs;   // [world] peer buffer addresses (bf16 [2][n_max], flags at flag_off)
+  size_t flag_off;
+  unsigned* epoch;        // this rank's call counter
+  unsigned* err;
+};
+
+__global__ void __launch_bounds__(kArThreads, 1) allreduce_kernel(ArParams p) {
+  __shared__ unsigned s_epoch;
+  if (threadIdx.x == 0) s_epoch = *p.epoch + 1u;
+  __syncthreads();
+  const unsigned e = s_epoch;
+  const size_t slot = (size_t)(e & 1u) * p.n_max;
+  __nv_bfloat16* mine = reinterpret_cast<__nv_bfloat16*>(p.bufs[p.rank]) + slot;
+  for (int i = threadIdx.x; i < p.n; i += blockDim.x) mine[i] = p.in[i];
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x < p.world) {
+    unsigned* peer_pad = reinterpret_cast<unsigned*>(p.bufs[threadIdx.x] + p.flag_off);
+    st_release_sys(peer_pad + p.rank, e);
+    const unsigned* own_pad = reinterpret_cast<const unsigned*>(p.bufs[p.rank] + p.flag_off);
+    unsigned it = 0;
+    while (ld_acquire_sys(own_pad + threadIdx.x) != e) {    // peer threadIdx.x's call-e data is in place
+      if (++it > kArSpinLimit) {
+        flag_error(p.err, 2u);
+        break;
+      }
+      __nanosleep(32);
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < p.n; i += blockDim.x) {
+    float acc = 0.f;
+    for (int r = 0; r < p.world; ++r) {
+      const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(p.bufs[r]) + slot;
+      acc += __bfloat162float(src[i]);
+    }
+    p.out[i] = __float2bfloat16(acc);
+  }
+  if (threadIdx.x == 0) *p.epoch = e;
+}
+
+}  // namespace
+
+int allreduce_peers_bf16(const void* in, void* out, int n, int n_max, const uint64_t* bufs, size_t flag_off, int rank,
+                         int world, unsigned* epoch, unsigned* err, cudaStream_t stream) {
+  if (n <= 0) return kOk;
+  if (!in || !out || !bufs || !epoch || world <= 0 || world > kArThreads || rank < 0 || rank >= world)
+    return kErrArg;
+  if (n > n_max || flag_off < (size_t)n_max * 4 || flag_off % 16) return kErrShape;
+  ArParams p{};
+  p.in = static_cast<const __nv_bfloat16*>(in);
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.n = n; p.n_max = n_max; p.rank = rank; p.world = world;
+  p.bufs = bufs; p.flag_off = flag_off; p.epoch = epoch; p.err = err;
+  allreduce_kernel<<<1, kArThreads, 0, stream>>>(p);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
+}
+
+}  // namespace w2a16

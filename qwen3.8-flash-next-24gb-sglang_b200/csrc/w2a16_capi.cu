@@ -137,6 +137,12 @@ int w2a16_gather_rows_tab(const int64_t* tab, const int32_t* ids, int n, void* o
 
 size_t w2a16_int8_workspace_bytes(int M, int K, int N) { return int8_workspace_bytes(M, K, N); }
 
+int w2a16_allreduce_peers_bf16(const void* in, void* out, int n, int n_max, const uint64_t* peer_bufs,
+                               size_t flag_offset, int rank, int world, unsigned int* epoch, unsigned int* err,
+                               void* stream) {
+  return allreduce_peers_bf16(in, out, n, n_max, peer_bufs, flag_offset, rank, world, epoch, err, as_stream(stream));
+}
+
 int w2a16_int8_gemv(const void* x, int64_t stride_xm, const int32_t* qweight, const void* scales, int group,
                     int zero, int M, int K, int N, void* y, int64_t stride_ym, void* workspace,
                     size_t workspace_bytes, void* stream) {

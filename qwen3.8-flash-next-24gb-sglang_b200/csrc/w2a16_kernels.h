@@ -44,6 +44,8 @@ struct LayerArgs {
 };
 size_t layer_workspace_bytes(int M, int H, int I, int top_k);
 int decode_layer_fused(const LayerArgs& a);
+int allreduce_peers_bf16(const void* in, void* out, int n, int n_max, const uint64_t* bufs, size_t flag_off, int rank,
+                         int world, unsigned* epoch, unsigned* err, cudaStream_t stream);
 
 // INT8 dense GEMV (w2a16_int8.cu).
 struct Int8Args {
