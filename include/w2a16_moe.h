@@ -199,10 +199,10 @@ size_t w2a16_int8_workspace_bytes(int M, int K, int N);
  * out[i] = sum over ranks r = 0..world-1 (in that order, fp32) of in_r[i], identical on every rank. Replaces
  * the per-layer NCCL all-reduce of the expert-parallel decode step (no counterpart in the reference, which
  * runs on one GPU). peer_bufs: device array of the `world` peer-visible buffer addresses (rank r's buffer
- * mapped into this process), each holding 2 x n_max bf16 and, at flag_offset bytes (>= 4 n_max, 16-byte
- * multiple), `world` uint32 flags that are zero before the first call. epoch: this rank's device call counter
- * (zero initially). Every rank must make the same sequence of calls; n <= n_max. A wait that gives up sets
- * bit 1 of `err`. */
+ * mapped into this process), each holding 2 x world x n_max bf16 and, at flag_offset bytes (>= 4 world n_max,
+ * 16-byte multiple), `world` uint32 flags that are zero before the first call. epoch: this rank's device call
+ * counter (zero initially). Every rank must make the same sequence of calls; n <= n_max, both multiples of 8,
+ * `in` 16-byte aligned. A wait that gives up sets bit 1 of `err`. */
 int w2a16_allreduce_peers_bf16(const void* in, void* out, int n, int n_max, const uint64_t* peer_bufs,
                                size_t flag_offset, int rank, int world, unsigned int* epoch, unsigned int* err,
                                void* stream);

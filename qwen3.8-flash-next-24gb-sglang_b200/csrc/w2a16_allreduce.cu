@@ -2,17 +2,19 @@
 // for the expert-parallel decode step: every rank holds a partial MoE-layer output [M, H] (8 KB at M=1)
 // and needs the sum.
 //
-// Buffers: each rank owns a peer-visible buffer holding 2 parity slots x n_max bf16 and, at `flag_off`
-// bytes, `world` flag words (zero before the first call); every rank maps every other rank's buffer (the
-// caller passes a device array of the N peer addresses, e.g. from torch symmetric memory). Call e (a
-// per-rank device counter, identical on all ranks because every rank makes the same calls) uses slot e & 1:
-//   1. copy the local partial into this rank's slot;
-//   2. fence (system scope), then store e into flag[my_rank] of every peer (release);
-//   3. wait until this rank's own flags hold e from every peer (acquire, bounded);
-//   4. read slot e & 1 of all N buffers and sum them in rank order 0..N-1 in fp32 -> bf16 out (the same
-//      order on every rank, so every rank gets bit-identical sums).
-// A rank reaches step 2 of call e only after step 4 of call e-1, so once it has seen every peer's
-// call-e signal no peer still reads the slot that call e+1 will overwrite. Plain loads and stores to peer
+// Buffers (push form): each rank owns a peer-visible buffer holding 2 parity slots x world x n_max bf16
+// (slot p, row r = rank r's partial) and, at `flag_off` bytes, `world` flag words (zero before the first
+// call); every rank maps every other rank's buffer (the caller passes a device array of the N peer addresses,
+// e.g. from torch symmetric memory). Call e (a per-rank device counter, identical on all ranks because every
+// rank makes the same calls) uses slot e & 1:
+//   1. write the local partial into row my_rank of slot e & 1 of EVERY rank's buffer (NVLink stores);
+//   2. one system-scope acq_rel fence after the CTA barrier, then store e into flag[my_rank] of every rank
+//      (release);
+//   3. wait until this rank's own flags hold e from every rank (acquire, bounded);
+//   4. sum the world rows of this rank's own slot in rank order 0..N-1 in fp32 -> bf16 out (local reads;
+//      the same order on every rank, so every rank gets bit-identical sums).
+// A rank writes call e's rows only after it saw every rank's call e-1 flag, which each rank raises only
+// after it finished reading call e-2's slot, the one call e overwrites. Plain loads and stores to peer
 // memory only; no multicast.
 #include "w2a16_kernels.h"
 
@@ -35,7 +37,7 @@ struct ArParams {
   const __nv_bfloat16* in;
   __nv_bfloat16* out;
   int n, n_max, rank, world;
-  const uint64_t* bufs;   // [world] peer buffer addresses (bf16 [2][n_max], flags at flag_off)
+  const uint64_t* bufs;   // [world] peer buffer addresses (bf16 [2][world][n_max], flags at flag_off)
   size_t flag_off;
   unsigned* epoch;        // this rank's call counter
   unsigned* err;
@@ -46,31 +48,34 @@ __global__ void __launch_bounds__(kArThreads, 1) allreduce_kernel(ArParams p) {
   if (threadIdx.x == 0) s_epoch = *p.epoch + 1u;
   __syncthreads();
   const unsigned e = s_epoch;
-  const size_t slot = (size_t)(e & 1u) * p.n_max;
-  __nv_bfloat16* mine = reinterpret_cast<__nv_bfloat16*>(p.bufs[p.rank]) + slot;
-  for (int i = threadIdx.x; i < p.n; i += blockDim.x) mine[i] = p.in[i];
-  __threadfence_system();
+  const size_t slot = (size_t)(e & 1u) * p.world * p.n_max;
+  const size_t row = slot + (size_t)p.rank * p.n_max;
+  // 16-byte pieces of the partial pushed to every rank (n is a multiple of 8)
+  const int n8 = p.n / 8;
+  for (int i = threadIdx.x; i < n8 * p.world; i += blockDim.x) {
+    const int r = i / n8, k = i - r * n8;
+    const uint4 v = reinterpret_cast<const uint4*>(p.in)[k];
+    reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.bufs[r]) + row)[k] = v;
+  }
   __syncthreads();
   if (threadIdx.x < p.world) {
-    unsigned* peer_pad = reinterpret_cast<unsigned*>(p.bufs[threadIdx.x] + p.flag_off);
-    st_release_sys(peer_pad + p.rank, e);
-    const unsigned* own_pad = reinterpret_cast<const unsigned*>(p.bufs[p.rank] + p.flag_off);
+    asm volatile("fence.acq_rel.sys;\n" ::: "memory");
+    unsigned* peer_flags = reinterpret_cast<unsigned*>(p.bufs[threadIdx.x] + p.flag_off);
+    st_release_sys(peer_flags + p.rank, e);
+    const unsigned* own_flags = reinterpret_cast<const unsigned*>(p.bufs[p.rank] + p.flag_off);
     unsigned it = 0;
-    while (ld_acquire_sys(own_pad + threadIdx.x) != e) {    // peer threadIdx.x's call-e data is in place
+    while (ld_acquire_sys(own_flags + threadIdx.x) != e) {  // rank threadIdx.x's call-e row is in place
       if (++it > kArSpinLimit) {
         flag_error(p.err, 2u);
         break;
       }
-      __nanosleep(32);
     }
   }
   __syncthreads();
+  const __nv_bfloat16* mine = reinterpret_cast<const __nv_bfloat16*>(p.bufs[p.rank]) + slot;
   for (int i = threadIdx.x; i < p.n; i += blockDim.x) {
     float acc = 0.f;
-    for (int r = 0; r < p.world; ++r) {
-      const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(p.bufs[r]) + slot;
-      acc += __bfloat162float(src[i]);
-    }
+    for (int r = 0; r < p.world; ++r) acc += __bfloat162float(mine[(size_t)r * p.n_max + i]);
     p.out[i] = __float2bfloat16(acc);
   }
   if (threadIdx.x == 0) *p.epoch = e;
@@ -83,7 +88,8 @@ int allreduce_peers_bf16(const void* in, void* out, int n, int n_max, const uint
   if (n <= 0) return kOk;
   if (!in || !out || !bufs || !epoch || world <= 0 || world > kArThreads || rank < 0 || rank >= world)
     return kErrArg;
-  if (n > n_max || flag_off < (size_t)n_max * 4 || flag_off % 16) return kErrShape;
+  if (n > n_max || n % 8 || n_max % 8 || flag_off < (size_t)n_max * 4 * world || flag_off % 16) return kErrShape;
+  if ((reinterpret_cast<uintptr_t>(in) & 15u)) return kErrAlign;
   ArParams p{};
   p.in = static_cast<const __nv_bfloat16*>(in);
   p.out = static_cast<__nv_bfloat16*>(out);

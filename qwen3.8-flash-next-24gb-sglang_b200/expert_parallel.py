@@ -67,12 +67,10 @@ class PeerAllReduce:
         self._native = _native
         self.group = group if group is not None else dist.group.WORLD
         self.n_max = n_max
-        self.flag_off = ((n_max * 4 + 255) // 256) * 256
         world = dist.get_world_size(self.group)
+        self.flag_off = ((n_max * 4 * world + 255) // 256) * 256
         self.buf = symm_mem.empty(self.flag_off + 4 * max(world, 64), dtype=torch.uint8, device=device)
         self.buf.zero_()
-        if hasattr(symm_mem, "enable_symm_mem_for_group"):
-            symm_mem.enable_symm_mem_for_group(self.group.group_name)
         self.handle = symm_mem.rendezvous(self.buf, self.group)
         self.rank, self.world = self.handle.rank, self.handle.world_size
         self.peers = torch.tensor([int(a) for a in self.handle.buffer_ptrs], dtype=torch.int64, device=device)
@@ -187,6 +185,33 @@ def _bench_ep(args, rank: int, world: int, dev: torch.device) -> None:
     dist.all_reduce(nccl)
     ar_err = O.max_rel_err(mine.float().cpu(), nccl.cpu())
     ar_flag = int(ar.err.item())
+    ar_us = {}
+    for name, fn in (("peer", lambda t: ar(t)), ("nccl", lambda t: dist.all_reduce(t))):
+        bufs = [part.clone() for _ in range(48)]
+        for t in bufs[:4]:
+            fn(t)
+        torch.cuda.synchronize()
+        ga = torch.cuda.CUDAGraph()
+        sa = torch.cuda.Stream()
+        sa.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(sa):
+            with torch.cuda.graph(ga, stream=sa):
+                for t in bufs:
+                    fn(t)
+        torch.cuda.current_stream().wait_stream(sa)
+        ga.replay()
+        torch.cuda.synchronize()
+        dist.barrier()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record()
+        for _ in range(5):
+            ga.replay()
+        a1.record()
+        torch.cuda.synchronize()
+        del ga
+        tm = torch.tensor([a0.elapsed_time(a1) * 1e3 / (5 * 48)], device=dev)
+        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+        ar_us[name] = round(float(tm.item()), 2)
 
     def run(i):
         x_in.copy_(x_d[i % P])
@@ -279,7 +304,8 @@ def _bench_ep(args, rank: int, world: int, dev: torch.device) -> None:
             "clocks": clk.summary(),
             "check_max_rel_err": err,
             "allreduce": {"impl": "w2a16_allreduce_peers_bf16 (one-shot over NVLink peer memory)",
-                          "max_rel_err_vs_nccl_fp32": ar_err, "device_error_word": ar_flag},
+                          "max_rel_err_vs_nccl_fp32": ar_err, "device_error_word": ar_flag,
+                          "us_per_call_graph": ar_us},
             "setup_s": round(setup_s, 1),
         }
         print(json.dumps(line), flush=True)
