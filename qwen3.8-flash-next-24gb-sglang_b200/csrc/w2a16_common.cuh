@@ -218,35 +218,6 @@ __device__ __forceinline__ void prep_group_regs(const float (&v)[4], int gl, XTa
   }
 }
 
-// Same conversion for an fp32 activation row written earlier in the same kernel by other CTAs:
-// the loads bypass L1 (ld.global.cg), so no stale line can be read. `gl` is the group's index in `tab`.
-__device__ __forceinline__ void prep_group_warp_l2(const float* __restrict__ src, int gl, XTable tab, int lane) {
-  const float4 v4 = __ldcg(reinterpret_cast<const float4*>(src) + lane);
-  const float v[4] = {v4.x, v4.y, v4.z, v4.w};
-  float mx = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  const int e = (mx > 0.f ? frexp_exponent(mx) : 0) - 15;
-  const float inv = pow2f(-e);
-  int s = 0;
-  uint16_t* half = reinterpret_cast<uint16_t*>(tab.pairs);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    int q = __float2int_rn(v[i] * inv);
-    q = max(-32767, min(32767, q));
-    s += q;
-    const int k = gl * kGroup + 4 * lane + i;
-    const int kw = k >> 4, c = k & 15;
-    half[(kw * kXRegs + (c & 3) * 2 + (c >> 3)) * 2 + ((c >> 2) & 1)] = static_cast<uint16_t>(q);
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-  if (lane == 0) {
-    tab.m64x[gl] = -64 * s;
-    tab.scl[gl] = pow2f(e - 6);
-  }
-}
-
 // ----------------------------------------------------------------------------- expert addressing
 // Either the reference's int64 address tables (make_tables, gemv/moe_gemv_int2_tab.py:88-97) or the
 // arena form: base + slot[e] * stride, slot -1 = expert not resident -> the row contributes zero.

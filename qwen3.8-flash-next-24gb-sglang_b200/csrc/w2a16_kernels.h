@@ -23,8 +23,6 @@ struct GemvArgs {
 };
 
 int gemv_plain(const GemvArgs& g);
-int gemv_gateup_silu(const GemvArgs& g, int I, float* h, int64_t stride_hm);
-int gemv_down_sum(const GemvArgs& g, int M, float routed_scaling);
 
 // Fused persistent decode layer (w2a16_layer.cu).
 struct LayerArgs {

@@ -96,12 +96,12 @@ struct RowPtr {
 SmemPlan smem_plan(const Geo& g) {
   SmemPlan s{};
   const size_t t1 = (size_t)g.M * token_table_bytes(g.H);
-  const size_t t2 = (size_t)g.max_units * g.top_k * token_table_bytes(g.I);
+  const size_t t2 = (size_t)g.top_k * token_table_bytes(g.I);  // one down unit's tables at a time
   s.tabs = t1 > t2 ? t1 : t2;
   s.mail1 = (size_t)g.max_range * 64 * 4;
-  s.mail2 = (size_t)g.max_units * g.s2 * 32 * 4;
+  s.mail2 = (size_t)g.s2 * 32 * 4;
   s.rows = ((size_t)g.R * sizeof(RowPtr) + 15) & ~size_t(15);
-  s.hstage = (size_t)g.max_units * g.top_k * g.I * 4;           // h rows of the down units (bulk copies)
+  s.hstage = (size_t)g.top_k * g.I * 4;                         // h rows of one down unit (bulk copies)
   s.misc = 64;                                                  // mbarrier, head counter, generation
   s.live = ((size_t)(2 * g.R + g.M + g.max_units * g.top_k) * 4 + 15) & ~size_t(15);   // LiveRows arrays
   s.itab = (size_t)(g.max_range + g.max_units * g.s2) * 16;     // the CTA's item descriptors (producers)
@@ -163,8 +163,7 @@ struct LiveRows {
   const int* rowmap;   // [R] compact phase-1 row -> routed row
   const int* tokrow;   // [M][top_k] j-th live row of token m, as an index within the token's top_k
   const int* tokcnt;   // [M] live rows per token
-  const int* slotrow;  // [max_units][top_k] routed row of each h staging slot of this CTA, -1 = dead
-  int live_slots;      // staging slots holding a live row (h rows this CTA copies)
+  const int* slotrow;  // [max_units][top_k] routed row of slot jr of this CTA's unit q, -1 = dead
   int n1;              // phase-1 items over the live rows
   int grid1;           // CTAs holding phase-1 items (each range at least one h-block)
 };
@@ -226,7 +225,7 @@ __device__ __forceinline__ Work work_at(const Geo& g, const LiveRows& lv, const 
   w.b = u - m * g.nb2;
   unit_row(g, lv, m, j, w);
   w.unit = q;
-  w.slot = q * g.s2 + j;
+  w.slot = j;                 // mail2 holds one unit at a time
   w.seq = L.range + q * g.s2 + j;
   return w;
 }
@@ -539,7 +538,7 @@ __device__ __forceinline__ void process_work(const FusedParams& p, const Work& w
   const RowPtr& rp = rows[w.r];
   unsigned char* tabs = smem + p.off_tabs;
   const XTable tb = k1 ? table_at(tabs + (size_t)(w.r / g.top_k) * token_table_bytes(g.H), g.H)
-                       : table_at(tabs + (size_t)(w.unit * g.top_k + w.jr) * token_table_bytes(g.I), g.I);
+                       : table_at(tabs + (size_t)w.jr * token_table_bytes(g.I), g.I);
   const LaneMap lm = lane_map(g, w, lane, rows);
   float v[4] = {0.f, 0.f, 0.f, 0.f};
   if (lm.valid) {
@@ -642,11 +641,9 @@ __device__ __forceinline__ void head_item_done(const FusedParams& p, const LiveR
 // Phase switch, entered by every warp of the CTA once its gate_up items are done. (1) h of every h-block
 // this CTA finishes, in item order: whole blocks from its own partials; the block it shares with the next
 // CTA from its head part plus the tail sums that CTA published (bounded wait on its flag); the block it
-// shares with the previous CTA is finished there. (2) Grid barrier: h is complete. (3) One bulk copy per
-// h row of this CTA's down units into shared memory, then every warp converts its groups from there.
-template <int kHB>
+// shares with the previous CTA is finished there. (2) Grid barrier: h is complete.
 __device__ __forceinline__ void phase_switch(const FusedParams& p, const LiveRows& lv, int cta, int warp, int lane,
-                                             unsigned char* smem, const float* mail1, unsigned epoch, uint32_t hbar) {
+                                             const float* mail1, unsigned epoch) {
   const Geo& g = p.geo;
   const WarpList L = warp_list(g, lv, cta, warp);
   csync();
@@ -690,20 +687,33 @@ __device__ __forceinline__ void phase_switch(const FusedParams& p, const LiveRow
   if (threadIdx.x == 0) grid_barrier(p.bar_count, p.bar_gen, epoch - 1u, gridDim.x, p.err);
   csync();
 
-  // (3) h rows of the down units' live rows -> shared memory (row slot q * top_k + jr), then the tables
+}
+
+// The down unit q of this CTA (token m, 32 output columns): the h rows of its live routed rows -> shared
+// memory with one bulk copy each (staging slot jr), then their fixed-point tables (table slot jr). Starts
+// and ends with a barrier of the reducing warps, so the previous unit's tables are free and this unit's are
+// complete when its items run.
+template <int kHB>
+__device__ __forceinline__ void unit_tables(const FusedParams& p, const LiveRows& lv, int q, int warp, int lane,
+                                            unsigned char* smem, uint32_t hbar) {
+  const Geo& g = p.geo;
   float* hst = reinterpret_cast<float*>(smem + p.off_hstage);
-  const int nrows = L.nu * g.top_k;
+  const int* slotrow = lv.slotrow + q * g.top_k;
   const unsigned row_bytes = (unsigned)g.I * 4u;
-  if (threadIdx.x == 0) mbar_arrive_tx(hbar, row_bytes * (unsigned)lv.live_slots);
-  if (threadIdx.x < nrows && lv.slotrow[threadIdx.x] >= 0) {
+  csync();
+  if (threadIdx.x == 0) {
+    unsigned live = 0;
+    for (int jr = 0; jr < g.top_k; ++jr) live += slotrow[jr] >= 0;
+    mbar_arrive_tx(hbar, row_bytes * live);
+  }
+  if (threadIdx.x < g.top_k && slotrow[threadIdx.x] >= 0) {
     asm volatile("fence.proxy.async.global;\n" ::: "memory");  // h was written through the generic proxy
-    bulk_g2s(smem_u32(hst + (size_t)threadIdx.x * g.I), p.hfin + (size_t)lv.slotrow[threadIdx.x] * g.I, row_bytes,
+    bulk_g2s(smem_u32(hst + (size_t)threadIdx.x * g.I), p.hfin + (size_t)slotrow[threadIdx.x] * g.I, row_bytes,
              hbar);
   }
-  if (threadIdx.x == 0) mbar_wait(hbar, 0u, p.err);
+  if (threadIdx.x == 0) mbar_wait(hbar, (unsigned)q & 1u, p.err);
   csync();
-  const int per_unit = g.top_k * g.G2;
-  const int ntab = L.nu * per_unit;
+  const int ntab = g.top_k * g.G2;
   unsigned char* tabs = smem + p.off_tabs;
   for (int k0 = warp; k0 < ntab; k0 += kHB * kWarps) {
     float hv[kHB][4];
@@ -714,8 +724,8 @@ __device__ __forceinline__ void phase_switch(const FusedParams& p, const LiveRow
       hv[j][0] = hv[j][1] = hv[j][2] = hv[j][3] = 0.f;
       gl[j] = -1;
       toff[j] = 0;
-      const int row = k / g.G2, gg = k - row * g.G2;           // row slot = q * top_k + jr
-      if (k < ntab && lv.slotrow[row] >= 0) {
+      const int row = k / g.G2, gg = k - row * g.G2;           // row = staging / table slot jr
+      if (k < ntab && slotrow[row] >= 0) {
         const float4 h4 = *reinterpret_cast<const float4*>(hst + (size_t)row * g.I + gg * kGroup + 4 * lane);
         hv[j][0] = h4.x; hv[j][1] = h4.y; hv[j][2] = h4.z; hv[j][3] = h4.w;
         gl[j] = gg;
@@ -828,19 +838,16 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
     const int nblk = nl * g.nb1;
     misc[4] = (unsigned)(nblk * g.kp1);
     misc[5] = (unsigned)max(1, min((int)gridDim.x, nblk));
-    int ls = 0;                            // h staging slots of this CTA's down units
-    for (int q = 0; q < g.max_units; ++q) {
+    for (int q = 0; q < g.max_units; ++q) {  // routed rows of this CTA's down units
       const int u = cta + g.grid * q, m = u / g.nb2;
       for (int jr = 0; jr < g.top_k; ++jr) {
         const bool on = u < g.u2 && jr < tokcnt[m];
         slotrow[q * g.top_k + jr] = on ? m * g.top_k + tokrow[m * g.top_k + jr] : -1;
-        ls += on;
       }
     }
-    misc[6] = (unsigned)ls;
   }
   __syncthreads();
-  const LiveRows lv{rowmap, tokrow, tokcnt, slotrow, (int)misc[6], (int)misc[4], (int)misc[5]};
+  const LiveRows lv{rowmap, tokrow, tokcnt, slotrow, (int)misc[4], (int)misc[5]};
   const WarpList L = warp_list(g, lv, cta, warp < kWarps ? warp : 0);
   const int total = L.total();
   if (kTma) {
@@ -885,18 +892,13 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
   }
   csync();
 
-  // One loop over this warp's work list. Register mode: take the item whose loads are in flight, issue
-  // the next one's, reduce. Copy-engine mode: wait for the item's ring stage, reduce, release the stage.
-  // t == n1w (the warp's first down item) switches phase.
+  // The warp's work list: its gate_up items, the phase switch, then unit by unit its down items (each unit
+  // preceded by the unit's h tables and followed by the unit's y). Register mode: take the item whose loads
+  // are in flight, issue the next one's, reduce. Copy-engine mode: wait for the item's ring stage, reduce,
+  // release the stage.
   const unsigned epoch = misc[3] + 1u;
   const int head_k = L.a % g.kp1 ? min(g.kp1 - L.a % g.kp1, L.range) : 0;   // items finishing a shared block
-  bool p1done = false;
-  for (int t = 0;; ++t) {
-    if (t == L.n1w && !p1done) {
-      phase_switch<kTma ? 6 : 2>(p, lv, cta, warp, lane, smem, mail1, epoch, hbar);
-      p1done = true;
-    }
-    if (t >= total) break;
+  auto do_item = [&](int t) {
     if (kTma) {
       const Work w = work_at(g, lv, L, cta, warp, t);
       const int st = w.seq % p.nstage;
@@ -920,15 +922,19 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
       __syncwarp();
       if (wc.kind == 1 && wc.slot < head_k) head_item_done(p, lv, L, cta, lane, mail1, head_k, epoch, misc + 2);
     }
-  }
-  csync();
-
-  // y of each unit: fixed-order sum of its top_k x K-part partials
-  for (int q = warp; q < L.nu; q += kWarps) {
-    const int u = cta + g.grid * q, m = u / g.nb2, b = u - m * g.nb2;
-    float acc = 0.f;
-    for (int j = 0; j < g.s2; ++j) acc += mail2[((size_t)q * g.s2 + j) * 32 + lane];
-    p.y[(int64_t)m * g.H + b * 32 + lane] = __float2bfloat16(acc * p.rsf);
+  };
+  for (int t = 0; t < L.n1w; ++t) do_item(t);
+  phase_switch(p, lv, cta, warp, lane, mail1, epoch);
+  for (int q = 0; q < L.nu; ++q) {
+    unit_tables<kTma ? 6 : 2>(p, lv, q, warp, lane, smem, hbar);
+    for (int k = 0; k < L.n2w; ++k) do_item(L.n1w + q * L.n2w + k);
+    csync();
+    if (warp == 0) {                          // y of the unit: fixed-order sum of its top_k x K-part partials
+      const int u = cta + g.grid * q, m = u / g.nb2, b = u - m * g.nb2;
+      float acc = 0.f;
+      for (int j = 0; j < g.s2; ++j) acc += mail2[(size_t)j * 32 + lane];
+      p.y[(int64_t)m * g.H + b * 32 + lane] = __float2bfloat16(acc * p.rsf);
+    }
   }
 }
 
