@@ -1,29 +1,33 @@
 // Decode MoE layer in one cooperative kernel: gate_up GEMV + SiLU*mul, down GEMV * routed weight,
 // sum over the top-k experts of each token (the composite of patches/ncontig_gemv.py:218-238).
 //
-// Phase 1 (gate_up). Work items are (row r, block of 32 h-columns, 2 groups of K): 32 lanes = 2 groups
-// x 16 column quads, quads 0-7 over the 32 gate columns and 8-15 over the matching 32 up columns, so a
-// warp reads two 128-byte runs per word row. The R * I/32 * ceil(G1/2) items are cut into one
-// contiguous, equal-sized range per CTA; a CTA's 16 warps share its range round-robin and leave one
-// 64-float partial per item in shared memory. Once the range is done the CTA sums the partials of each
-// h-block it touched in item order (deterministic) and writes (gate, up) to one of two part slots in
-// the workspace: slot 0 when the block starts in this CTA, slot 1 when it started in the previous CTA
-// (a range is at least one block long, so no block spans more than two CTAs); a block wholly inside the
-// range also zeroes its slot 1.
+// Prologue. The routing (ids -> slot -> expert bases) is resolved first, the activation rows are turned
+// into fixed-point tables while those loads are in flight, and one warp compacts the live routed rows
+// (slot >= 0) with ballots, so the first weight copy is issued a few hundred nanoseconds after the
+// routing arrives.
+//
+// Phase 1 (gate_up). Work items are (live row r, block of 32 h-columns, 2 groups of K): 32 lanes = 2
+// groups x 16 column quads, quads 0-7 over the 32 gate columns and 8-15 over the matching 32 up columns.
+// The items are cut into one contiguous range per CTA (sizes differ by at most one, and a range is at
+// least one h-block long, so no block spans more than two CTAs); a CTA's 16 warps share its range
+// round-robin and leave one 64-float partial per item in shared memory. The CTA then finishes each h-block
+// that starts in its range, in item order (deterministic): the tail of a block that runs into the next
+// CTA comes from that CTA's published partial sums (neighbour hand-off, bounded wait on its flag).
+// A finished block's 32 values h = silu(gate) * up are written straight into the row's down-projection
+// activation table in the workspace: 16-bit fixed point with one power-of-two exponent per 32 values
+// (the block), so no CTA ever converts h again.
 //
 // One grid barrier (bounded wait), then phase 2 (down). Work units are (token m, block of 32 output
-// columns): top_k rows x ceil(G2/4) K-parts = items of 4 groups x 8 column quads. Units are dealt
-// round-robin to CTAs; their code data were already prefetched into the warps' staging buffers while
-// phase 1 finished. The CTA builds the h tables of its units' rows, h = silu(g0 + g1) * (u0 + u1) from
-// the part slots, computes the items, and reduces each unit's top_k x K-part partials in fixed order in
-// shared memory into y. No atomics beyond the barrier, no ticket chains.
+// columns): live rows x ceil(G2/4) K-parts = items of 4 groups x 8 column quads. Units are dealt
+// round-robin to CTAs and processed one at a time: the unit's h tables are bulk-copied into shared
+// memory, its items reduced, and its partials summed in fixed order into y. No atomics beyond the
+// barrier and the hand-off flags.
 //
-// Weight stream. At launch every CTA asks L2 to fetch its 1/grid share of each routed expert's code,
-// scale and zero-point arrays (cp.async.bulk.prefetch.L2, gate_up first, then down), so HBM streams the
-// whole layer at full rate from the first microsecond. Each lane then loads its own item data straight
-// into registers with 16-byte non-allocating loads -- 8 word rows of its 4 columns, 4 scales and one
-// zero-point byte -- one item ahead of the one it is reducing; those loads hit L2 or merge with the
-// prefetch in flight, and no shared-memory staging or copy engine sits on the path.
+// Weight stream. Copy-engine mode (slot arenas): producer threads stream every item's codes, scales
+// and zero points through a ring of shared-memory stages with tensor copies, phase-2 items right behind
+// phase-1 items, so the down weights are in flight while phase 1 finishes. Register mode (int64 address
+// tables): at launch every CTA asks L2 to fetch its 1/grid share of each routed expert's arrays, and each
+// lane loads its own item data into registers one item ahead of the one it is reducing.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -80,8 +84,16 @@ __host__ __device__ __forceinline__ size_t token_table_bytes(int K) {
   return ((size_t)(K / 16) * kXRegs * 4 + (size_t)(K / kGroup) * 8 + 15) & ~size_t(15);
 }
 
+// Down-projection activation table of one routed row (K = I): packed pairs [I/16][kXRegs], then per
+// 32-value sub-group m64x [I/32] and scl [I/32]. I is a multiple of 128, so the size is a multiple of
+// 16 bytes and rows can be moved with bulk copies.
+constexpr int kSub = 32;                                     // values per exponent in the h tables
+__host__ __device__ __forceinline__ size_t htab_bytes(int I) {
+  return (size_t)(I / 16) * kXRegs * 4 + (size_t)(I / kSub) * 8;
+}
+
 struct SmemPlan {
-  size_t tabs, mail1, mail2, rows, hstage, misc, live, itab, total;
+  size_t tabs, mail1, mail2, rows, misc, live, itab, total;
 };
 
 // Per routed row, resolved once per CTA: expert code / scale / zero-point bases of gate_up and down.
@@ -96,16 +108,16 @@ struct RowPtr {
 SmemPlan smem_plan(const Geo& g) {
   SmemPlan s{};
   const size_t t1 = (size_t)g.M * token_table_bytes(g.H);
-  const size_t t2 = (size_t)g.top_k * token_table_bytes(g.I);  // one down unit's tables at a time
+  const size_t t2 = (size_t)g.top_k * htab_bytes(g.I);         // one down unit's h tables at a time
   s.tabs = t1 > t2 ? t1 : t2;
   s.mail1 = (size_t)g.max_range * 64 * 4;
   s.mail2 = (size_t)g.s2 * 32 * 4;
   s.rows = ((size_t)g.R * sizeof(RowPtr) + 15) & ~size_t(15);
-  s.hstage = (size_t)g.top_k * g.I * 4;                         // h rows of one down unit (bulk copies)
   s.misc = 64;                                                  // mbarrier, head counter, generation
-  s.live = ((size_t)(2 * g.R + g.M + g.max_units * g.top_k) * 4 + 15) & ~size_t(15);   // LiveRows arrays
+  // LiveRows arrays and the live-row bit words
+  s.live = ((size_t)(2 * g.R + g.M + g.max_units * g.top_k + (g.R + 31) / 32) * 4 + 15) & ~size_t(15);
   s.itab = (size_t)(g.max_range + g.max_units * g.s2) * 16;     // the CTA's item descriptors (producers)
-  s.total = s.tabs + s.mail1 + s.mail2 + s.rows + s.hstage + s.misc + s.live + s.itab;
+  s.total = s.tabs + s.mail1 + s.mail2 + s.rows + s.misc + s.live + s.itab;
   return s;
 }
 
@@ -123,21 +135,51 @@ struct FusedParams {
   float rsf;
   __nv_bfloat16* y;
   Geo geo;
-  size_t off_tabs, off_mail1, off_mail2, off_rows, off_hstage, off_misc, off_live, off_itab;
+  size_t off_tabs, off_mail1, off_mail2, off_rows, off_misc, off_live, off_itab;
   unsigned* bar_count;   // grid barrier: arrivals (zero between calls)
   unsigned* bar_gen;     // grid barrier: generation, 128 bytes further
-  float* hfin;           // [R][I] h of h-blocks computed wholly inside one CTA
+  unsigned char* htab;   // [R][htab_bytes(I)] down-projection activation tables of the routed rows
   unsigned* hflags;      // [grid] generation + 1 once the CTA published the partial of its first h-block
   float* hpart;          // [R][2 (gate, up)][I] partial sums of the tails of h-blocks split across two CTAs
   unsigned* err;
 };
 
+// Activation table of a K-long row: one exponent per 128-value group (gate_up, from x) ...
 __device__ __forceinline__ XTable table_at(unsigned char* base, int K) {
   XTable t;
   t.pairs = reinterpret_cast<uint32_t*>(base);
   t.m64x = reinterpret_cast<int*>(base + (size_t)(K / 16) * kXRegs * 4);
   t.scl = reinterpret_cast<float*>(t.m64x + K / kGroup);
   return t;
+}
+// ... or one per 32-value sub-group (down, from h).
+__device__ __forceinline__ XTable htable_at(unsigned char* base, int I) {
+  XTable t;
+  t.pairs = reinterpret_cast<uint32_t*>(base);
+  t.m64x = reinterpret_cast<int*>(base + (size_t)(I / 16) * kXRegs * 4);
+  t.scl = reinterpret_cast<float*>(t.m64x + I / kSub);
+  return t;
+}
+
+// The 32 values of h-block hb (lane l holds element 32*hb + l) -> fixed-point entries of a down table:
+// exponent from the block's max |h| exactly as the 128-value activation groups take theirs, values
+// rounded to nearest and clamped to +-32767, pairs packed as in the activation tables (elements c and
+// c + 4 of a 16-value word row share a register). Whole warp, uniform control flow.
+__device__ __forceinline__ void htab_block(unsigned char* tab, int I, int hb, float h, int lane) {
+  const float mx = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(h))));
+  const int e = (mx > 0.f ? frexp_exponent(mx) : 0) - 15;
+  const int q = max(-32767, min(32767, __float2int_rn(h * pow2f(-e))));
+  const int s = __reduce_add_sync(0xffffffffu, q);
+  const int hi = __shfl_xor_sync(0xffffffffu, q, 4);
+  if ((lane & 4) == 0) {
+    const int c = lane & 15, kw = hb * 2 + (lane >> 4);
+    reinterpret_cast<uint32_t*>(tab)[kw * kXRegs + (c & 3) * 2 + (c >> 3)] = (uint32_t)(q & 0xFFFF) | ((uint32_t)hi << 16);
+  }
+  if (lane == 0) {
+    int* m64x = reinterpret_cast<int*>(tab + (size_t)(I / 16) * kXRegs * 4);
+    m64x[hb] = -64 * s;
+    reinterpret_cast<float*>(m64x + I / kSub)[hb] = pow2f(e - 6);
+  }
 }
 
 // Barrier of the 512 reducing threads only (the producer warp of copy-engine mode never joins).
@@ -178,13 +220,16 @@ struct WarpList {
   __device__ int total() const { return n1w + nu * n2w; }
 };
 
+// CTA ranges: the first n1 % grid1 CTAs take one item more than the others.
 __device__ __forceinline__ WarpList warp_list(const Geo& g, const LiveRows& lv, int cta, int warp) {
   WarpList L;
-  const long long a = cta < lv.grid1 ? (long long)cta * lv.n1 / lv.grid1 : lv.n1;
-  const long long b = cta < lv.grid1 ? (long long)(cta + 1) * lv.n1 / lv.grid1 : lv.n1;
-  L.a = (int)a;
-  L.b = (int)b;
-  const int range = (int)(b - a);
+  L.a = L.b = lv.n1;
+  if (cta < lv.grid1) {
+    const int q = lv.n1 / lv.grid1, rem = lv.n1 - q * lv.grid1;
+    L.a = cta * q + min(cta, rem);
+    L.b = L.a + q + (cta < rem ? 1 : 0);
+  }
+  const int range = L.b - L.a;
   L.range = range;
   L.n1w = range > warp ? (range - warp + kWarps - 1) / kWarps : 0;
   L.nu = cta < g.u2 ? (g.u2 - cta + g.grid - 1) / g.grid : 0;
@@ -293,42 +338,65 @@ __device__ __forceinline__ void load_item(const FusedParams& p, const Work& w, i
   it.z = rp.z[mi] != nullptr ? ldg_stream1(rp.z[mi] + (int64_t)lm.gl * (N / 4) + lm.col / 4) : 0u;
 }
 
-// 4 columns x 1 group of this lane from its registers against an activation table.
-__device__ __forceinline__ void dot_regs(const ItemRegs& it, const XTable& tb, int gl, bool sbf, bool has_z,
-                                         float (&v)[4]) {
-  int acc[4][4];
-#pragma unroll
-  for (int c = 0; c < 4; ++c)
-#pragma unroll
-    for (int j = 0; j < 4; ++j) acc[c][j] = 0;
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    const uint4* xp = reinterpret_cast<const uint4*>(tb.pairs + (gl * 8 + k) * kXRegs);
-    const uint4 xa = xp[0], xb = xp[1];
-    const uint32_t xr[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-    word_dot(it.w[k].x, xr, acc[0]);
-    word_dot(it.w[k].y, xr, acc[1]);
-    word_dot(it.w[k].z, xr, acc[2]);
-    word_dot(it.w[k].w, xr, acc[3]);
-  }
-  float s[4];
+__device__ __forceinline__ void scales4(uint2 sr, bool sbf, float (&s)[4]) {
   if (sbf) {
-    const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&it.s.x);
-    const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&it.s.y);
+    const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&sr.x);
+    const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&sr.y);
     s[0] = __low2float(a); s[1] = __high2float(a); s[2] = __low2float(b); s[3] = __high2float(b);
   } else {
-    const __half2 a = *reinterpret_cast<const __half2*>(&it.s.x);
-    const __half2 b = *reinterpret_cast<const __half2*>(&it.s.y);
+    const __half2 a = *reinterpret_cast<const __half2*>(&sr.x);
+    const __half2 b = *reinterpret_cast<const __half2*>(&sr.y);
     s[0] = __low2float(a); s[1] = __high2float(a); s[2] = __low2float(b); s[3] = __high2float(b);
   }
-  const int m64x = tb.m64x[gl];
-  const float scl = tb.scl[gl];
+}
+
+// 4 columns x 1 group of K (8 word rows) against an activation table with kPer exponents per group
+// (1: the gate_up tables, 4: the down tables, one per 32 values). wd(k) gives word row k of the 4
+// columns; z = zero-point byte of the 4 columns (has_z), s = their scales. Per exponent span:
+// T = 64 * sum (q - zp) x_fixed exactly, then v += T * 2^(e - 6); v * s at the end.
+template <int kPer, typename WordRow>
+__device__ __forceinline__ void dot_group(WordRow wd, const XTable& tb, int gl, const float (&s)[4], bool has_z,
+                                          uint32_t z, float (&v)[4]) {
+  constexpr int kRows = 8 / kPer;
+  float f[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    const int zp = has_z ? (int)((it.z >> (2 * c)) & 3u) : 2;
-    const int T = combine_classes(acc[c]) + zp * m64x;
-    v[c] = (float)T * (s[c] * scl);
+  for (int sp = 0; sp < kPer; ++sp) {
+    int acc[4][4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[c][j] = 0;
+#pragma unroll
+    for (int kk = 0; kk < kRows; ++kk) {
+      const int k = sp * kRows + kk;
+      const uint4 w = wd(k);
+      const uint4* xp = reinterpret_cast<const uint4*>(tb.pairs + (gl * 8 + k) * kXRegs);
+      const uint4 xa = xp[0], xb = xp[1];
+      const uint32_t xr[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+      word_dot(w.x, xr, acc[0]);
+      word_dot(w.y, xr, acc[1]);
+      word_dot(w.z, xr, acc[2]);
+      word_dot(w.w, xr, acc[3]);
+    }
+    const int m64x = tb.m64x[gl * kPer + sp];
+    const float scl = tb.scl[gl * kPer + sp];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int zp = has_z ? (int)((z >> (2 * c)) & 3u) : 2;
+      f[c] += (float)(combine_classes(acc[c]) + zp * m64x) * scl;
+    }
   }
+#pragma unroll
+  for (int c = 0; c < 4; ++c) v[c] = f[c] * s[c];
+}
+
+// 4 columns x 1 group of this lane from its registers against an activation table.
+template <int kPer>
+__device__ __forceinline__ void dot_regs(const ItemRegs& it, const XTable& tb, int gl, bool sbf, bool has_z,
+                                         float (&v)[4]) {
+  float s[4];
+  scales4(it.s, sbf, s);
+  dot_group<kPer>([&](int k) { return it.w[k]; }, tb, gl, s, has_z, it.z, v);
 }
 
 // ----------------------------------------------------------------------------- copy-engine mode
@@ -479,6 +547,7 @@ __device__ void produce(const FusedParams& p, int n, const int4* itab, unsigned 
 // 4 columns x 1 group of this lane from a ring stage. Gate_up stages hold 256-byte word rows (32 gate |
 // 32 up columns), scales [group][half][32] and zero windows [group][half][16 B]; down stages 128-byte
 // rows, scales [group][32] and windows [group][16 B].
+template <int kPer>
 __device__ __forceinline__ void dot_stage(const unsigned char* st, const Work& w, int lane, const XTable& tb, int gl,
                                           bool sbf, bool has_z, float (&v)[4]) {
   const bool k1 = w.kind == 1;
@@ -489,42 +558,12 @@ __device__ __forceinline__ void dot_stage(const unsigned char* st, const Work& w
   const int row_bytes = k1 ? 256 : 128;
   const int sub = k1 ? gi * 2 + side : gi;                   // (group, half) index of scales / windows
   const unsigned char* code = st + (size_t)(8 * gi) * row_bytes + side * 128 + q8 * 16;
-  int acc[4][4];
-#pragma unroll
-  for (int c = 0; c < 4; ++c)
-#pragma unroll
-    for (int j = 0; j < 4; ++j) acc[c][j] = 0;
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    const uint4 wd = *reinterpret_cast<const uint4*>(code + k * row_bytes);
-    const uint4* xp = reinterpret_cast<const uint4*>(tb.pairs + (gl * 8 + k) * kXRegs);
-    const uint4 xa = xp[0], xb = xp[1];
-    const uint32_t xr[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-    word_dot(wd.x, xr, acc[0]);
-    word_dot(wd.y, xr, acc[1]);
-    word_dot(wd.z, xr, acc[2]);
-    word_dot(wd.w, xr, acc[3]);
-  }
   const uint2 sr = *reinterpret_cast<const uint2*>(st + kScaleOff + (sub * 32 + q8 * 4) * 2);
   float s[4];
-  if (sbf) {
-    const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&sr.x);
-    const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&sr.y);
-    s[0] = __low2float(a); s[1] = __high2float(a); s[2] = __low2float(b); s[3] = __high2float(b);
-  } else {
-    const __half2 a = *reinterpret_cast<const __half2*>(&sr.x);
-    const __half2 b = *reinterpret_cast<const __half2*>(&sr.y);
-    s[0] = __low2float(a); s[1] = __high2float(a); s[2] = __low2float(b); s[3] = __high2float(b);
-  }
+  scales4(sr, sbf, s);
   const uint32_t zbyte = has_z ? (uint32_t)st[kZeroOff + sub * 16 + ((8 * w.b) & 15) + q8] : 0u;
-  const int m64x = tb.m64x[gl];
-  const float scl = tb.scl[gl];
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    const int zp = has_z ? (int)((zbyte >> (2 * c)) & 3u) : 2;
-    const int T = combine_classes(acc[c]) + zp * m64x;
-    v[c] = (float)T * (s[c] * scl);
-  }
+  dot_group<kPer>([&](int k) { return *reinterpret_cast<const uint4*>(code + k * row_bytes); }, tb, gl, s, has_z,
+                  zbyte, v);
 }
 
 
@@ -537,13 +576,19 @@ __device__ __forceinline__ void process_work(const FusedParams& p, const Work& w
   const int mi = w.kind - 1;
   const RowPtr& rp = rows[w.r];
   unsigned char* tabs = smem + p.off_tabs;
-  const XTable tb = k1 ? table_at(tabs + (size_t)(w.r / g.top_k) * token_table_bytes(g.H), g.H)
-                       : table_at(tabs + (size_t)w.jr * token_table_bytes(g.I), g.I);
   const LaneMap lm = lane_map(g, w, lane, rows);
   float v[4] = {0.f, 0.f, 0.f, 0.f};
   if (lm.valid) {
-    if (kTma) dot_stage(stage, w, lane, tb, lm.gl, p.scale_bf16 != 0, rp.z[mi] != nullptr, v);
-    else dot_regs(it, tb, lm.gl, p.scale_bf16 != 0, rp.z[mi] != nullptr, v);
+    const bool sbf = p.scale_bf16 != 0, hz = rp.z[mi] != nullptr;
+    if (k1) {
+      const XTable tb = table_at(tabs + (size_t)(w.r / g.top_k) * token_table_bytes(g.H), g.H);
+      if (kTma) dot_stage<1>(stage, w, lane, tb, lm.gl, sbf, hz, v);
+      else dot_regs<1>(it, tb, lm.gl, sbf, hz, v);
+    } else {
+      const XTable tb = htable_at(tabs + (size_t)w.jr * htab_bytes(g.I), g.I);
+      if (kTma) dot_stage<kGroup / kSub>(stage, w, lane, tb, lm.gl, sbf, hz, v);
+      else dot_regs<kGroup / kSub>(it, tb, lm.gl, sbf, hz, v);
+    }
   }
   if (k1) {
 #pragma unroll
@@ -639,9 +684,10 @@ __device__ __forceinline__ void head_item_done(const FusedParams& p, const LiveR
 }
 
 // Phase switch, entered by every warp of the CTA once its gate_up items are done. (1) h of every h-block
-// this CTA finishes, in item order: whole blocks from its own partials; the block it shares with the next
-// CTA from its head part plus the tail sums that CTA published (bounded wait on its flag); the block it
-// shares with the previous CTA is finished there. (2) Grid barrier: h is complete.
+// this CTA finishes, in item order, into the down tables: whole blocks from its own partials; the block it
+// shares with the next CTA from its head part plus the tail sums that CTA published (bounded wait on its
+// flag); the block it shares with the previous CTA is finished there. (2) Grid barrier: the tables are
+// complete.
 __device__ __forceinline__ void phase_switch(const FusedParams& p, const LiveRows& lv, int cta, int warp, int lane,
                                              const float* mail1, unsigned epoch) {
   const Geo& g = p.geo;
@@ -678,7 +724,7 @@ __device__ __forceinline__ void phase_switch(const FusedParams& p, const LiveRow
           gs += __ldcg(p.hpart + ((size_t)r * 2) * g.I + col);
           us += __ldcg(p.hpart + ((size_t)r * 2 + 1) * g.I + col);
         }
-        p.hfin[(size_t)r * g.I + col] = silu(gs) * us;
+        htab_block(p.htab + (size_t)r * htab_bytes(g.I), g.I, hb, silu(gs) * us, lane);
       }
       __threadfence();
     }
@@ -689,51 +735,26 @@ __device__ __forceinline__ void phase_switch(const FusedParams& p, const LiveRow
 
 }
 
-// The down unit q of this CTA (token m, 32 output columns): the h rows of its live routed rows -> shared
-// memory with one bulk copy each (staging slot jr), then their fixed-point tables (table slot jr). Starts
-// and ends with a barrier of the reducing warps, so the previous unit's tables are free and this unit's are
-// complete when its items run.
-template <int kHB>
-__device__ __forceinline__ void unit_tables(const FusedParams& p, const LiveRows& lv, int q, int warp, int lane,
-                                            unsigned char* smem, uint32_t hbar) {
+// The down unit q of this CTA (token m, 32 output columns): the h tables of its live routed rows ->
+// shared memory (table slot jr), one bulk copy each. Starts with a barrier of the reducing warps (the
+// previous unit's tables are free) and ends with one (this unit's are in place).
+__device__ __forceinline__ void unit_tables(const FusedParams& p, const LiveRows& lv, int q, unsigned char* smem,
+                                            uint32_t hbar) {
   const Geo& g = p.geo;
-  float* hst = reinterpret_cast<float*>(smem + p.off_hstage);
   const int* slotrow = lv.slotrow + q * g.top_k;
-  const unsigned row_bytes = (unsigned)g.I * 4u;
+  const size_t tb = htab_bytes(g.I);
   csync();
   if (threadIdx.x == 0) {
     unsigned live = 0;
     for (int jr = 0; jr < g.top_k; ++jr) live += slotrow[jr] >= 0;
-    mbar_arrive_tx(hbar, row_bytes * live);
+    mbar_arrive_tx(hbar, (unsigned)tb * live);
   }
   if (threadIdx.x < g.top_k && slotrow[threadIdx.x] >= 0) {
-    asm volatile("fence.proxy.async.global;\n" ::: "memory");  // h was written through the generic proxy
-    bulk_g2s(smem_u32(hst + (size_t)threadIdx.x * g.I), p.hfin + (size_t)slotrow[threadIdx.x] * g.I, row_bytes,
-             hbar);
+    asm volatile("fence.proxy.async.global;\n" ::: "memory");  // the tables were written through the generic proxy
+    bulk_g2s(smem_u32(smem + p.off_tabs + (size_t)threadIdx.x * tb), p.htab + (size_t)slotrow[threadIdx.x] * tb,
+             (unsigned)tb, hbar);
   }
   if (threadIdx.x == 0) mbar_wait(hbar, (unsigned)q & 1u, p.err);
-  csync();
-  const int ntab = g.top_k * g.G2;
-  unsigned char* tabs = smem + p.off_tabs;
-  for (int k0 = warp; k0 < ntab; k0 += kHB * kWarps) {
-    float hv[kHB][4];
-    int gl[kHB], toff[kHB];
-#pragma unroll
-    for (int j = 0; j < kHB; ++j) {
-      const int k = k0 + j * kWarps;
-      hv[j][0] = hv[j][1] = hv[j][2] = hv[j][3] = 0.f;
-      gl[j] = -1;
-      toff[j] = 0;
-      const int row = k / g.G2, gg = k - row * g.G2;           // row = staging / table slot jr
-      if (k < ntab && slotrow[row] >= 0) {
-        const float4 h4 = *reinterpret_cast<const float4*>(hst + (size_t)row * g.I + gg * kGroup + 4 * lane);
-        hv[j][0] = h4.x; hv[j][1] = h4.y; hv[j][2] = h4.z; hv[j][3] = h4.w;
-        gl[j] = gg;
-        toff[j] = row * (int)token_table_bytes(g.I);
-      }
-    }
-    prep_groups<kHB>(hv, gl, toff, tabs, g.I, lane);
-  }
   csync();
 }
 
@@ -755,8 +776,20 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
   const uint32_t bars = kTma ? smem_u32(smem + p.off_bars) : 0u;
   int* tags = kTma ? reinterpret_cast<int*>(smem + p.off_bars + 16 * (size_t)p.nstage) : nullptr;
 
-  // the barrier generation of this call, loaded first (its latency overlaps the prologue)
+  // the barrier generation of this call (read at entry; the count reaches it before any CTA of this call
+  // can pass the barrier)
   const unsigned gen_entry = threadIdx.x == 0 ? ld_acquire_u32(p.bar_gen) : 0u;
+  // routing first: expert bases of every routed row, resolved once per CTA; the loads' latency overlaps
+  // the barrier setup and the activation tables below
+  for (int r = threadIdx.x; r < g.R; r += blockDim.x) {
+    RowPtr rp;
+    const int e = p.ids[r];
+    rp.ok[0] = p.map13.resolve(e, rp.w[0], rp.s[0], rp.z[0], p.err);
+    rp.ok[1] = p.map2.resolve(e, rp.w[1], rp.s[1], rp.z[1], p.err);
+    rp.slot = (p.map13.slots != nullptr && e >= 0 && e < p.map13.E) ? p.map13.slots[e] : -1;
+    if (kTma && rp.slot >= kSlotExtent) flag_error(p.err, 1u);
+    rows[r] = rp;
+  }
   if (!kTma) {
     // Start the whole layer's weight stream: this CTA's 1/grid share of every routed row's six arrays.
     // A prefetch is only a hint, so arrays whose base is not 16-byte aligned are left to the loads.
@@ -779,118 +812,120 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
       if (len > 0)
         asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(base + start), "r"((unsigned)len) : "memory");
     }
-  } else if (threadIdx.x < 2 * p.nstage) {
-    mbar_init(bars + threadIdx.x * 8, 1);                     // full[0..ns), then empty[0..ns)
-    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
-    if (threadIdx.x < p.nstage) tags[threadIdx.x] = -1;
-  }
-
-  const int nxt = g.M * g.G1;
-
-  // activation values of this warp's first table groups
-  constexpr int kXPre = 4;
-  float xv[kXPre][4];
-#pragma unroll
-  for (int j = 0; j < kXPre; ++j) {
-    const int t = warp + j * kWarps;
-    if (warp < kWarps && t < nxt) {
-      const int m = t / g.G1, gi = t - m * g.G1;
-      const __nv_bfloat162* src =
-          reinterpret_cast<const __nv_bfloat162*>(p.x + (int64_t)m * g.H + gi * kGroup + 4 * lane);
-      const float2 a0 = __bfloat1622float2(src[0]), a1 = __bfloat1622float2(src[1]);
-      xv[j][0] = a0.x; xv[j][1] = a0.y; xv[j][2] = a1.x; xv[j][3] = a1.y;
-    } else {
-      xv[j][0] = xv[j][1] = xv[j][2] = xv[j][3] = 0.f;
+  } else {
+    if (threadIdx.x < 2 * p.nstage) {
+      mbar_init(bars + threadIdx.x * 8, 1);                   // full[0..ns), then empty[0..ns)
+      asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+      if (threadIdx.x < p.nstage) tags[threadIdx.x] = -1;
     }
+    // the producers' tensor maps into the descriptor cache before their first copies (maps of absent
+    // zero-point arrays are not encoded and are skipped)
+    if (warp == kWarps && lane < 6 && (p.map13.has_zeros || (lane != 2 && lane != 5)))
+      asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&p.tm[lane])) : "memory");
   }
-  // expert bases of every routed row, resolved once per CTA
-  for (int r = threadIdx.x; r < g.R; r += blockDim.x) {
-    RowPtr rp;
-    const int e = p.ids[r];
-    rp.ok[0] = p.map13.resolve(e, rp.w[0], rp.s[0], rp.z[0], p.err);
-    rp.ok[1] = p.map2.resolve(e, rp.w[1], rp.s[1], rp.z[1], p.err);
-    rp.slot = (p.map13.slots != nullptr && e >= 0 && e < p.map13.E) ? p.map13.slots[e] : -1;
-    if (kTma && rp.slot >= kSlotExtent) flag_error(p.err, 1u);
-    rows[r] = rp;
+
+  // activation tables of the M rows of x (no dependence on the routing)
+  if (warp < kWarps) {
+    const int nxt = g.M * g.G1;
+    constexpr int kXPre = 4;
+    float xv[kXPre][4];
+    int gl[kXPre], toff[kXPre];
+#pragma unroll
+    for (int j = 0; j < kXPre; ++j) {
+      const int t = warp + j * kWarps;
+      const int m = t / g.G1, gi = t - m * g.G1;
+      xv[j][0] = xv[j][1] = xv[j][2] = xv[j][3] = 0.f;
+      gl[j] = -1;
+      toff[j] = 0;
+      if (t < nxt) {
+        const __nv_bfloat162* src =
+            reinterpret_cast<const __nv_bfloat162*>(p.x + (int64_t)m * g.H + gi * kGroup + 4 * lane);
+        const float2 a0 = __bfloat1622float2(src[0]), a1 = __bfloat1622float2(src[1]);
+        xv[j][0] = a0.x; xv[j][1] = a0.y; xv[j][2] = a1.x; xv[j][3] = a1.y;
+        gl[j] = gi;
+        toff[j] = m * (int)token_table_bytes(g.H);
+      }
+    }
+    prep_groups<kXPre>(xv, gl, toff, smem + p.off_tabs, g.H, lane);
+    for (int tt = warp + kXPre * kWarps; tt < nxt; tt += kWarps) {
+      const int m = tt / g.G1, gi = tt - m * g.G1;
+      const __nv_bfloat16* src = p.x + (int64_t)m * g.H + gi * kGroup + 4 * lane;
+      const float v[4] = {__bfloat162float(src[0]), __bfloat162float(src[1]), __bfloat162float(src[2]),
+                          __bfloat162float(src[3])};
+      prep_group_regs(v, gi, table_at(smem + p.off_tabs + (size_t)m * token_table_bytes(g.H), g.H), lane);
+    }
   }
   int* rowmap = reinterpret_cast<int*>(smem + p.off_live);
   int* tokrow = rowmap + g.R;
   int* tokcnt = tokrow + g.R;
   int* slotrow = tokcnt + g.M;
+  unsigned* livebits = reinterpret_cast<unsigned*>(slotrow + g.max_units * g.top_k);
   __syncthreads();
-  if (threadIdx.x == 0) {
-    mbar_init(hbar, 1);
-    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
-    misc[2] = 0u;
-    misc[3] = gen_entry;                   // read by every CTA before any passes this call's barrier
-    int nl = 0;                            // live rows, token by token, in routing order
-    for (int m = 0; m < g.M; ++m) {
+  // Live routed rows (both experts resolve), compacted by one warp with ballots: rowmap in routing order,
+  // and per token its live rows' positions within its top_k.
+  if (warp == 0) {
+    int nl = 0;
+    for (int c0 = 0; c0 < g.R; c0 += 32) {
+      const int r = c0 + lane;
+      const bool live = r < g.R && rows[r].ok[0] && rows[r].ok[1];
+      const unsigned bal = __ballot_sync(0xffffffffu, live);
+      if (live) rowmap[nl + __popc(bal & ((1u << lane) - 1u))] = r;
+      if (lane == 0) livebits[c0 >> 5] = bal;
+      nl += __popc(bal);
+    }
+    __syncwarp();
+    for (int m = lane; m < g.M; m += 32) {
       int c = 0;
       for (int j = 0; j < g.top_k; ++j) {
         const int r = m * g.top_k + j;
-        if (rows[r].ok[0] && rows[r].ok[1]) {
-          tokrow[m * g.top_k + c++] = j;
-          rowmap[nl++] = r;
-        }
+        if ((livebits[r >> 5] >> (r & 31)) & 1u) tokrow[m * g.top_k + c++] = j;
       }
       tokcnt[m] = c;
     }
-    const int nblk = nl * g.nb1;
-    misc[4] = (unsigned)(nblk * g.kp1);
-    misc[5] = (unsigned)max(1, min((int)gridDim.x, nblk));
-    for (int q = 0; q < g.max_units; ++q) {  // routed rows of this CTA's down units
-      const int u = cta + g.grid * q, m = u / g.nb2;
-      for (int jr = 0; jr < g.top_k; ++jr) {
-        const bool on = u < g.u2 && jr < tokcnt[m];
-        slotrow[q * g.top_k + jr] = on ? m * g.top_k + tokrow[m * g.top_k + jr] : -1;
-      }
+    if (lane == 0) {
+      mbar_init(hbar, 1);
+      asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+      misc[2] = 0u;
+      misc[3] = gen_entry;                 // read by every CTA before any passes this call's barrier
+      const int nblk = nl * g.nb1;
+      misc[4] = (unsigned)(nblk * g.kp1);
+      misc[5] = (unsigned)max(1, min((int)gridDim.x, nblk));
     }
   }
   __syncthreads();
   const LiveRows lv{rowmap, tokrow, tokcnt, slotrow, (int)misc[4], (int)misc[5]};
+  for (int idx = threadIdx.x; idx < g.max_units * g.top_k; idx += blockDim.x) {   // rows of the CTA's down units
+    const int q = idx / g.top_k, jr = idx - q * g.top_k, u = cta + g.grid * q;
+    int row = -1;
+    if (u < g.u2) {
+      const int m = u / g.nb2;
+      if (jr < tokcnt[m]) row = m * g.top_k + tokrow[m * g.top_k + jr];
+    }
+    slotrow[idx] = row;
+  }
   const WarpList L = warp_list(g, lv, cta, warp < kWarps ? warp : 0);
   const int total = L.total();
+  int n_items = 0;
+  int4* itab = reinterpret_cast<int4*>(smem + p.off_itab);
   if (kTma) {
     // descriptors of the CTA's items in ring order, built once in parallel for the producers
     const WarpList L0 = warp_list(g, lv, cta, 0);
-    const int n_items = L0.range + L0.nu * g.s2;
-    int4* itab = reinterpret_cast<int4*>(smem + p.off_itab);
+    n_items = L0.range + L0.nu * g.s2;
     for (int i = threadIdx.x; i < n_items; i += blockDim.x) {
       const Work w = cta_item(g, lv, L0, cta, i);
       const RowPtr& rp = rows[w.r];
       const bool live = !w.dead && rp.ok[w.kind - 1] && rp.slot >= 0 && rp.slot < kSlotExtent;
       itab[i] = make_int4(live ? w.kind : 0, rp.slot, w.b, w.kp);
     }
-    __syncthreads();
-    if (warp >= kWarps) {
-      if (lane == 0) produce(p, n_items, itab, stages, bars, tags, warp - kWarps);
-      return;
-    }
   }
-
-  // register mode: this warp's first item in flight while the activation tables are built
+  __syncthreads();
+  if (kTma && warp >= kWarps) {
+    if (lane == 0) produce(p, n_items, itab, stages, bars, tags, warp - kWarps);
+    return;
+  }
   ItemRegs cur, nxt_it;
   Work wn = work_at(g, lv, L, cta, warp, 0);
   if (!kTma) load_item(p, wn, lane, rows, nxt_it);
-  {
-    int gl[kXPre], toff[kXPre];
-#pragma unroll
-    for (int j = 0; j < kXPre; ++j) {
-      const int tt = warp + j * kWarps;
-      const int m = tt / g.G1;
-      gl[j] = tt < nxt ? tt - m * g.G1 : -1;
-      toff[j] = tt < nxt ? m * (int)token_table_bytes(g.H) : 0;
-    }
-    prep_groups<kXPre>(xv, gl, toff, smem + p.off_tabs, g.H, lane);
-  }
-  for (int tt = warp + kXPre * kWarps; tt < nxt; tt += kWarps) {
-    const int m = tt / g.G1, gi = tt - m * g.G1;
-    const __nv_bfloat16* src = p.x + (int64_t)m * g.H + gi * kGroup + 4 * lane;
-    const float v[4] = {__bfloat162float(src[0]), __bfloat162float(src[1]), __bfloat162float(src[2]),
-                        __bfloat162float(src[3])};
-    prep_group_regs(v, gi, table_at(smem + p.off_tabs + (size_t)m * token_table_bytes(g.H), g.H), lane);
-  }
-  csync();
 
   // The warp's work list: its gate_up items, the phase switch, then unit by unit its down items (each unit
   // preceded by the unit's h tables and followed by the unit's y). Register mode: take the item whose loads
@@ -926,7 +961,7 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
   for (int t = 0; t < L.n1w; ++t) do_item(t);
   phase_switch(p, lv, cta, warp, lane, mail1, epoch);
   for (int q = 0; q < L.nu; ++q) {
-    unit_tables<kTma ? 6 : 2>(p, lv, q, warp, lane, smem, hbar);
+    unit_tables(p, lv, q, smem, hbar);
     for (int k = 0; k < L.n2w; ++k) do_item(L.n1w + q * L.n2w + k);
     csync();
     if (warp == 0) {                          // y of the unit: fixed-order sum of its top_k x K-part partials
@@ -942,8 +977,9 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
 
 // Workspace: 256 bytes of control words (grid barrier arrival count at 0 and generation at 128; both
 // only grow and are equal between calls, so zero-filling before the first call is all they need),
-// kMaxGrid hand-off flags (hold past generations + 1, never reset), then h [R][I] fp32 and the
-// split-block tail partials [R][2][I] fp32.
+// kMaxGrid hand-off flags (hold past generations + 1, never reset), then the down tables of the routed
+// rows [R][htab_bytes(I)] (2.25 I bytes each) and the split-block tail partials [R][2][I] fp32; the size
+// keeps 3 * I * 4 bytes per routed row, an upper bound of both.
 constexpr int kMaxGrid = 1024;
 size_t layer_workspace_bytes(int M, int H, int I, int top_k) {
   (void)H;
@@ -1084,16 +1120,15 @@ int launch_fused(const LayerArgs& a, int M, const void* x, const int32_t* ids, c
   p.off_mail1 = base + sp.tabs;
   p.off_mail2 = p.off_mail1 + sp.mail1;
   p.off_rows = p.off_mail2 + sp.mail2;
-  p.off_hstage = p.off_rows + sp.rows;
-  p.off_misc = p.off_hstage + sp.hstage;
+  p.off_misc = p.off_rows + sp.rows;
   p.off_live = p.off_misc + sp.misc;
   p.off_itab = p.off_live + sp.live;
   unsigned* ctl = static_cast<unsigned*>(a.workspace);
   p.bar_count = ctl;
   p.bar_gen = ctl + 32;
   p.hflags = ctl + 64;
-  p.hfin = reinterpret_cast<float*>(static_cast<char*>(a.workspace) + 256 + (size_t)kMaxGrid * 4);
-  p.hpart = p.hfin + (size_t)g.R * a.I;
+  p.htab = static_cast<unsigned char*>(a.workspace) + 256 + (size_t)kMaxGrid * 4;
+  p.hpart = reinterpret_cast<float*>(p.htab + (size_t)g.R * htab_bytes(a.I));
 
   auto kern = tma ? fused_layer_kernel<true> : fused_layer_kernel<false>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)total) != cudaSuccess)
