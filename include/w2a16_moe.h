@@ -146,7 +146,7 @@ int w2a16_moe_decode_layer_slots(const void* x, int M, int H, int I, int top_k,
  * start-up. It calls no cudaMalloc, cudaFree or allocating library routine. Its workspace is a fixed
  * array of W2A16_NOALLOC_SCRATCH_BYTES (4 MiB) inside the library that every GPU loading the library
  * holds until the process exits; layers needing more (w2a16_moe_layer_workspace_bytes(M, H, I, top_k)
- * > W2A16_NOALLOC_SCRATCH_BYTES; at I=1536, top-8 that is M > 28) return W2A16_ERR_WORKSPACE.
+ * > W2A16_NOALLOC_SCRATCH_BYTES; at I=1536, top-8 that is M > 146) return W2A16_ERR_WORKSPACE.
  * The first call on a device looks up that array's device address for the calling thread's current
  * device (which must own `stream`); make that first call before any stream capture. All calls share
  * the one array: calls that overlap on the GPU (different streams, or concurrent graph replays) race

@@ -127,16 +127,18 @@ __global__ void __launch_bounds__(256) int8_gemv_kernel(I8Params p) {
     for (int w = 0; w < kWarps; ++w) v += red[m][w][col];
     if (n < p.N) p.part[((int64_t)ks * p.M + (m0 + m)) * p.N + n] = v;
   }
-  __threadfence();
+  // Ticket: the CTA barrier orders every thread's partial before thread 0's acquire-release add, which
+  // publishes them and, in the CTA that takes the last ticket, orders the other slices' partials before
+  // its reads (after the second barrier). No full fences: they stall for microseconds under load.
   __syncthreads();
   if (threadIdx.x == 0) {
     unsigned* t = p.tickets + (int64_t)mz * gridDim.x + cb;
-    const unsigned prev = atomicAdd(t, 1u);
+    unsigned prev;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;\n" : "=r"(prev) : "l"(t) : "memory");
     is_last = (prev == (unsigned)(nslices - 1));
   }
   __syncthreads();
   if (!is_last) return;
-  __threadfence();
   for (int t = threadIdx.x; t < mt * 128; t += blockDim.x) {
     const int m = t >> 7, col = t & 127;
     const int n = cb * 128 + col;

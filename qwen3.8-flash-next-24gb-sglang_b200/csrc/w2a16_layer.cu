@@ -52,6 +52,23 @@ constexpr int kSlotExtent = 1 << 20;                         // slot ids the are
 constexpr unsigned kSpinLimit = 1u << 22;                    // polls before a wait gives up
 constexpr unsigned kWaitLimit = 1u << 17;                    // suspending mbarrier tries before a wait gives up
 
+// Division of a non-negative int below 2^31 by a divisor d >= 1 fixed at launch: q = (x * m) >> s with
+// l = ceil(log2 d), s = 31 + l, m = ceil(2^s / d) < 2^32 -- exact for every such x (the round-up method
+// for unsigned division by invariant integers, Granlund and Montgomery 1994).
+struct FDiv {
+  uint32_t m;
+  int s;
+};
+FDiv make_fdiv(int d) {
+  int l = 0;
+  while ((1ll << l) < d) ++l;
+  const int s = 31 + l;
+  return FDiv{(uint32_t)(((1ull << s) + (uint64_t)d - 1) / (uint64_t)d), s};
+}
+__device__ __forceinline__ int fdiv(int x, FDiv d) {
+  return (int)(((uint64_t)(uint32_t)x * d.m) >> d.s);
+}
+
 struct Geo {
   int M, H, I, top_k, R;
   int G1, G2;          // groups along K of gate_up (H/128) and down (I/128)
@@ -62,6 +79,7 @@ struct Geo {
   int grid;            // CTAs
   int max_range;       // max phase-1 items per CTA
   int max_units;       // max phase-2 units per CTA
+  FDiv d_kp1, d_nb1, d_row1, d_kp2, d_nb2, d_s2, d_topk, d_G1;   // row1 = nb1 * kp1 (items per row)
 };
 
 Geo make_geo(int M, int H, int I, int top_k, int grid_cap) {
@@ -77,6 +95,9 @@ Geo make_geo(int M, int H, int I, int top_k, int grid_cap) {
   if (g.grid < 1) g.grid = 1;
   g.max_range = (g.n1 + g.grid - 1) / g.grid;
   g.max_units = (g.u2 + g.grid - 1) / g.grid;
+  g.d_kp1 = make_fdiv(g.kp1); g.d_nb1 = make_fdiv(g.nb1); g.d_row1 = make_fdiv(g.nb1 * g.kp1);
+  g.d_kp2 = make_fdiv(g.kp2); g.d_nb2 = make_fdiv(g.nb2); g.d_s2 = make_fdiv(g.s2);
+  g.d_topk = make_fdiv(top_k); g.d_G1 = make_fdiv(g.G1);
   return g;
 }
 
@@ -93,7 +114,7 @@ __host__ __device__ __forceinline__ size_t htab_bytes(int I) {
 }
 
 struct SmemPlan {
-  size_t tabs, mail1, mail2, rows, misc, live, itab, total;
+  size_t tabs, mail1, mail2, rows, misc, live, total;
 };
 
 // Per routed row, resolved once per CTA: expert code / scale / zero-point bases of gate_up and down.
@@ -103,6 +124,7 @@ struct RowPtr {
   const uint8_t* z[2];
   int ok[2];
   int slot;      // arena slot of the row's expert (copy-engine mode)
+  float wt;      // routing weight
 };
 
 SmemPlan smem_plan(const Geo& g) {
@@ -116,8 +138,7 @@ SmemPlan smem_plan(const Geo& g) {
   s.misc = 64;                                                  // mbarrier, head counter, generation
   // LiveRows arrays and the live-row bit words
   s.live = ((size_t)(2 * g.R + g.M + g.max_units * g.top_k + (g.R + 31) / 32) * 4 + 15) & ~size_t(15);
-  s.itab = (size_t)(g.max_range + g.max_units * g.s2) * 16;     // the CTA's item descriptors (producers)
-  s.total = s.tabs + s.mail1 + s.mail2 + s.rows + s.misc + s.live + s.itab;
+  s.total = s.tabs + s.mail1 + s.mail2 + s.rows + s.misc + s.live;
   return s;
 }
 
@@ -135,12 +156,13 @@ struct FusedParams {
   float rsf;
   __nv_bfloat16* y;
   Geo geo;
-  size_t off_tabs, off_mail1, off_mail2, off_rows, off_misc, off_live, off_itab;
+  size_t off_tabs, off_mail1, off_mail2, off_rows, off_misc, off_live;
   unsigned* bar_count;   // grid barrier: arrivals (zero between calls)
   unsigned* bar_gen;     // grid barrier: generation, 128 bytes further
   unsigned char* htab;   // [R][htab_bytes(I)] down-projection activation tables of the routed rows
-  unsigned* hflags;      // [grid] generation + 1 once the CTA published the partial of its first h-block
-  float* hpart;          // [R][2 (gate, up)][I] partial sums of the tails of h-blocks split across two CTAs
+  // [grid][2 (gate, up)][32 columns] hand-off words: (epoch << 32) | float bits of the partial sums a CTA
+  // publishes for the tail of the h-block it shares with the previous CTA
+  unsigned long long* hand;
   unsigned* err;
 };
 
@@ -239,33 +261,33 @@ __device__ __forceinline__ WarpList warp_list(const Geo& g, const LiveRows& lv, 
 
 // Phase-2 item j of unit (token m, block b) -> its live row (or a dead slot).
 __device__ __forceinline__ void unit_row(const Geo& g, const LiveRows& lv, int m, int j, Work& w) {
-  w.jr = j / g.kp2;
+  w.jr = fdiv(j, g.d_kp2);
   w.kp = j - w.jr * g.kp2;
   w.dead = w.jr >= lv.tokcnt[m];
   w.r = m * g.top_k + (w.dead ? w.jr : lv.tokrow[m * g.top_k + w.jr]);
 }
 
-__device__ __forceinline__ Work work_at(const Geo& g, const LiveRows& lv, const WarpList& L, int cta, int warp,
-                                        int t) {
+// The warp's t-th gate_up item ...
+__device__ __forceinline__ Work work1(const Geo& g, const LiveRows& lv, const WarpList& L, int warp, int t) {
   Work w{};
-  if (t < L.n1w) {
-    const int i = L.a + warp + kWarps * t;
-    const int per_row = g.nb1 * g.kp1;
-    w.kind = 1;
-    const int rc = i / per_row;
-    w.r = lv.rowmap[rc];
-    const int rem = i - rc * per_row;
-    w.b = rem / g.kp1;
-    w.kp = rem - w.b * g.kp1;
-    w.slot = i - L.a;
-    w.seq = warp + kWarps * t;
-    return w;
-  }
-  const int t2 = t - L.n1w;
-  if (L.n2w == 0 || t2 >= L.nu * L.n2w) return w;
-  const int q = t2 / L.n2w, k = t2 - q * L.n2w;
+  const int i = L.a + warp + kWarps * t;
+  w.kind = 1;
+  const int rc = fdiv(i, g.d_row1);
+  w.r = lv.rowmap[rc];
+  const int rem = i - rc * (g.nb1 * g.kp1);
+  w.b = fdiv(rem, g.d_kp1);
+  w.kp = rem - w.b * g.kp1;
+  w.slot = i - L.a;
+  w.seq = warp + kWarps * t;
+  return w;
+}
+
+// ... and its k-th down item of unit q.
+__device__ __forceinline__ Work work2(const Geo& g, const LiveRows& lv, const WarpList& L, int cta, int warp, int q,
+                                     int k) {
+  Work w{};
   const int u = cta + g.grid * q, j = warp + kWarps * k;
-  const int m = u / g.nb2;
+  const int m = fdiv(u, g.d_nb2);
   w.kind = 2;
   w.b = u - m * g.nb2;
   unit_row(g, lv, m, j, w);
@@ -477,58 +499,82 @@ __device__ __forceinline__ Work cta_item(const Geo& g, const LiveRows& lv, const
     const int ii = L.a + i;
     const int per_row = g.nb1 * g.kp1;
     w.kind = 1;
-    const int rc = ii / per_row;
+    const int rc = fdiv(ii, g.d_row1);
     w.r = lv.rowmap[rc];
     const int rem = ii - rc * per_row;
-    w.b = rem / g.kp1;
+    w.b = fdiv(rem, g.d_kp1);
     w.kp = rem - w.b * g.kp1;
     return w;
   }
   const int i2 = i - L.range;
-  const int q = i2 / g.s2, j = i2 - q * g.s2;
-  const int u = cta + g.grid * q, m = u / g.nb2;
+  const int q = fdiv(i2, g.d_s2), j = i2 - q * g.s2;
+  const int u = cta + g.grid * q, m = fdiv(u, g.d_nb2);
   w.kind = 2;
   w.b = u - m * g.nb2;
   unit_row(g, lv, m, j, w);
   return w;
 }
 
-// The producers: lane 0 of producer warp pr streams items pr, pr + kProducers, ... of the CTA's order
-// through the ring (one issuing thread sustains only about a quarter of an SM's share of HBM bandwidth:
-// each arm-and-copy sequence has a long latency, so several threads issue side by side). The stage count
-// is a multiple of kProducers, so every stage has a single producer. Each item is one tensor copy of
-// codes (4 KB), one of scales and one of zero-point windows, completing on the stage's `full` barrier; a
-// stage is refilled once the warp that reduced it arrived on its `empty` barrier. Items of a
-// non-resident expert complete their phase on the arrival alone.
-__device__ void produce(const FusedParams& p, int n, const int4* itab, unsigned char* stages, uint32_t bars, int* tags,
-                        int pr) {
+// Copy descriptor of item i of the CTA's order: {kind (0 = nothing to copy), slot, block, K-part}.
+__device__ __forceinline__ int4 item_desc(const Geo& g, const LiveRows& lv, const WarpList& L0, int cta,
+                                          const RowPtr* rows, int i) {
+  const Work w = cta_item(g, lv, L0, cta, i);
+  const RowPtr& rp = rows[w.r];
+  const bool live = !w.dead && rp.ok[w.kind - 1] && rp.slot >= 0 && rp.slot < kSlotExtent;
+  return make_int4(live ? w.kind : 0, rp.slot, w.b, w.kp);
+}
+
+// The producers: producer warp pr streams items pr, pr + kProducers, ... of the CTA's order through the
+// ring (one issuing thread sustains only about a quarter of an SM's share of HBM bandwidth: each
+// arm-and-copy sequence has a long latency, so several threads issue side by side). The warp's lanes
+// decode the next 32 descriptors in parallel; lane 0 issues. The stage count is a multiple of kProducers,
+// so every stage has a single producer. Each item is one tensor copy of codes (4 KB), one of scales and
+// one of zero-point windows, completing on the stage's `full` barrier; a stage is refilled once the warp
+// that reduced it arrived on its `empty` barrier. Items of a non-resident expert complete their phase on
+// the arrival alone.
+__device__ void produce(const FusedParams& p, const LiveRows& lv, const RowPtr* rows, int cta, unsigned char* stages,
+                        uint32_t bars, int* tags, int pr, int lane) {
+  const Geo& g = p.geo;
+  const WarpList L0 = warp_list(g, lv, cta, 0);
+  const int n = L0.range + L0.nu * g.s2;
   const int ns = p.nstage;
   const bool hz = p.map13.has_zeros != 0;
   const bool aligned = (smem_u32(stages) & 127u) == 0;        // tensor copies land on 128-byte boundaries
-  if (!aligned) flag_error(p.err, 4u);
+  if (!aligned && lane == 0) flag_error(p.err, 4u);
+  int4 batch = make_int4(0, 0, 0, 0);
   int st = pr, round = 0;                                     // st = i % ns, round = i / ns
-  for (int i = pr; i < n; i += kProducers) {
-    const uint32_t full = bars + st * 8, empty = bars + (ns + st) * 8;
-    if (round > 0) mbar_wait(empty, (unsigned)(round - 1) & 1u, p.err);
-    // Tag the stage with the item it now holds. A warp waits for its item's tag before it waits on the
-    // stage's `full` phase: a stage is refilled by another warp's item, and without the tag a warp that
-    // runs ahead could take the still-pending previous fill's phase parity for its own.
-    st_volatile_shared(tags + st, i);
-    const int4 it = itab[i];                                  // {kind (0 = nothing to copy), slot, b, kp}
-    if (!aligned || it.x == 0) {
-      mbar_arrive(full);
-    } else {
-      const uint32_t dst = smem_u32(stages + (size_t)st * kStageBytes);
-      mbar_arrive_tx(full, (unsigned)(kScaleOff + 256 + (hz ? 64 : 0)));
-      const int zx = (8 * it.z) & ~15;                        // 16-byte aligned zero-point window
-      if (it.x == 1) {
-        tma_load_4d(dst, &p.tm[0], it.z * 32, 0, 16 * it.w, it.y, full);
-        tma_load_4d(dst + kScaleOff, &p.tm[1], it.z * 32, 0, 2 * it.w, it.y, full);
-        if (hz) tma_load_4d(dst + kZeroOff, &p.tm[2], zx, 0, 2 * it.w, it.y, full);
+  for (int t = 0, i = pr; i < n; ++t, i += kProducers) {
+    if ((t & 31) == 0) {
+      const int ii = i + kProducers * lane;
+      batch = ii < n ? item_desc(g, lv, L0, cta, rows, ii) : make_int4(0, 0, 0, 0);
+    }
+    int4 it;
+    it.x = __shfl_sync(0xffffffffu, batch.x, t & 31);
+    it.y = __shfl_sync(0xffffffffu, batch.y, t & 31);
+    it.z = __shfl_sync(0xffffffffu, batch.z, t & 31);
+    it.w = __shfl_sync(0xffffffffu, batch.w, t & 31);
+    if (lane == 0) {
+      const uint32_t full = bars + st * 8, empty = bars + (ns + st) * 8;
+      if (round > 0) mbar_wait(empty, (unsigned)(round - 1) & 1u, p.err);
+      // Tag the stage with the item it now holds. A warp waits for its item's tag before it waits on the
+      // stage's `full` phase: a stage is refilled by another warp's item, and without the tag a warp that
+      // runs ahead could take the still-pending previous fill's phase parity for its own.
+      st_volatile_shared(tags + st, i);
+      if (!aligned || it.x == 0) {
+        mbar_arrive(full);
       } else {
-        tma_load_3d(dst, &p.tm[3], it.z * 32, 32 * it.w, it.y, full);
-        tma_load_3d(dst + kScaleOff, &p.tm[4], it.z * 32, 4 * it.w, it.y, full);
-        if (hz) tma_load_3d(dst + kZeroOff, &p.tm[5], zx, 4 * it.w, it.y, full);
+        const uint32_t dst = smem_u32(stages + (size_t)st * kStageBytes);
+        mbar_arrive_tx(full, (unsigned)(kScaleOff + 256 + (hz ? 64 : 0)));
+        const int zx = (8 * it.z) & ~15;                      // 16-byte aligned zero-point window
+        if (it.x == 1) {
+          tma_load_4d(dst, &p.tm[0], it.z * 32, 0, 16 * it.w, it.y, full);
+          tma_load_4d(dst + kScaleOff, &p.tm[1], it.z * 32, 0, 2 * it.w, it.y, full);
+          if (hz) tma_load_4d(dst + kZeroOff, &p.tm[2], zx, 0, 2 * it.w, it.y, full);
+        } else {
+          tma_load_3d(dst, &p.tm[3], it.z * 32, 32 * it.w, it.y, full);
+          tma_load_3d(dst + kScaleOff, &p.tm[4], it.z * 32, 4 * it.w, it.y, full);
+          if (hz) tma_load_3d(dst + kZeroOff, &p.tm[5], zx, 4 * it.w, it.y, full);
+        }
       }
     }
     st += kProducers;
@@ -538,10 +584,11 @@ __device__ void produce(const FusedParams& p, int n, const int4* itab, unsigned 
     }
   }
   // every copy has landed before the producer leaves (the reducing warps wait on the same phases)
-  for (int st = pr; st < ns && st < n; st += kProducers) {
-    const int last = st + ((n - 1 - st) / ns) * ns;
-    mbar_wait(bars + st * 8, (unsigned)(last / ns) & 1u, p.err);
-  }
+  if (lane == 0)
+    for (int s0 = pr; s0 < ns && s0 < n; s0 += kProducers) {
+      const int last = s0 + ((n - 1 - s0) / ns) * ns;
+      mbar_wait(bars + s0 * 8, (unsigned)(last / ns) & 1u, p.err);
+    }
 }
 
 // 4 columns x 1 group of this lane from a ring stage. Gate_up stages hold 256-byte word rows (32 gate |
@@ -581,7 +628,7 @@ __device__ __forceinline__ void process_work(const FusedParams& p, const Work& w
   if (lm.valid) {
     const bool sbf = p.scale_bf16 != 0, hz = rp.z[mi] != nullptr;
     if (k1) {
-      const XTable tb = table_at(tabs + (size_t)(w.r / g.top_k) * token_table_bytes(g.H), g.H);
+      const XTable tb = table_at(tabs + (size_t)fdiv(w.r, g.d_topk) * token_table_bytes(g.H), g.H);
       if (kTma) dot_stage<1>(stage, w, lane, tb, lm.gl, sbf, hz, v);
       else dot_regs<1>(it, tb, lm.gl, sbf, hz, v);
     } else {
@@ -601,7 +648,7 @@ __device__ __forceinline__ void process_work(const FusedParams& p, const Work& w
       v[c] += __shfl_xor_sync(0xffffffffu, v[c], 8);
       v[c] += __shfl_xor_sync(0xffffffffu, v[c], 16);
     }
-    const float wr = p.topk_w[w.r];
+    const float wr = rows[w.r].wt;
     if (lane < 8)
       *reinterpret_cast<float4*>(mail2 + (size_t)w.slot * 32 + lane * 4) =
           make_float4(v[0] * wr, v[1] * wr, v[2] * wr, v[3] * wr);
@@ -617,6 +664,14 @@ __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* ptr) {
 __device__ __forceinline__ void st_release_u32(unsigned* ptr, unsigned v) {
   asm volatile("st.release.gpu.global.u32 [%0], %1;\n" ::"l"(ptr), "r"(v) : "memory");
 }
+__device__ __forceinline__ void st_relaxed_u64(unsigned long long* ptr, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;\n" ::"l"(ptr), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* ptr) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];\n" : "=l"(v) : "l"(ptr) : "memory");
+  return v;
+}
 
 // All CTAs arrive; thread 0 of each CTA calls this with `base`, the generation word it read at kernel
 // entry. The arrival count only grows, and the generation word holds the count every completed call
@@ -624,9 +679,10 @@ __device__ __forceinline__ void st_release_u32(unsigned* ptr, unsigned v) {
 // base + ncta (signed distance, so the words may wrap). CTA 0 then stores that value as the new
 // generation, which the next call reads at entry; no CTA of this call reads it after its own entry, and
 // the grid size may differ from call to call. The count sits 128 bytes away from the generation. Gives
-// up after kSpinLimit polls (error bit 1).
+// up after kSpinLimit polls (error bit 1). The caller brackets it with CTA barriers: the release add then
+// publishes every write the CTA made before the first one, and the acquire load orders every read the
+// CTA makes after the second one (no full fences, which stall for microseconds under the weight stream).
 __device__ void grid_barrier(unsigned* count, unsigned* gen, unsigned base, unsigned ncta, unsigned* err) {
-  __threadfence();
   asm volatile("red.release.gpu.global.add.u32 [%0], 1;\n" ::"l"(count) : "memory");
   const unsigned target = base + ncta;
   unsigned it = 0;
@@ -637,7 +693,6 @@ __device__ void grid_barrier(unsigned* count, unsigned* gen, unsigned base, unsi
     }
   }
   if (blockIdx.x == 0) st_release_u32(gen, target);
-  __threadfence();
 }
 
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, unsigned bytes, uint32_t bar) {
@@ -648,26 +703,22 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, unsigned
 
 // Items [0, head_k) of a CTA's range are the tail of an h-block that began in the previous CTA. Once
 // they are reduced (round 0 of the item loop), the warp that completes them sums their partials and
-// publishes the (gate, up) tail sums with a flag, so the previous CTA can finish that block before the
-// grid barrier.
-__device__ void publish_head(const FusedParams& p, const LiveRows& lv, const WarpList& L, int cta, int lane,
-                             const float* mail1, int head_k, unsigned epoch) {
-  const Geo& g = p.geo;
-  const int blk = L.a / g.kp1;
-  const int rc = blk / g.nb1, hb = blk - rc * g.nb1;
-  const int r = lv.rowmap[rc];
-  const size_t col = (size_t)hb * 32 + lane;
-  __syncwarp();                                               // lane 0's acquire of the count covers the warp
+// publishes the (gate, up) tail sums of its 32 columns, so the previous CTA can finish that block before
+// the grid barrier. Each sum travels with the call's epoch in one 64-bit word (single-copy atomic), so
+// the reader needs no flag and neither side a fence -- a release store here would stall the warp until
+// its earlier stores drain, for microseconds under the weight stream.
+__device__ void publish_head(const FusedParams& p, int cta, int lane, const float* mail1, int head_k,
+                             unsigned epoch) {
+  __syncwarp();                                               // the warps' partials are in place (counter)
   float gs = 0.f, us = 0.f;
   for (int i = 0; i < head_k; ++i) {
     gs += mail1[(size_t)i * 64 + lane];
     us += mail1[(size_t)i * 64 + 32 + lane];
   }
-  p.hpart[((size_t)r * 2) * g.I + col] = gs;
-  p.hpart[((size_t)r * 2 + 1) * g.I + col] = us;
-  __threadfence();
-  __syncwarp();
-  if (lane == 0) st_release_u32(p.hflags + cta, epoch);
+  const unsigned long long tag = (unsigned long long)epoch << 32;
+  unsigned long long* slot = p.hand + (size_t)cta * 64;
+  st_relaxed_u64(slot + lane, tag | __float_as_uint(gs));
+  st_relaxed_u64(slot + 32 + lane, tag | __float_as_uint(us));
 }
 
 // Count one reduced head item; the warp that reduces the last of them publishes the tail sums.
@@ -680,7 +731,7 @@ __device__ __forceinline__ void head_item_done(const FusedParams& p, const LiveR
     last = atomicAdd(counter, 1u) == (unsigned)head_k - 1u;
     __threadfence_block();
   }
-  if (__shfl_sync(0xffffffffu, last, 0)) publish_head(p, lv, L, cta, lane, mail1, head_k, epoch);
+  if (__shfl_sync(0xffffffffu, last, 0)) publish_head(p, cta, lane, mail1, head_k, epoch);
 }
 
 // Phase switch, entered by every warp of the CTA once its gate_up items are done. (1) h of every h-block
@@ -696,7 +747,7 @@ __device__ __forceinline__ void phase_switch(const FusedParams& p, const LiveRow
   {
     const long long a = L.a, b = L.b;
     if (b > a) {
-      const int blk0 = (int)(a / g.kp1), blk1 = (int)((b - 1) / g.kp1);
+      const int blk0 = fdiv((int)a, g.d_kp1), blk1 = fdiv((int)(b - 1), g.d_kp1);
       for (int blk = blk0 + warp; blk <= blk1; blk += kWarps) {
         const long long i0 = (long long)blk * g.kp1, i1 = i0 + g.kp1;
         if (i0 < a) continue;                                 // finished by the previous CTA
@@ -706,27 +757,28 @@ __device__ __forceinline__ void phase_switch(const FusedParams& p, const LiveRow
           gs += mail1[(size_t)(i - a) * 64 + lane];
           us += mail1[(size_t)(i - a) * 64 + 32 + lane];
         }
-        const int rc = blk / g.nb1, hb = blk - rc * g.nb1;
+        const int rc = fdiv(blk, g.d_nb1), hb = blk - rc * g.nb1;
         const int r = lv.rowmap[rc];
-        const size_t col = (size_t)hb * 32 + lane;
-        if (i1 > b) {                                         // tail published by the next CTA
-          if (lane == 0) {
-            unsigned it = 0;
-            while (ld_acquire_u32(p.hflags + cta + 1) != epoch) {
-              if (++it > kSpinLimit) {
-                flag_error(p.err, 2u);
-                break;
-              }
-              __nanosleep(32);
+        if (i1 > b) {                                         // tail published by the next CTA (bounded wait)
+          const unsigned long long* slot = p.hand + (size_t)(cta + 1) * 64;
+          unsigned long long vg = 0, vu = 0;
+          unsigned it = 0;
+          while (true) {
+            vg = ld_relaxed_u64(slot + lane);
+            vu = ld_relaxed_u64(slot + 32 + lane);
+            if ((unsigned)(vg >> 32) == epoch && (unsigned)(vu >> 32) == epoch) break;
+            if (++it > kSpinLimit) {
+              flag_error(p.err, 2u);
+              break;
             }
+            __nanosleep(32);
           }
           __syncwarp();
-          gs += __ldcg(p.hpart + ((size_t)r * 2) * g.I + col);
-          us += __ldcg(p.hpart + ((size_t)r * 2 + 1) * g.I + col);
+          gs += __uint_as_float((unsigned)vg);
+          us += __uint_as_float((unsigned)vu);
         }
         htab_block(p.htab + (size_t)r * htab_bytes(g.I), g.I, hb, silu(gs) * us, lane);
       }
-      __threadfence();
     }
   }
   csync();
@@ -779,16 +831,28 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
   // the barrier generation of this call (read at entry; the count reaches it before any CTA of this call
   // can pass the barrier)
   const unsigned gen_entry = threadIdx.x == 0 ? ld_acquire_u32(p.bar_gen) : 0u;
-  // routing first: expert bases of every routed row, resolved once per CTA; the loads' latency overlaps
-  // the barrier setup and the activation tables below
-  for (int r = threadIdx.x; r < g.R; r += blockDim.x) {
+  int* rowmap = reinterpret_cast<int*>(smem + p.off_live);
+  int* tokrow = rowmap + g.R;
+  int* tokcnt = tokrow + g.R;
+  int* slotrow = tokcnt + g.M;
+  unsigned* livebits = reinterpret_cast<unsigned*>(slotrow + g.max_units * g.top_k);
+  // Routing first: expert bases of every routed row, resolved once per CTA -- by warp 0 alone when the
+  // rows fit one warp (it compacts them right after, with no CTA barrier in between), else by every thread.
+  const bool one_warp = g.R <= 32;
+  auto resolve_row = [&](int r) {
     RowPtr rp;
     const int e = p.ids[r];
     rp.ok[0] = p.map13.resolve(e, rp.w[0], rp.s[0], rp.z[0], p.err);
     rp.ok[1] = p.map2.resolve(e, rp.w[1], rp.s[1], rp.z[1], p.err);
     rp.slot = (p.map13.slots != nullptr && e >= 0 && e < p.map13.E) ? p.map13.slots[e] : -1;
+    rp.wt = p.topk_w[r];
     if (kTma && rp.slot >= kSlotExtent) flag_error(p.err, 1u);
     rows[r] = rp;
+  };
+  if (one_warp) {
+    if (warp == 0 && lane < g.R) resolve_row(lane);
+  } else {
+    for (int r = threadIdx.x; r < g.R; r += blockDim.x) resolve_row(r);
   }
   if (!kTma) {
     // Start the whole layer's weight stream: this CTA's 1/grid share of every routed row's six arrays.
@@ -812,28 +876,28 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
       if (len > 0)
         asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(base + start), "r"((unsigned)len) : "memory");
     }
-  } else {
-    if (threadIdx.x < 2 * p.nstage) {
-      mbar_init(bars + threadIdx.x * 8, 1);                   // full[0..ns), then empty[0..ns)
-      asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
-      if (threadIdx.x < p.nstage) tags[threadIdx.x] = -1;
+  } else if (warp >= kWarps) {
+    // producer warps: ring barriers and stage tags, and the tensor maps into the descriptor cache
+    const int pt = threadIdx.x - kThreads;
+    for (int b = pt; b < 2 * p.nstage; b += 32 * kProducers) {
+      mbar_init(bars + b * 8, 1);                             // full[0..ns), then empty[0..ns)
+      if (b < p.nstage) tags[b] = -1;
     }
-    // the producers' tensor maps into the descriptor cache before their first copies (maps of absent
-    // zero-point arrays are not encoded and are skipped)
-    if (warp == kWarps && lane < 6 && (p.map13.has_zeros || (lane != 2 && lane != 5)))
-      asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&p.tm[lane])) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    if (pt < 6 && (p.map13.has_zeros || (pt != 2 && pt != 5)))
+      asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&p.tm[pt])) : "memory");
   }
 
-  // activation tables of the M rows of x (no dependence on the routing)
-  if (warp < kWarps) {
-    const int nxt = g.M * g.G1;
-    constexpr int kXPre = 4;
+  // activation tables of the M rows of x (no dependence on the routing), by reducing warps 1..15
+  if (warp >= 1 && warp < kWarps) {
+    constexpr int kXW = kWarps - 1, kXPre = 4;
+    const int xw = warp - 1, nxt = g.M * g.G1;
     float xv[kXPre][4];
     int gl[kXPre], toff[kXPre];
 #pragma unroll
     for (int j = 0; j < kXPre; ++j) {
-      const int t = warp + j * kWarps;
-      const int m = t / g.G1, gi = t - m * g.G1;
+      const int t = xw + j * kXW;
+      const int m = fdiv(t, g.d_G1), gi = t - m * g.G1;
       xv[j][0] = xv[j][1] = xv[j][2] = xv[j][3] = 0.f;
       gl[j] = -1;
       toff[j] = 0;
@@ -847,23 +911,19 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
       }
     }
     prep_groups<kXPre>(xv, gl, toff, smem + p.off_tabs, g.H, lane);
-    for (int tt = warp + kXPre * kWarps; tt < nxt; tt += kWarps) {
-      const int m = tt / g.G1, gi = tt - m * g.G1;
+    for (int tt = xw + kXPre * kXW; tt < nxt; tt += kXW) {
+      const int m = fdiv(tt, g.d_G1), gi = tt - m * g.G1;
       const __nv_bfloat16* src = p.x + (int64_t)m * g.H + gi * kGroup + 4 * lane;
       const float v[4] = {__bfloat162float(src[0]), __bfloat162float(src[1]), __bfloat162float(src[2]),
                           __bfloat162float(src[3])};
       prep_group_regs(v, gi, table_at(smem + p.off_tabs + (size_t)m * token_table_bytes(g.H), g.H), lane);
     }
   }
-  int* rowmap = reinterpret_cast<int*>(smem + p.off_live);
-  int* tokrow = rowmap + g.R;
-  int* tokcnt = tokrow + g.R;
-  int* slotrow = tokcnt + g.M;
-  unsigned* livebits = reinterpret_cast<unsigned*>(slotrow + g.max_units * g.top_k);
-  __syncthreads();
-  // Live routed rows (both experts resolve), compacted by one warp with ballots: rowmap in routing order,
+  if (!one_warp) __syncthreads();
+  // Live routed rows (both experts resolve), compacted by warp 0 with ballots: rowmap in routing order,
   // and per token its live rows' positions within its top_k.
   if (warp == 0) {
+    __syncwarp();
     int nl = 0;
     for (int c0 = 0; c0 < g.R; c0 += 32) {
       const int r = c0 + lane;
@@ -894,38 +954,20 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
   }
   __syncthreads();
   const LiveRows lv{rowmap, tokrow, tokcnt, slotrow, (int)misc[4], (int)misc[5]};
-  for (int idx = threadIdx.x; idx < g.max_units * g.top_k; idx += blockDim.x) {   // rows of the CTA's down units
-    const int q = idx / g.top_k, jr = idx - q * g.top_k, u = cta + g.grid * q;
-    int row = -1;
-    if (u < g.u2) {
-      const int m = u / g.nb2;
-      if (jr < tokcnt[m]) row = m * g.top_k + tokrow[m * g.top_k + jr];
-    }
-    slotrow[idx] = row;
-  }
-  const WarpList L = warp_list(g, lv, cta, warp < kWarps ? warp : 0);
-  const int total = L.total();
-  int n_items = 0;
-  int4* itab = reinterpret_cast<int4*>(smem + p.off_itab);
-  if (kTma) {
-    // descriptors of the CTA's items in ring order, built once in parallel for the producers
-    const WarpList L0 = warp_list(g, lv, cta, 0);
-    n_items = L0.range + L0.nu * g.s2;
-    for (int i = threadIdx.x; i < n_items; i += blockDim.x) {
-      const Work w = cta_item(g, lv, L0, cta, i);
-      const RowPtr& rp = rows[w.r];
-      const bool live = !w.dead && rp.ok[w.kind - 1] && rp.slot >= 0 && rp.slot < kSlotExtent;
-      itab[i] = make_int4(live ? w.kind : 0, rp.slot, w.b, w.kp);
-    }
-  }
-  __syncthreads();
   if (kTma && warp >= kWarps) {
-    if (lane == 0) produce(p, n_items, itab, stages, bars, tags, warp - kWarps);
+    produce(p, lv, rows, cta, stages, bars, tags, warp - kWarps, lane);
     return;
   }
-  ItemRegs cur, nxt_it;
-  Work wn = work_at(g, lv, L, cta, warp, 0);
-  if (!kTma) load_item(p, wn, lane, rows, nxt_it);
+  const WarpList L = warp_list(g, lv, cta, warp);
+  for (int idx = threadIdx.x; idx < g.max_units * g.top_k; idx += kThreads) {   // rows of the CTA's down units
+    const int q = fdiv(idx, g.d_topk), jr = idx - q * g.top_k, u = cta + g.grid * q;
+    int row = -1;
+    if (u < g.u2) {
+      const int m = fdiv(u, g.d_nb2);
+      if (jr < tokcnt[m]) row = m * g.top_k + tokrow[m * g.top_k + jr];
+    }
+    slotrow[idx] = row;                    // read after the phase switch's barriers
+  }
 
   // The warp's work list: its gate_up items, the phase switch, then unit by unit its down items (each unit
   // preceded by the unit's h tables and followed by the unit's y). Register mode: take the item whose loads
@@ -933,9 +975,23 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
   // release the stage.
   const unsigned epoch = misc[3] + 1u;
   const int head_k = L.a % g.kp1 ? min(g.kp1 - L.a % g.kp1, L.range) : 0;   // items finishing a shared block
-  auto do_item = [&](int t) {
+  const int total = L.total();
+  auto item_at = [&](int t) -> Work {                         // register mode look-ahead only
+    if (t < L.n1w) return work1(g, lv, L, warp, t);
+    const int t2 = t - L.n1w;
+    if (L.n2w == 0 || t2 >= L.nu * L.n2w) return Work{};
+    const int q = t2 / L.n2w;
+    return work2(g, lv, L, cta, warp, q, t2 - q * L.n2w);
+  };
+  ItemRegs cur, nxt_it;
+  Work wn{};
+  if (!kTma) {
+    wn = item_at(0);
+    load_item(p, wn, lane, rows, nxt_it);
+  }
+  int tr = 0;                                                 // register mode: flat index of the item
+  auto do_item = [&](const Work& w) {
     if (kTma) {
-      const Work w = work_at(g, lv, L, cta, warp, t);
       const int st = w.seq % p.nstage;
       if (lane == 0) {
         wait_tag(tags, st, w.seq, p.err);
@@ -949,8 +1005,8 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
     } else {
       const Work wc = wn;
       cur = nxt_it;
-      if (t + 1 < total) {
-        wn = work_at(g, lv, L, cta, warp, t + 1);
+      if (++tr < total) {
+        wn = item_at(tr);
         load_item(p, wn, lane, rows, nxt_it);
       }
       process_work<false>(p, wc, lane, cur, nullptr, smem, mail1, mail2, rows);
@@ -958,14 +1014,14 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
       if (wc.kind == 1 && wc.slot < head_k) head_item_done(p, lv, L, cta, lane, mail1, head_k, epoch, misc + 2);
     }
   };
-  for (int t = 0; t < L.n1w; ++t) do_item(t);
+  for (int t = 0; t < L.n1w; ++t) do_item(work1(g, lv, L, warp, t));
   phase_switch(p, lv, cta, warp, lane, mail1, epoch);
   for (int q = 0; q < L.nu; ++q) {
     unit_tables(p, lv, q, smem, hbar);
-    for (int k = 0; k < L.n2w; ++k) do_item(L.n1w + q * L.n2w + k);
+    for (int k = 0; k < L.n2w; ++k) do_item(work2(g, lv, L, cta, warp, q, k));
     csync();
     if (warp == 0) {                          // y of the unit: fixed-order sum of its top_k x K-part partials
-      const int u = cta + g.grid * q, m = u / g.nb2, b = u - m * g.nb2;
+      const int u = cta + g.grid * q, m = fdiv(u, g.d_nb2), b = u - m * g.nb2;
       float acc = 0.f;
       for (int j = 0; j < g.s2; ++j) acc += mail2[(size_t)j * 32 + lane];
       p.y[(int64_t)m * g.H + b * 32 + lane] = __float2bfloat16(acc * p.rsf);
@@ -977,15 +1033,15 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
 
 // Workspace: 256 bytes of control words (grid barrier arrival count at 0 and generation at 128; both
 // only grow and are equal between calls, so zero-filling before the first call is all they need),
-// kMaxGrid hand-off flags (hold past generations + 1, never reset), then the down tables of the routed
-// rows [R][htab_bytes(I)] (2.25 I bytes each) and the split-block tail partials [R][2][I] fp32; the size
-// keeps 3 * I * 4 bytes per routed row, an upper bound of both.
-constexpr int kMaxGrid = 1024;
+// kMaxGrid x 512 bytes of hand-off words (tagged with past epochs, never reset; zero qualifies), then the
+// down tables of the routed rows [R][htab_bytes(I)] (2.25 I bytes each).
+constexpr int kMaxGrid = 256;
+constexpr size_t kHandBytes = (size_t)kMaxGrid * 64 * 8;
 size_t layer_workspace_bytes(int M, int H, int I, int top_k) {
   (void)H;
-  const size_t head = 256 + (size_t)kMaxGrid * 4;
+  const size_t head = 256 + kHandBytes;
   if (M <= 0 || I <= 0 || top_k <= 0) return head;
-  return head + (size_t)M * top_k * 3 * (size_t)I * 4;
+  return head + (size_t)M * top_k * htab_bytes(I);
 }
 
 namespace {
@@ -1122,13 +1178,11 @@ int launch_fused(const LayerArgs& a, int M, const void* x, const int32_t* ids, c
   p.off_rows = p.off_mail2 + sp.mail2;
   p.off_misc = p.off_rows + sp.rows;
   p.off_live = p.off_misc + sp.misc;
-  p.off_itab = p.off_live + sp.live;
   unsigned* ctl = static_cast<unsigned*>(a.workspace);
   p.bar_count = ctl;
   p.bar_gen = ctl + 32;
-  p.hflags = ctl + 64;
-  p.htab = static_cast<unsigned char*>(a.workspace) + 256 + (size_t)kMaxGrid * 4;
-  p.hpart = reinterpret_cast<float*>(p.htab + (size_t)g.R * htab_bytes(a.I));
+  p.hand = reinterpret_cast<unsigned long long*>(static_cast<unsigned char*>(a.workspace) + 256);
+  p.htab = static_cast<unsigned char*>(a.workspace) + 256 + kHandBytes;
 
   auto kern = tma ? fused_layer_kernel<true> : fused_layer_kernel<false>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)total) != cudaSuccess)

@@ -18,7 +18,7 @@
 namespace {
 
 // Zero-initialised at module load. The layer kernels need their two barrier words equal on entry and
-// leave them equal on exit, and their hand-off flags below the next generation (zero qualifies); the rest
+// leave them equal on exit, and their hand-off words tagged with no future epoch (zero qualifies); the rest
 // of the array (the SiLU*mul activations and partial sums) is overwritten by every call.
 __device__ __align__(256) unsigned char g_noalloc_scratch[W2A16_NOALLOC_SCRATCH_BYTES];
 

@@ -26,8 +26,8 @@ _WS = {}
 
 def layer_workspace(device: torch.device, nbytes: int) -> torch.Tensor:
     """Per-device workspace (uint8, zero-filled on creation, grown on demand). The layer kernels leave
-    its control words consistent after every call (barrier count equal to its generation, hand-off flags
-    below the next generation), so it is reused without clearing."""
+    its control words consistent after every call (barrier count equal to its generation, hand-off words
+    tagged with past calls' epochs), so it is reused without clearing."""
     key = (device.type, device.index)
     t = _WS.get(key)
     if t is None or t.numel() < nbytes:
