@@ -254,6 +254,15 @@ struct ExpertMap {
     }
     return true;
   }
+
+  // Arena form with the slot of expert e already looked up (e in [0, E) checked by the caller).
+  __device__ __forceinline__ bool resolve_slot(int sl, const uint32_t*& w, const char*& s, const uint8_t*& z) const {
+    if (sl < 0) return false;
+    w = reinterpret_cast<const uint32_t*>(wbase + (int64_t)sl * wstride);
+    s = sbase + (int64_t)sl * sstride;
+    z = has_zeros ? reinterpret_cast<const uint8_t*>(zbase + (int64_t)sl * zstride) : nullptr;
+    return true;
+  }
 };
 
 __device__ __forceinline__ float load_scale(const char* sptr, int64_t idx, bool bf16) {

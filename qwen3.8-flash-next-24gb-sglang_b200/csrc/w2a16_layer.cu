@@ -39,6 +39,7 @@ namespace {
 constexpr int kThreads = 512;                                // reducing warps (both modes)
 constexpr int kWarps = kThreads / 32;
 constexpr int kProducers = 4;                                // producer warps (copy-engine mode)
+constexpr int kIssuers = 2 * kProducers;                     // issuing threads: lanes 0 and 1 of each
 constexpr int kTmaThreads = kThreads + 32 * kProducers;
 // Copy-engine mode: one stage of the shared-memory ring holds one item -- codes at 0 (4 KB: 16 word rows
 // x [32 gate | 32 up] columns, or 32 word rows x 32 columns), scales at 4096 (256 B), zero-point windows
@@ -46,7 +47,7 @@ constexpr int kTmaThreads = kThreads + 32 * kProducers;
 constexpr int kStageBytes = 4480;
 constexpr int kScaleOff = 4096;
 constexpr int kZeroOff = 4352;
-constexpr int kMinStages = 16, kMaxStages = 48;             // multiples of kProducers
+constexpr int kMinStages = 16, kMaxStages = 48;             // multiples of kIssuers
 constexpr int kSlotExtent = 1 << 20;                         // slot ids the arena tensor maps accept
 
 constexpr unsigned kSpinLimit = 1u << 22;                    // polls before a wait gives up
@@ -80,6 +81,7 @@ struct Geo {
   int max_range;       // max phase-1 items per CTA
   int max_units;       // max phase-2 units per CTA
   FDiv d_kp1, d_nb1, d_row1, d_kp2, d_nb2, d_s2, d_topk, d_G1;   // row1 = nb1 * kp1 (items per row)
+  int stab;            // slot-table entries staged in shared memory (0: looked up in global memory)
 };
 
 Geo make_geo(int M, int H, int I, int top_k, int grid_cap) {
@@ -114,8 +116,18 @@ __host__ __device__ __forceinline__ size_t htab_bytes(int I) {
 }
 
 struct SmemPlan {
-  size_t tabs, mail1, mail2, rows, misc, live, total;
+  size_t tabs, mail1, mail2, rows, misc, live, slots, preg, total;
 };
+constexpr int kMaxStagedSlots = 2048;                        // slot tables up to 8 KB are staged
+constexpr int kMaxPrivSlots = 512;                           // producers keep private copies up to 2 KB
+
+// Copy-engine producers route privately (no hand-over from warp 0) when the routed rows fit one warp and
+// the slot table is staged and small: region per producer warp = slot, rowmap, tokrow, tokcnt [32 each]
+// and the slot table.
+__host__ __device__ __forceinline__ bool private_routing(const Geo& g) {
+  return g.R <= 32 && g.stab > 0 && g.stab <= kMaxPrivSlots;
+}
+__host__ __device__ __forceinline__ int preg_ints(const Geo& g) { return (128 + g.stab + 3) & ~3; }
 
 // Per routed row, resolved once per CTA: expert code / scale / zero-point bases of gate_up and down.
 struct RowPtr {
@@ -138,7 +150,9 @@ SmemPlan smem_plan(const Geo& g) {
   s.misc = 64;                                                  // mbarrier, head counter, generation
   // LiveRows arrays and the live-row bit words
   s.live = ((size_t)(2 * g.R + g.M + g.max_units * g.top_k + (g.R + 31) / 32) * 4 + 15) & ~size_t(15);
-  s.total = s.tabs + s.mail1 + s.mail2 + s.rows + s.misc + s.live;
+  s.slots = ((size_t)g.stab * 4 + 15) & ~size_t(15);
+  s.preg = private_routing(g) ? (size_t)kProducers * preg_ints(g) * 4 : 0;   // (copy-engine mode only)
+  s.total = s.tabs + s.mail1 + s.mail2 + s.rows + s.misc + s.live + s.slots + s.preg;
   return s;
 }
 
@@ -156,7 +170,7 @@ struct FusedParams {
   float rsf;
   __nv_bfloat16* y;
   Geo geo;
-  size_t off_tabs, off_mail1, off_mail2, off_rows, off_misc, off_live;
+  size_t off_tabs, off_mail1, off_mail2, off_rows, off_misc, off_live, off_slots, off_preg;
   unsigned* bar_count;   // grid barrier: arrivals (zero between calls)
   unsigned* bar_gen;     // grid barrier: generation, 128 bytes further
   unsigned char* htab;   // [R][htab_bytes(I)] down-projection activation tables of the routed rows
@@ -204,8 +218,12 @@ __device__ __forceinline__ void htab_block(unsigned char* tab, int I, int hb, fl
   }
 }
 
-// Barrier of the 512 reducing threads only (the producer warp of copy-engine mode never joins).
+// Barrier of the 512 reducing threads only (the producer warps of copy-engine mode never join).
 __device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;\n" ::"n"(kThreads) : "memory"); }
+// Prologue hand-overs of copy-engine mode: warp 0 -> producer warps once the routing is compacted
+// (barrier 2), producer warps -> reducing warps once the ring barriers exist (barrier 3).
+__device__ __forceinline__ void bar_arrive(int id, int n) { asm volatile("bar.arrive %0, %1;\n" ::"r"(id), "r"(n) : "memory"); }
+__device__ __forceinline__ void bar_wait(int id, int n) { asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(n) : "memory"); }
 
 
 // One entry of a warp's work list.
@@ -515,45 +533,53 @@ __device__ __forceinline__ Work cta_item(const Geo& g, const LiveRows& lv, const
   return w;
 }
 
-// Copy descriptor of item i of the CTA's order: {kind (0 = nothing to copy), slot, block, K-part}.
+// Copy descriptor of item i of the CTA's order: {kind (0 = nothing to copy), slot, block, K-part};
+// slot_of(r, kind) = arena slot of routed row r's expert for that projection, -1 when it does not resolve.
+template <class SlotOf>
 __device__ __forceinline__ int4 item_desc(const Geo& g, const LiveRows& lv, const WarpList& L0, int cta,
-                                          const RowPtr* rows, int i) {
+                                          SlotOf slot_of, int i) {
   const Work w = cta_item(g, lv, L0, cta, i);
-  const RowPtr& rp = rows[w.r];
-  const bool live = !w.dead && rp.ok[w.kind - 1] && rp.slot >= 0 && rp.slot < kSlotExtent;
-  return make_int4(live ? w.kind : 0, rp.slot, w.b, w.kp);
+  const int sl = w.dead ? -1 : slot_of(w.r, w.kind);
+  const bool live = sl >= 0 && sl < kSlotExtent;
+  return make_int4(live ? w.kind : 0, sl, w.b, w.kp);
 }
 
-// The producers: producer warp pr streams items pr, pr + kProducers, ... of the CTA's order through the
-// ring (one issuing thread sustains only about a quarter of an SM's share of HBM bandwidth: each
-// arm-and-copy sequence has a long latency, so several threads issue side by side). The warp's lanes
-// decode the next 32 descriptors in parallel; lane 0 issues. The stage count is a multiple of kProducers,
-// so every stage has a single producer. Each item is one tensor copy of codes (4 KB), one of scales and
-// one of zero-point windows, completing on the stage's `full` barrier; a stage is refilled once the warp
-// that reduced it arrived on its `empty` barrier. Items of a non-resident expert complete their phase on
-// the arrival alone.
-__device__ void produce(const FusedParams& p, const LiveRows& lv, const RowPtr* rows, int cta, unsigned char* stages,
+// The producers: issuing thread k (lane k / kProducers of producer warp k % kProducers) streams items
+// k, k + kIssuers, ... of the CTA's order through the ring. One issuing thread sustains only about an
+// eighth of an SM's share of HBM bandwidth (each arm-and-copy sequence has a long latency), so several
+// issue side by side; two lanes of one warp issue in the same instructions. The warp's lanes decode its
+// next 32 descriptors in parallel. The stage count is a multiple of kIssuers, so every stage has a single
+// issuer. Each item is one tensor copy of codes (4 KB), one of scales and one of zero-point windows,
+// completing on the stage's `full` barrier; a stage is refilled once the warp that reduced it arrived on
+// its `empty` barrier. Items of a non-resident expert complete their phase on the arrival alone.
+template <class SlotOf>
+__device__ void produce(const FusedParams& p, const LiveRows& lv, SlotOf slot_of, int cta, unsigned char* stages,
                         uint32_t bars, int* tags, int pr, int lane) {
   const Geo& g = p.geo;
   const WarpList L0 = warp_list(g, lv, cta, 0);
   const int n = L0.range + L0.nu * g.s2;
+  const int nw = n > pr ? (n - pr + kProducers - 1) / kProducers : 0;   // items of this warp: pr + kProducers*j
   const int ns = p.nstage;
   const bool hz = p.map13.has_zeros != 0;
   const bool aligned = (smem_u32(stages) & 127u) == 0;        // tensor copies land on 128-byte boundaries
   if (!aligned && lane == 0) flag_error(p.err, 4u);
+  const bool issuer = lane < kIssuers / kProducers;
   int4 batch = make_int4(0, 0, 0, 0);
-  int st = pr, round = 0;                                     // st = i % ns, round = i / ns
-  for (int t = 0, i = pr; i < n; ++t, i += kProducers) {
-    if ((t & 31) == 0) {
-      const int ii = i + kProducers * lane;
-      batch = ii < n ? item_desc(g, lv, L0, cta, rows, ii) : make_int4(0, 0, 0, 0);
+  for (int j0 = 0; j0 < nw; j0 += kIssuers / kProducers) {
+    if ((j0 & 31) == 0) {
+      const int ii = pr + kProducers * (j0 + lane);
+      batch = j0 + lane < nw ? item_desc(g, lv, L0, cta, slot_of, ii) : make_int4(0, 0, 0, 0);
     }
+    const int src = (j0 & 31) + (lane & 1);
     int4 it;
-    it.x = __shfl_sync(0xffffffffu, batch.x, t & 31);
-    it.y = __shfl_sync(0xffffffffu, batch.y, t & 31);
-    it.z = __shfl_sync(0xffffffffu, batch.z, t & 31);
-    it.w = __shfl_sync(0xffffffffu, batch.w, t & 31);
-    if (lane == 0) {
+    it.x = __shfl_sync(0xffffffffu, batch.x, src);
+    it.y = __shfl_sync(0xffffffffu, batch.y, src);
+    it.z = __shfl_sync(0xffffffffu, batch.z, src);
+    it.w = __shfl_sync(0xffffffffu, batch.w, src);
+    const int j = j0 + lane;
+    if (issuer && j < nw) {
+      const int i = pr + kProducers * j;
+      const int st = i % ns, round = i / ns;
       const uint32_t full = bars + st * 8, empty = bars + (ns + st) * 8;
       if (round > 0) mbar_wait(empty, (unsigned)(round - 1) & 1u, p.err);
       // Tag the stage with the item it now holds. A warp waits for its item's tag before it waits on the
@@ -577,15 +603,11 @@ __device__ void produce(const FusedParams& p, const LiveRows& lv, const RowPtr* 
         }
       }
     }
-    st += kProducers;
-    if (st >= ns) {
-      st -= ns;
-      ++round;
-    }
+    __syncwarp();
   }
   // every copy has landed before the producer leaves (the reducing warps wait on the same phases)
-  if (lane == 0)
-    for (int s0 = pr; s0 < ns && s0 < n; s0 += kProducers) {
+  if (issuer)
+    for (int s0 = pr + kProducers * lane; s0 < ns && s0 < n; s0 += kIssuers) {
       const int last = s0 + ((n - 1 - s0) / ns) * ns;
       mbar_wait(bars + s0 * 8, (unsigned)(last / ns) & 1u, p.err);
     }
@@ -655,6 +677,11 @@ __device__ __forceinline__ void process_work(const FusedParams& p, const Work& w
   }
 }
 
+__device__ __forceinline__ unsigned ld_relaxed_u32(const unsigned* ptr) {
+  unsigned v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(ptr) : "memory");
+  return v;
+}
 __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* ptr) {
   unsigned v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(ptr) : "memory");
@@ -784,21 +811,25 @@ __device__ __forceinline__ void phase_switch(const FusedParams& p, const LiveRow
   csync();
   if (threadIdx.x == 0) grid_barrier(p.bar_count, p.bar_gen, epoch - 1u, gridDim.x, p.err);
   csync();
+  // Every CTA of this grid is resident: the next kernel of the stream may be scheduled as SMs free up (its
+  // CTAs wait for this grid's completion before reading anything it writes).
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
 
 }
 
 // The down unit q of this CTA (token m, 32 output columns): the h tables of its live routed rows ->
 // shared memory (table slot jr), one bulk copy each. Starts with a barrier of the reducing warps (the
-// previous unit's tables are free) and ends with one (this unit's are in place).
-__device__ __forceinline__ void unit_tables(const FusedParams& p, const LiveRows& lv, int q, unsigned char* smem,
-                                            uint32_t hbar) {
+// previous unit's tables are free; the phase switch ends with one before unit 0) and ends with one (this
+// unit's are in place). The live rows of a unit are its token's first tokcnt[m] table slots.
+__device__ __forceinline__ void unit_tables(const FusedParams& p, const LiveRows& lv, int cta, int q,
+                                            unsigned char* smem, uint32_t hbar) {
   const Geo& g = p.geo;
   const int* slotrow = lv.slotrow + q * g.top_k;
   const size_t tb = htab_bytes(g.I);
-  csync();
+  if (q > 0) csync();
   if (threadIdx.x == 0) {
-    unsigned live = 0;
-    for (int jr = 0; jr < g.top_k; ++jr) live += slotrow[jr] >= 0;
+    const int u = cta + g.grid * q;
+    const unsigned live = u < g.u2 ? (unsigned)lv.tokcnt[fdiv(u, g.d_nb2)] : 0u;
     mbar_arrive_tx(hbar, (unsigned)tb * live);
   }
   if (threadIdx.x < g.top_k && slotrow[threadIdx.x] >= 0) {
@@ -828,9 +859,27 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
   const uint32_t bars = kTma ? smem_u32(smem + p.off_bars) : 0u;
   int* tags = kTma ? reinterpret_cast<int*>(smem + p.off_bars + 16 * (size_t)p.nstage) : nullptr;
 
+  if (kTma && warp >= kWarps) {
+    // producer warps: ring barriers and stage tags, and the tensor maps into the descriptor cache
+    const int pt = threadIdx.x - kThreads;
+    for (int b = pt; b < 2 * p.nstage; b += 32 * kProducers) {
+      mbar_init(bars + b * 8, 1);                             // full[0..ns), then empty[0..ns)
+      if (b < p.nstage) tags[b] = -1;
+    }
+    if (pt == 0) mbar_init(hbar, 1);                          // the h-table copies' barrier
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    if (pt < 6 && (p.map13.has_zeros || (pt != 2 && pt != 5)))
+      asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&p.tm[pt])) : "memory");
+  }
+  // Launched with programmatic stream serialisation, this CTA may start while the previous kernel of the
+  // stream is finishing: everything above touches only shared memory and the kernel's own parameters;
+  // from here on it reads what earlier work wrote (routing, activations, workspace, weights).
+  asm volatile("griddepcontrol.wait;\n" ::: "memory");
+
   // the barrier generation of this call (read at entry; the count reaches it before any CTA of this call
-  // can pass the barrier)
-  const unsigned gen_entry = threadIdx.x == 0 ? ld_acquire_u32(p.bar_gen) : 0u;
+  // can pass the barrier). The previous call stored it before it ended, so stream order alone makes it
+  // visible: a relaxed load, which -- unlike an acquire -- does not hold back this thread's routing loads.
+  const unsigned gen_entry = threadIdx.x == 0 ? ld_relaxed_u32(p.bar_gen) : 0u;
   int* rowmap = reinterpret_cast<int*>(smem + p.off_live);
   int* tokrow = rowmap + g.R;
   int* tokcnt = tokrow + g.R;
@@ -839,20 +888,36 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
   // Routing first: expert bases of every routed row, resolved once per CTA -- by warp 0 alone when the
   // rows fit one warp (it compacts them right after, with no CTA barrier in between), else by every thread.
   const bool one_warp = g.R <= 32;
-  auto resolve_row = [&](int r) {
+  int* sltab = reinterpret_cast<int*>(smem + p.off_slots);    // staged slot table (g.stab entries)
+  auto resolve_row = [&](int r, int e, float wt, bool staged) {
     RowPtr rp;
-    const int e = p.ids[r];
-    rp.ok[0] = p.map13.resolve(e, rp.w[0], rp.s[0], rp.z[0], p.err);
-    rp.ok[1] = p.map2.resolve(e, rp.w[1], rp.s[1], rp.z[1], p.err);
-    rp.slot = (p.map13.slots != nullptr && e >= 0 && e < p.map13.E) ? p.map13.slots[e] : -1;
-    rp.wt = p.topk_w[r];
+    rp.wt = wt;
+    if (staged) {                                             // one shared slot table for both projections
+      const bool in = e >= 0 && e < p.map13.E;
+      if (!in) flag_error(p.err, 1u);
+      const int sl = in ? sltab[e] : -1;
+      rp.ok[0] = in && p.map13.resolve_slot(sl, rp.w[0], rp.s[0], rp.z[0]);
+      rp.ok[1] = in && p.map2.resolve_slot(sl, rp.w[1], rp.s[1], rp.z[1]);
+      rp.slot = sl;
+    } else {
+      rp.ok[0] = p.map13.resolve(e, rp.w[0], rp.s[0], rp.z[0], p.err);
+      rp.ok[1] = p.map2.resolve(e, rp.w[1], rp.s[1], rp.z[1], p.err);
+      rp.slot = (p.map13.slots != nullptr && e >= 0 && e < p.map13.E) ? p.map13.slots[e] : -1;
+    }
     if (kTma && rp.slot >= kSlotExtent) flag_error(p.err, 1u);
     rows[r] = rp;
   };
   if (one_warp) {
-    if (warp == 0 && lane < g.R) resolve_row(lane);
+    // warp 0: the routing and the whole slot table in one round of loads, then lookups in shared memory
+    if (warp == 0) {
+      const int e = lane < g.R ? p.ids[lane] : -1;
+      const float wt = lane < g.R ? p.topk_w[lane] : 0.f;
+      for (int k = lane; k < g.stab; k += 32) sltab[k] = p.map13.slots[k];
+      __syncwarp();
+      if (lane < g.R) resolve_row(lane, e, wt, g.stab > 0);
+    }
   } else {
-    for (int r = threadIdx.x; r < g.R; r += blockDim.x) resolve_row(r);
+    for (int r = threadIdx.x; r < g.R; r += blockDim.x) resolve_row(r, p.ids[r], p.topk_w[r], false);
   }
   if (!kTma) {
     // Start the whole layer's weight stream: this CTA's 1/grid share of every routed row's six arrays.
@@ -876,16 +941,6 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
       if (len > 0)
         asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(base + start), "r"((unsigned)len) : "memory");
     }
-  } else if (warp >= kWarps) {
-    // producer warps: ring barriers and stage tags, and the tensor maps into the descriptor cache
-    const int pt = threadIdx.x - kThreads;
-    for (int b = pt; b < 2 * p.nstage; b += 32 * kProducers) {
-      mbar_init(bars + b * 8, 1);                             // full[0..ns), then empty[0..ns)
-      if (b < p.nstage) tags[b] = -1;
-    }
-    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
-    if (pt < 6 && (p.map13.has_zeros || (pt != 2 && pt != 5)))
-      asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&p.tm[pt])) : "memory");
   }
 
   // activation tables of the M rows of x (no dependence on the routing), by reducing warps 1..15
@@ -921,7 +976,8 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
   }
   if (!one_warp) __syncthreads();
   // Live routed rows (both experts resolve), compacted by warp 0 with ballots: rowmap in routing order,
-  // and per token its live rows' positions within its top_k.
+  // and per token its live rows' positions within its top_k. The producers start as soon as warp 0 is
+  // done (they need the routing, not the activation tables).
   if (warp == 0) {
     __syncwarp();
     int nl = 0;
@@ -943,21 +999,65 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
       tokcnt[m] = c;
     }
     if (lane == 0) {
-      mbar_init(hbar, 1);
-      asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+      if (!kTma) {                                            // (copy-engine mode: the producers set it up)
+        mbar_init(hbar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+      }
       misc[2] = 0u;
       misc[3] = gen_entry;                 // read by every CTA before any passes this call's barrier
       const int nblk = nl * g.nb1;
       misc[4] = (unsigned)(nblk * g.kp1);
       misc[5] = (unsigned)max(1, min((int)gridDim.x, nblk));
     }
+    if (kTma && !private_routing(g)) bar_arrive(2, 32 * (kProducers + 1));
   }
-  __syncthreads();
-  const LiveRows lv{rowmap, tokrow, tokcnt, slotrow, (int)misc[4], (int)misc[5]};
-  if (kTma && warp >= kWarps) {
-    produce(p, lv, rows, cta, stages, bars, tags, warp - kWarps, lane);
+  if constexpr (kTma) {
+   if (warp >= kWarps) {
+    bar_arrive(3, kTmaThreads);                               // ring barriers and tags initialised
+    const int pw = warp - kWarps;
+    if (private_routing(g)) {
+      // This warp's own copy of the routing, by the rules warp 0 applies for the reducing warps (the same
+      // live rows in the same order): ids and slot table in one round of loads, ballot compaction.
+      int* reg = reinterpret_cast<int*>(smem + p.off_preg) + pw * preg_ints(g);
+      int* pslot = reg;
+      int* prow = reg + 32;
+      int* ptokrow = reg + 64;
+      int* ptokcnt = reg + 96;
+      int* pstab = reg + 128;
+      const int e = lane < g.R ? p.ids[lane] : -1;
+      for (int k = lane; k < g.stab; k += 32) pstab[k] = p.map13.slots[k];
+      __syncwarp();
+      const bool in = lane < g.R && e >= 0 && e < p.map13.E;
+      const int sl = in ? pstab[e] : -1;
+      const bool live = in && sl >= 0;
+      const unsigned bal = __ballot_sync(0xffffffffu, live);
+      pslot[lane] = live ? sl : -1;
+      if (live) prow[__popc(bal & ((1u << lane) - 1u))] = lane;
+      if (lane < g.M) {
+        unsigned bits = (bal >> (lane * g.top_k)) & (g.top_k >= 32 ? 0xffffffffu : (1u << g.top_k) - 1u);
+        int c = 0;
+        while (bits) {
+          ptokrow[lane * g.top_k + c++] = __ffs(bits) - 1;
+          bits &= bits - 1u;
+        }
+        ptokcnt[lane] = c;
+      }
+      __syncwarp();
+      const int nblk = __popc(bal) * g.nb1;
+      const LiveRows plv{prow, ptokrow, ptokcnt, nullptr, nblk * g.kp1, max(1, min((int)gridDim.x, nblk))};
+      produce(p, plv, [&](int r, int) { return pslot[r]; }, cta, stages, bars, tags, pw, lane);
+    } else {
+      bar_wait(2, 32 * (kProducers + 1));                     // routing compacted by warp 0
+      const LiveRows lv{rowmap, tokrow, tokcnt, slotrow, (int)misc[4], (int)misc[5]};
+      produce(p, lv, [&](int r, int kind) { const RowPtr& rp = rows[r]; return rp.ok[kind - 1] ? rp.slot : -1; }, cta,
+              stages, bars, tags, pw, lane);
+    }
     return;
+   }
   }
+  if (kTma) bar_wait(3, kTmaThreads);                         // reducing warps: tables, routing, ring ready
+  else csync();
+  const LiveRows lv{rowmap, tokrow, tokcnt, slotrow, (int)misc[4], (int)misc[5]};
   const WarpList L = warp_list(g, lv, cta, warp);
   for (int idx = threadIdx.x; idx < g.max_units * g.top_k; idx += kThreads) {   // rows of the CTA's down units
     const int q = fdiv(idx, g.d_topk), jr = idx - q * g.top_k, u = cta + g.grid * q;
@@ -1017,7 +1117,7 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
   for (int t = 0; t < L.n1w; ++t) do_item(work1(g, lv, L, warp, t));
   phase_switch(p, lv, cta, warp, lane, mail1, epoch);
   for (int q = 0; q < L.nu; ++q) {
-    unit_tables(p, lv, q, smem, hbar);
+    unit_tables(p, lv, cta, q, smem, hbar);
     for (int k = 0; k < L.n2w; ++k) do_item(work2(g, lv, L, cta, warp, q, k));
     csync();
     if (warp == 0) {                          // y of the unit: fixed-order sum of its top_k x K-part partials
@@ -1061,7 +1161,7 @@ TmaPlan tma_plan(const Geo& g) {
   const size_t fixed = t.rest + 2 * kMaxStages * 8 + kMaxStages * 4;
   int ns = fixed < cap ? (int)((cap - fixed) / kStageBytes) : 0;
   if (ns > kMaxStages) ns = kMaxStages;
-  ns -= ns % kProducers;
+  ns -= ns % kIssuers;
   t.nstage = ns >= kMinStages ? ns : 0;
   t.stages = (size_t)t.nstage * kStageBytes;
   t.total = t.stages + t.rest + 2 * (size_t)t.nstage * 8 + (size_t)t.nstage * 4;
@@ -1154,9 +1254,18 @@ bool tma_eligible(const LayerArgs& a) {
   return tensor_map_encoder() != nullptr;
 }
 
+// The layer geometry of an M-token launch, with the slot table staged in shared memory when both
+// projections share one that is small enough.
+Geo layer_geo(const LayerArgs& a, int M, int grid_cap) {
+  Geo g = make_geo(M, a.H, a.I, a.top_k, grid_cap);
+  const bool shared = a.map13.slots != nullptr && a.map13.slots == a.map2.slots && a.map13.E == a.map2.E;
+  g.stab = shared && a.map13.E > 0 && a.map13.E <= kMaxStagedSlots ? a.map13.E : 0;
+  return g;
+}
+
 int launch_fused(const LayerArgs& a, int M, const void* x, const int32_t* ids, const float* w, void* y,
                         int grid_cap, bool tma) {
-  const Geo g = make_geo(M, a.H, a.I, a.top_k, grid_cap);
+  const Geo g = layer_geo(a, M, grid_cap);
   const SmemPlan sp = smem_plan(g);
   FusedParams p{};
   p.x = static_cast<const __nv_bfloat16*>(x); p.ids = ids; p.topk_w = w;
@@ -1178,6 +1287,8 @@ int launch_fused(const LayerArgs& a, int M, const void* x, const int32_t* ids, c
   p.off_rows = p.off_mail2 + sp.mail2;
   p.off_misc = p.off_rows + sp.rows;
   p.off_live = p.off_misc + sp.misc;
+  p.off_slots = p.off_live + sp.live;
+  p.off_preg = p.off_slots + sp.slots;
   unsigned* ctl = static_cast<unsigned*>(a.workspace);
   p.bar_count = ctl;
   p.bar_gen = ctl + 32;
@@ -1192,11 +1303,13 @@ int launch_fused(const LayerArgs& a, int M, const void* x, const int32_t* ids, c
   cfg.blockDim = dim3(tma ? kTmaThreads : kThreads);
   cfg.dynamicSmemBytes = total;
   cfg.stream = a.stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;   // start while the previous kernel ends
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, kern, p) == cudaSuccess ? kOk : kErrLaunch;
 }
 
@@ -1222,7 +1335,7 @@ int decode_layer_fused(const LayerArgs& a) {
   // at least kMinStages stages)
   const bool tma = tma_eligible(a);
   auto fits = [&](int m) {
-    const Geo g = make_geo(m, a.H, a.I, a.top_k, cached_cap);
+    const Geo g = layer_geo(a, m, cached_cap);
     return tma ? tma_plan(g).nstage > 0 : smem_plan(g).total <= 227 * 1024;
   };
   int mmax = a.M;
