@@ -29,6 +29,7 @@
 // tables): at launch every CTA asks L2 to fetch its 1/grid share of each routed expert's arrays, and each
 // lane loads its own item data into registers one item ahead of the one it is reducing.
 #include <cuda.h>
+#include <type_traits>
 #include <cudaTypedefs.h>
 
 #include "w2a16_kernels.h"
@@ -323,17 +324,21 @@ struct LaneMap {
   bool valid;
 };
 
-__device__ __forceinline__ LaneMap lane_map(const Geo& g, const Work& w, int lane, const RowPtr* rows) {
+template <int kKind>
+__device__ __forceinline__ LaneMap lane_map_k(const Geo& g, const Work& w, int lane, const RowPtr* rows) {
   LaneMap lm{};
-  if (w.kind == 0) return lm;
-  const bool k1 = w.kind == 1;
+  if (w.kind != kKind) return lm;
+  constexpr bool k1 = kKind == 1;
   const int gi = k1 ? (lane >> 4) : (lane >> 3);
   const int q = k1 ? (lane & 15) : (lane & 7);
   const int q8 = k1 ? (q & 7) : q;
   lm.col = (k1 && q >= 8 ? g.I : 0) + w.b * 32 + q8 * 4;
   lm.gl = k1 ? w.kp * 2 + gi : w.kp * 4 + gi;
-  lm.valid = !w.dead && rows[w.r].ok[w.kind - 1] && lm.gl < (k1 ? g.G1 : g.G2);
+  lm.valid = !w.dead && rows[w.r].ok[kKind - 1] && lm.gl < (k1 ? g.G1 : g.G2);
   return lm;
+}
+__device__ __forceinline__ LaneMap lane_map(const Geo& g, const Work& w, int lane, const RowPtr* rows) {
+  return w.kind == 1 ? lane_map_k<1>(g, w, lane, rows) : lane_map_k<2>(g, w, lane, rows);
 }
 
 // One lane's share of an item, held in registers.
@@ -616,10 +621,10 @@ __device__ void produce(const FusedParams& p, const LiveRows& lv, SlotOf slot_of
 // 4 columns x 1 group of this lane from a ring stage. Gate_up stages hold 256-byte word rows (32 gate |
 // 32 up columns), scales [group][half][32] and zero windows [group][half][16 B]; down stages 128-byte
 // rows, scales [group][32] and windows [group][16 B].
-template <int kPer>
+template <int kPer, int kKind>
 __device__ __forceinline__ void dot_stage(const unsigned char* st, const Work& w, int lane, const XTable& tb, int gl,
                                           bool sbf, bool has_z, float (&v)[4]) {
-  const bool k1 = w.kind == 1;
+  constexpr bool k1 = kKind == 1;
   const int gi = k1 ? (lane >> 4) : (lane >> 3);
   const int q = k1 ? (lane & 15) : (lane & 7);
   const int side = k1 && q >= 8 ? 1 : 0;
@@ -636,30 +641,31 @@ __device__ __forceinline__ void dot_stage(const unsigned char* st, const Work& w
 }
 
 
-template <bool kTma>
+// One item of kind kKind (1 gate_up, 2 down; compile-time, so each loop carries only its own inner product).
+template <bool kTma, int kKind>
 __device__ __forceinline__ void process_work(const FusedParams& p, const Work& w, int lane, const ItemRegs& it,
                                              const unsigned char* stage, unsigned char* smem, float* mail1,
                                              float* mail2, const RowPtr* rows) {
   const Geo& g = p.geo;
-  const bool k1 = w.kind == 1;
-  const int mi = w.kind - 1;
+  constexpr bool k1 = kKind == 1;
+  constexpr int mi = kKind - 1;
   const RowPtr& rp = rows[w.r];
   unsigned char* tabs = smem + p.off_tabs;
-  const LaneMap lm = lane_map(g, w, lane, rows);
+  const LaneMap lm = lane_map_k<kKind>(g, w, lane, rows);
   float v[4] = {0.f, 0.f, 0.f, 0.f};
   if (lm.valid) {
     const bool sbf = p.scale_bf16 != 0, hz = rp.z[mi] != nullptr;
-    if (k1) {
+    if constexpr (k1) {
       const XTable tb = table_at(tabs + (size_t)fdiv(w.r, g.d_topk) * token_table_bytes(g.H), g.H);
-      if (kTma) dot_stage<1>(stage, w, lane, tb, lm.gl, sbf, hz, v);
+      if constexpr (kTma) dot_stage<1, 1>(stage, w, lane, tb, lm.gl, sbf, hz, v);
       else dot_regs<1>(it, tb, lm.gl, sbf, hz, v);
     } else {
       const XTable tb = htable_at(tabs + (size_t)w.jr * htab_bytes(g.I), g.I);
-      if (kTma) dot_stage<kGroup / kSub>(stage, w, lane, tb, lm.gl, sbf, hz, v);
+      if constexpr (kTma) dot_stage<kGroup / kSub, 2>(stage, w, lane, tb, lm.gl, sbf, hz, v);
       else dot_regs<kGroup / kSub>(it, tb, lm.gl, sbf, hz, v);
     }
   }
-  if (k1) {
+  if constexpr (k1) {
 #pragma unroll
     for (int c = 0; c < 4; ++c) v[c] += __shfl_xor_sync(0xffffffffu, v[c], 16);
     if (lane < 16)
@@ -1090,18 +1096,20 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
     load_item(p, wn, lane, rows, nxt_it);
   }
   int tr = 0;                                                 // register mode: flat index of the item
-  auto do_item = [&](const Work& w) {
-    if (kTma) {
+  auto do_item = [&](const Work& w, auto kind) {
+    constexpr int K = decltype(kind)::value;
+    if constexpr (kTma) {
       const int st = w.seq % p.nstage;
       if (lane == 0) {
         wait_tag(tags, st, w.seq, p.err);
         mbar_wait(bars + st * 8, (unsigned)(w.seq / p.nstage) & 1u, p.err);
       }
       __syncwarp();
-      process_work<true>(p, w, lane, cur, stages + (size_t)st * kStageBytes, smem, mail1, mail2, rows);
+      process_work<true, K>(p, w, lane, cur, stages + (size_t)st * kStageBytes, smem, mail1, mail2, rows);
       __syncwarp();
       if (lane == 0) mbar_arrive(bars + (p.nstage + st) * 8);
-      if (w.kind == 1 && w.slot < head_k) head_item_done(p, lv, L, cta, lane, mail1, head_k, epoch, misc + 2);
+      if constexpr (K == 1)
+        if (w.slot < head_k) head_item_done(p, lv, L, cta, lane, mail1, head_k, epoch, misc + 2);
     } else {
       const Work wc = wn;
       cur = nxt_it;
@@ -1109,16 +1117,17 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
         wn = item_at(tr);
         load_item(p, wn, lane, rows, nxt_it);
       }
-      process_work<false>(p, wc, lane, cur, nullptr, smem, mail1, mail2, rows);
+      process_work<false, K>(p, wc, lane, cur, nullptr, smem, mail1, mail2, rows);
       __syncwarp();
-      if (wc.kind == 1 && wc.slot < head_k) head_item_done(p, lv, L, cta, lane, mail1, head_k, epoch, misc + 2);
+      if constexpr (K == 1)
+        if (wc.slot < head_k) head_item_done(p, lv, L, cta, lane, mail1, head_k, epoch, misc + 2);
     }
   };
-  for (int t = 0; t < L.n1w; ++t) do_item(work1(g, lv, L, warp, t));
+  for (int t = 0; t < L.n1w; ++t) do_item(work1(g, lv, L, warp, t), std::integral_constant<int, 1>{});
   phase_switch(p, lv, cta, warp, lane, mail1, epoch);
   for (int q = 0; q < L.nu; ++q) {
     unit_tables(p, lv, cta, q, smem, hbar);
-    for (int k = 0; k < L.n2w; ++k) do_item(work2(g, lv, L, cta, warp, q, k));
+    for (int k = 0; k < L.n2w; ++k) do_item(work2(g, lv, L, cta, warp, q, k), std::integral_constant<int, 2>{});
     csync();
     if (warp == 0) {                          // y of the unit: fixed-order sum of its top_k x K-part partials
       const int u = cta + g.grid * q, m = fdiv(u, g.d_nb2), b = u - m * g.nb2;
