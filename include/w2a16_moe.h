@@ -192,7 +192,8 @@ int w2a16_int8_gemv(const void* x, int64_t stride_xm, const int32_t* qweight, co
                     int group, int zero, int M, int K, int N, void* y, int64_t stride_ym,
                     void* workspace, size_t workspace_bytes, void* stream);
 
-/* Workspace bytes w2a16_int8_gemv needs (split-K partials + counters; zero-filled before first use). */
+/* Workspace bytes w2a16_int8_gemv accepts (a token amount: its K slices are reduced inside a thread-block
+ * cluster; the argument stays for ABI stability). */
 size_t w2a16_int8_workspace_bytes(int M, int K, int N);
 
 /* One-shot all-reduce (sum) of a small bf16 vector across the GPUs of one node over NVLink peer memory:

@@ -44,6 +44,9 @@ struct ArParams {
 };
 
 __global__ void __launch_bounds__(kArThreads, 1) allreduce_kernel(ArParams p) {
+  // the next kernel of the stream (the INT8 projection, launched with programmatic stream serialisation)
+  // may start its weight loads now; it waits for this grid before it reads the sum
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
   __shared__ unsigned s_epoch;
   if (threadIdx.x == 0) s_epoch = *p.epoch + 1u;
   __syncthreads();

@@ -100,19 +100,29 @@ class ExpertArena:
         return n
 
 
-@torch.library.custom_op("w2a16_moe::decode_layer_slots", mutates_args=())
-def _decode_layer_slots(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor, slots: torch.Tensor,
-                        codes13: torch.Tensor, scales13: torch.Tensor, zeros13: Optional[torch.Tensor],
-                        codes2: torch.Tensor, scales2: torch.Tensor, zeros2: Optional[torch.Tensor],
-                        routed_scaling_factor: float) -> torch.Tensor:
+_WS_BYTES = {}
+
+
+def _workspace_bytes(M: int, H: int, I: int, top_k: int) -> int:
+    key = (M, H, I, top_k)
+    n = _WS_BYTES.get(key)
+    if n is None:
+        n = int(_native.lib().w2a16_moe_layer_workspace_bytes(M, H, I, top_k))
+        _WS_BYTES[key] = n
+    return n
+
+
+def _decode_layer_slots_impl(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor, slots: torch.Tensor,
+                             codes13: torch.Tensor, scales13: torch.Tensor, zeros13: Optional[torch.Tensor],
+                             codes2: torch.Tensor, scales2: torch.Tensor, zeros2: Optional[torch.Tensor],
+                             routed_scaling_factor: float) -> torch.Tensor:
     M, H = x.shape
     top_k = topk_ids.shape[1]
     I = codes13.shape[2] // 2
     y = torch.empty((M, H), dtype=torch.bfloat16, device=x.device)
     if M == 0:
         return y
-    nbytes = int(_native.lib().w2a16_moe_layer_workspace_bytes(M, H, I, top_k))
-    ws = layer_workspace(x.device, nbytes)
+    ws = layer_workspace(x.device, _workspace_bytes(M, H, I, top_k))
     esz = scales13.element_size()
     _native.call("w2a16_moe_decode_layer_slots", x.data_ptr(), M, H, I, top_k, topk_ids.data_ptr(),
                  topk_w.data_ptr(), slots.data_ptr(), slots.numel(),
@@ -123,6 +133,15 @@ def _decode_layer_slots(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.T
                  int(scales13.dtype == torch.bfloat16), float(routed_scaling_factor), y.data_ptr(),
                  ws.data_ptr(), ws.numel(), _err_word(x.device).data_ptr(), _stream(x.device))
     return y
+
+
+@torch.library.custom_op("w2a16_moe::decode_layer_slots", mutates_args=())
+def _decode_layer_slots(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor, slots: torch.Tensor,
+                        codes13: torch.Tensor, scales13: torch.Tensor, zeros13: Optional[torch.Tensor],
+                        codes2: torch.Tensor, scales2: torch.Tensor, zeros2: Optional[torch.Tensor],
+                        routed_scaling_factor: float) -> torch.Tensor:
+    return _decode_layer_slots_impl(x, topk_ids, topk_w, slots, codes13, scales13, zeros13, codes2, scales2,
+                                    zeros2, routed_scaling_factor)
 
 
 @_decode_layer_slots.register_fake
@@ -146,8 +165,11 @@ def moe_decode_layer(x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torc
     """y[m] = routed_scaling_factor * sum_j w[m, j] * down_e(silu(gate_e(x_m)) * up_e(x_m)),
     e = topk_ids[m, j] looked up through ``arena.slots``. x bf16 [M, H] -> bf16 [M, H]."""
     x, ids, w = _routing(x, topk_ids, topk_weights)
-    return _decode_layer_slots(x, ids, w, arena.slots, arena.codes13, arena.scales13, arena.zeros13,
-                               arena.codes2, arena.scales2, arena.zeros2, float(routed_scaling_factor))
+    # eager calls skip the custom-op dispatcher (tens of microseconds of host time); traced/compiled code
+    # goes through the registered op
+    op = _decode_layer_slots if torch.compiler.is_compiling() else _decode_layer_slots_impl
+    return op(x, ids, w, arena.slots, arena.codes13, arena.scales13, arena.zeros13, arena.codes2, arena.scales2,
+              arena.zeros2, float(routed_scaling_factor))
 
 
 @torch.library.custom_op("w2a16_moe::decode_layer_tab", mutates_args=())

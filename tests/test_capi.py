@@ -85,4 +85,5 @@ def test_argument_errors_return_status(pkg):
 def test_workspace_sizes(pkg):
     lib = pkg._native.lib()
     assert lib.w2a16_moe_layer_workspace_bytes(1, 4096, 1536, 8) >= 8 * 1536 * 4
-    assert lib.w2a16_int8_workspace_bytes(1, 4096, 4096) >= 16 * 4096 * 4
+    # the INT8 GEMV reduces its K slices inside a thread-block cluster: no scratch beyond a token amount
+    assert 0 < lib.w2a16_int8_workspace_bytes(1, 4096, 4096) <= 4096
