@@ -219,6 +219,26 @@ __device__ __forceinline__ void htab_block(unsigned char* tab, int I, int hb, fl
   }
 }
 
+// One warp copies the first n entries of the slot table into shared memory. Every load of a lane is
+// issued before its first store: the compiler cannot tell the two arrays apart, so a store between two
+// loads would hold the second back until the first returned (one global round trip per 32 entries).
+__device__ __forceinline__ void stage_slots(int* dst, const int* src, int n, int lane) {
+  constexpr int kPer = 16;
+  for (int k0 = 0; k0 < n; k0 += 32 * kPer) {
+    int v[kPer];
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int k = k0 + lane + 32 * j;
+      v[j] = k < n ? src[k] : 0;
+    }
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int k = k0 + lane + 32 * j;
+      if (k < n) dst[k] = v[j];
+    }
+  }
+}
+
 // Barrier of the 512 reducing threads only (the producer warps of copy-engine mode never join).
 __device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;\n" ::"n"(kThreads) : "memory"); }
 // Prologue hand-overs of copy-engine mode: warp 0 -> producer warps once the routing is compacted
@@ -918,7 +938,7 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
     if (warp == 0) {
       const int e = lane < g.R ? p.ids[lane] : -1;
       const float wt = lane < g.R ? p.topk_w[lane] : 0.f;
-      for (int k = lane; k < g.stab; k += 32) sltab[k] = p.map13.slots[k];
+      stage_slots(sltab, p.map13.slots, g.stab, lane);
       __syncwarp();
       if (lane < g.R) resolve_row(lane, e, wt, g.stab > 0);
     }
@@ -1031,7 +1051,7 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
       int* ptokcnt = reg + 96;
       int* pstab = reg + 128;
       const int e = lane < g.R ? p.ids[lane] : -1;
-      for (int k = lane; k < g.stab; k += 32) pstab[k] = p.map13.slots[k];
+      stage_slots(pstab, p.map13.slots, g.stab, lane);
       __syncwarp();
       const bool in = lane < g.R && e >= 0 && e < p.map13.E;
       const int sl = in ? pstab[e] : -1;
