@@ -100,6 +100,19 @@ int w2a16_moe_gemv_slots(const void* a, int64_t stride_am,
 size_t w2a16_moe_layer_workspace_bytes(int M, int H, int I, int top_k);
 
 /*
+ * No counterpart in the reference (its batched path is the same Triton GEMV per routed row).
+ * Workspace bytes with which w2a16_moe_decode_layer_slots takes its batched path where that path is the
+ * faster one: from 64 tokens it returns the batched path's size (the routed rows grouped by expert, every
+ * resident expert streamed once for all of its rows, the products on the tensor cores; route tables,
+ * h [rows, I] bf16 and y rows [rows, H] fp32 for up to 128 tokens at a time); below 64 tokens it returns
+ * w2a16_moe_layer_workspace_bytes (the per-token path). Any workspace at least as large as the batched
+ * path's size for M tokens makes calls with M >= 16 take it; a smaller one runs the per-token path, as
+ * does the int64-table entry point. The batched path keeps out of the per-token path's persistent
+ * workspace words, so one workspace serves calls of either path.
+ */
+size_t w2a16_moe_layer_workspace_bytes_batched(int M, int H, int I, int top_k);
+
+/*
  * Full decode MoE layer: gate_up GEMV, SiLU(gate) * up, down GEMV * routed weight, sum over the
  * top-k experts of each token, times routed_scaling_factor.
  * Replaces MoeWNA16Method._apply_gemv — patches/ncontig_gemv.py:218-238 (serving patch:3358-3400):

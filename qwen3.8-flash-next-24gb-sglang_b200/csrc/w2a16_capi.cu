@@ -85,6 +85,13 @@ size_t w2a16_moe_layer_workspace_bytes(int M, int H, int I, int top_k) {
   return layer_workspace_bytes(M, H, I, top_k);
 }
 
+size_t w2a16_moe_layer_workspace_bytes_batched(int M, int H, int I, int top_k) {
+  const size_t a = layer_workspace_bytes(M, H, I, top_k);
+  if (M < kGroupedAutoTokens) return a;
+  const size_t b = grouped_workspace_bytes(M, H, I, top_k);
+  return a > b ? a : b;
+}
+
 int w2a16_moe_decode_layer_tab(const void* x, int M, int H, int I, int top_k, const int32_t* topk_ids,
                                const float* topk_w, int num_experts, const int64_t* wtab13, const int64_t* stab13,
                                const int64_t* ztab13, const int64_t* wtab2, const int64_t* stab2,
@@ -124,6 +131,13 @@ int w2a16_moe_decode_layer_slots(const void* x, int M, int H, int I, int top_k, 
                     zeros2_slot_bytes);
   a.scale_bf16 = scale_bf16; a.routed_scaling = routed_scaling_factor; a.y = y;
   a.workspace = workspace; a.workspace_bytes = workspace_bytes; a.err = err; a.stream = as_stream(stream);
+  // M >= 16 with a workspace of w2a16_moe_layer_workspace_bytes_batched: experts grouped over the tokens on
+  // the tensor cores (each expert streamed once); otherwise, or when the arena maps do not qualify, the
+  // per-token fused layer.
+  if (grouped_eligible(a)) {
+    const int st = decode_layer_grouped(a);
+    if (st != kErrShape) return st;
+  }
   return decode_layer_fused(a);
 }
 

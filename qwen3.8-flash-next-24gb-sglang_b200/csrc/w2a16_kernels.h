@@ -1,6 +1,7 @@
 // Internal host-side declarations shared by the kernel translation units and the C ABI layer.
 #pragma once
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include "w2a16_common.cuh"
 
@@ -42,6 +43,19 @@ struct LayerArgs {
 };
 size_t layer_workspace_bytes(int M, int H, int I, int top_k);
 int decode_layer_fused(const LayerArgs& a);
+// The six arena tensor maps of the fused layer's copy-engine mode (gate_up codes / scales / zeros, then
+// down); false when the arena does not qualify (no slot table, H or I not a multiple of 64, no encoder).
+bool layer_arena_maps(const LayerArgs& a, CUtensorMap (&tm)[6]);
+
+// Batched layer on the tensor cores (w2a16_grouped.cu): M >= kGroupedMinTokens, slot arenas only.
+constexpr int kGroupedMinTokens = 16;
+// From this many tokens the batched path is the faster one (measured at H=4096, I=1536, E=256, top-8: 0.87x
+// of the per-token path at 48 tokens, 1.07x at 64, 1.84x at 128), so the batched workspace size asks for it.
+constexpr int kGroupedAutoTokens = 64;
+size_t grouped_workspace_bytes(int M, int H, int I, int top_k);
+// 1 when the grouped path takes this call (slot arena, M large enough, the workspace holds its buffers).
+bool grouped_eligible(const LayerArgs& a);
+int decode_layer_grouped(const LayerArgs& a);
 int allreduce_peers_bf16(const void* in, void* out, int n, int n_max, const uint64_t* bufs, size_t flag_off, int rank,
                          int world, unsigned* epoch, unsigned* err, cudaStream_t stream);
 

@@ -1344,6 +1344,8 @@ int launch_fused(const LayerArgs& a, int M, const void* x, const int32_t* ids, c
 
 }  // namespace
 
+bool layer_arena_maps(const LayerArgs& a, CUtensorMap (&tm)[6]) { return tma_eligible(a) && arena_maps(a, tm); }
+
 int decode_layer_fused(const LayerArgs& a) {
   if (a.M <= 0) return kOk;
   if (a.H % kGroup != 0 || a.I % kGroup != 0 || a.top_k <= 0) return kErrShape;

@@ -103,11 +103,23 @@ class ExpertArena:
 _WS_BYTES = {}
 
 
-def _workspace_bytes(M: int, H: int, I: int, top_k: int) -> int:
-    key = (M, H, I, top_k)
+BATCHED_MIN_TOKENS = 64   # the library's own choice: the batched path from this many tokens
+
+
+def _workspace_bytes(M: int, H: int, I: int, top_k: int, batched: int = -1) -> int:
+    """Workspace bytes of a slot-form layer call. batched -1: the library's choice (the batched path from
+    BATCHED_MIN_TOKENS tokens, where it is the faster one); 1: the batched path from 16 tokens; 0: the
+    per-token path."""
+    key = (M, H, I, top_k, batched)
     n = _WS_BYTES.get(key)
     if n is None:
-        n = int(_native.lib().w2a16_moe_layer_workspace_bytes(M, H, I, top_k))
+        lib = _native.lib()
+        if batched == 0:
+            n = int(lib.w2a16_moe_layer_workspace_bytes(M, H, I, top_k))
+        else:
+            Mq = max(M, BATCHED_MIN_TOKENS) if batched == 1 else M
+            n = max(int(lib.w2a16_moe_layer_workspace_bytes_batched(Mq, H, I, top_k)),
+                    int(lib.w2a16_moe_layer_workspace_bytes(M, H, I, top_k)))
         _WS_BYTES[key] = n
     return n
 
@@ -115,14 +127,15 @@ def _workspace_bytes(M: int, H: int, I: int, top_k: int) -> int:
 def _decode_layer_slots_impl(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor, slots: torch.Tensor,
                              codes13: torch.Tensor, scales13: torch.Tensor, zeros13: Optional[torch.Tensor],
                              codes2: torch.Tensor, scales2: torch.Tensor, zeros2: Optional[torch.Tensor],
-                             routed_scaling_factor: float) -> torch.Tensor:
+                             routed_scaling_factor: float, batched: int = -1) -> torch.Tensor:
     M, H = x.shape
     top_k = topk_ids.shape[1]
     I = codes13.shape[2] // 2
     y = torch.empty((M, H), dtype=torch.bfloat16, device=x.device)
     if M == 0:
         return y
-    ws = layer_workspace(x.device, _workspace_bytes(M, H, I, top_k))
+    nbytes = _workspace_bytes(M, H, I, top_k, batched)
+    ws = layer_workspace(x.device, nbytes)
     esz = scales13.element_size()
     _native.call("w2a16_moe_decode_layer_slots", x.data_ptr(), M, H, I, top_k, topk_ids.data_ptr(),
                  topk_w.data_ptr(), slots.data_ptr(), slots.numel(),
@@ -131,7 +144,7 @@ def _decode_layer_slots_impl(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: to
                  codes2.data_ptr(), codes2.stride(0) * 4, scales2.data_ptr(), scales2.stride(0) * esz,
                  _p(zeros2), 0 if zeros2 is None else zeros2.stride(0),
                  int(scales13.dtype == torch.bfloat16), float(routed_scaling_factor), y.data_ptr(),
-                 ws.data_ptr(), ws.numel(), _err_word(x.device).data_ptr(), _stream(x.device))
+                 ws.data_ptr(), nbytes, _err_word(x.device).data_ptr(), _stream(x.device))
     return y
 
 
@@ -139,14 +152,14 @@ def _decode_layer_slots_impl(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: to
 def _decode_layer_slots(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor, slots: torch.Tensor,
                         codes13: torch.Tensor, scales13: torch.Tensor, zeros13: Optional[torch.Tensor],
                         codes2: torch.Tensor, scales2: torch.Tensor, zeros2: Optional[torch.Tensor],
-                        routed_scaling_factor: float) -> torch.Tensor:
+                        routed_scaling_factor: float, batched: int = -1) -> torch.Tensor:
     return _decode_layer_slots_impl(x, topk_ids, topk_w, slots, codes13, scales13, zeros13, codes2, scales2,
-                                    zeros2, routed_scaling_factor)
+                                    zeros2, routed_scaling_factor, batched)
 
 
 @_decode_layer_slots.register_fake
 def _decode_layer_slots_fake(x, topk_ids, topk_w, slots, codes13, scales13, zeros13, codes2, scales2, zeros2,
-                             routed_scaling_factor):
+                             routed_scaling_factor, batched=-1):
     return torch.empty_like(x, dtype=torch.bfloat16)
 
 
@@ -161,15 +174,19 @@ def _routing(x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor
 
 
 def moe_decode_layer(x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor, arena: ExpertArena,
-                     routed_scaling_factor: float = 1.0) -> torch.Tensor:
+                     routed_scaling_factor: float = 1.0, batched: Optional[bool] = None) -> torch.Tensor:
     """y[m] = routed_scaling_factor * sum_j w[m, j] * down_e(silu(gate_e(x_m)) * up_e(x_m)),
-    e = topk_ids[m, j] looked up through ``arena.slots``. x bf16 [M, H] -> bf16 [M, H]."""
+    e = topk_ids[m, j] looked up through ``arena.slots``. x bf16 [M, H] -> bf16 [M, H].
+
+    ``batched``: None lets the library choose (the batched path -- routed rows grouped by expert, each
+    expert streamed once, products on the tensor cores -- from 64 tokens, where it is faster than the
+    per-token path); True takes it from 16 tokens; False always takes the per-token path."""
     x, ids, w = _routing(x, topk_ids, topk_weights)
     # eager calls skip the custom-op dispatcher (tens of microseconds of host time); traced/compiled code
     # goes through the registered op
     op = _decode_layer_slots if torch.compiler.is_compiling() else _decode_layer_slots_impl
     return op(x, ids, w, arena.slots, arena.codes13, arena.scales13, arena.zeros13, arena.codes2, arena.scales2,
-              arena.zeros2, float(routed_scaling_factor))
+              arena.zeros2, float(routed_scaling_factor), -1 if batched is None else int(bool(batched)))
 
 
 @torch.library.custom_op("w2a16_moe::decode_layer_tab", mutates_args=())
