@@ -10,18 +10,22 @@
 // proj_kernel<kGateUp> (persistent, one CTA per SM): work items (group, tile of 128 weight columns -- gate_up:
 // 64 gate columns and the matching 64 up columns; down: 128 output columns), dealt round-robin. A producer warp
 // streams each item's codes, scales and zero points through a ring of shared-memory stages with tensor copies
-// (the fused layer's arena maps). Per 128-value quantization group along K, 16 warps expand the codes to
-// bf16(128 + q) -- exact -- straight into tensor memory as the MMA's A operand (the tile's column r is TMEM
-// lane r; one 16-value word is 8 columns, one tcgen05.st), and warps 0-3 stage the group's rows of the
-// activation (x for gate_up, h for down) in shared memory as the B operand with their sums. An MMA warp issues
-// 8 tcgen05.mma (A from tensor memory, M = 128 columns, N = 16 rows, K = 16, fp32 accumulation in tensor
-// memory) once the operands are in place and commits them to an mbarrier; warps 0-3 then read the
-// accumulators (tcgen05.ld) and fold them into registers: acc += s * (D - (128 + zp) * sum x), the
-// reference's zero-point fold (gemv/moe_gemv_int2_tab.py:61-66) applied per group with its scale. Two operand
-// and two accumulator buffers alternate between groups, handed over with mbarriers (operands ready, MMA done,
-// accumulator read), so expansion, MMA issue and folding of consecutive groups overlap. Within each 16-value
-// word the MMA's K order is permuted (position 2j = value j, 2j + 1 = value j + 8, which is what one LOP3 per
-// pair yields); the B operand is staged in the same order.
+// (the fused layer's arena maps). Per 128-value quantization group along K:
+//   * warps 8-15 expand the codes to bf16(128 + q) -- exact -- straight into tensor memory as the MMA's A
+//     operand (the tile's column r is TMEM lane r; one 16-value word is 8 columns, one tcgen05.st);
+//   * warps 4-7 stage the group's rows of the activation (x for gate_up, h for down) in shared memory as the
+//     B operand, with the rows' sums and the tile's scales and zero points;
+//   * two MMA warps, taking alternate groups, issue 8 tcgen05.mma (A from tensor memory, M = 128 columns,
+//     N = 16 rows, K = 16, fp32 accumulation in tensor memory) and commit them to an mbarrier;
+//   * warps 0-3 read the accumulators (tcgen05.ld) and fold them into registers:
+//     acc += s * (D - (128 + zp) * sum x), the reference's zero-point fold (gemv/moe_gemv_int2_tab.py:61-66)
+//     applied per group with its scale.
+// Three operand and accumulator buffers rotate between groups, handed over with mbarriers (operands ready,
+// MMA done, accumulator read), so every role works on a different group at a time. Within each 16-value word
+// the MMA's K order is permuted (position 2j = value j, 2j + 1 = value j + 8, which is what one LOP3 per pair
+// yields); the B operand is staged in the same order. At decode sizes an expert has only a few rows per call,
+// so N = 16 MMAs leave the tensor pipe mostly idle (about 5 % active); the path pays where the per-token
+// path re-reads each expert many times, from about 64 tokens.
 // Epilogues: gate_up -> h = silu(gate) * up in bf16 per routed row; down -> routed weight * y row in fp32.
 //
 // sum_kernel: y[m] = routed_scaling * (sum of the token's live y rows in routing order), deterministic.
@@ -38,7 +42,8 @@ constexpr int kGN = 16;                          // MMA N: rows of one group
 constexpr int kTileCols = 128;                   // MMA M: weight columns of a tile
 constexpr int kCompute = 512;                    // warps 0-3 fold, 4-7 stage B and the scales, 8-15 expand codes
 constexpr int kWriters = kCompute - 128;          // threads that write a group's operands (warps 4-15)
-constexpr int kGThreads = kCompute + 64;         // + the producer warp and the MMA warp
+constexpr int kMmaWarps = 2;                     // MMA issuers, taking alternate groups
+constexpr int kGThreads = kCompute + 32 + 32 * kMmaWarps;   // + the producer warp and the MMA warps
 constexpr int kAcols = kGroup / 2;               // TMEM columns of one group of the A operand (bf16 pairs)
 constexpr int kWordRows = kGroup / 16;           // 16-value word rows of a group
 constexpr int kBBytes = kGN * kGroup * 2;        // one group of the B operand (bf16)
@@ -315,12 +320,15 @@ __global__ void __launch_bounds__(kGThreads, 1) proj_kernel(const __grid_constan
     return;
   }
 
-  if (warp == kMmaWarp) {
-    // MMA issuer: per group, once its operands are in place and its accumulator buffer has been read
+  if (warp >= kMmaWarp) {
+    // MMA issuers (one thread per warp takes every kMmaWarps-th group: one thread issues an MMA only every
+    // few tens of cycles): per group, once its operands are in place and its accumulator buffer has been read
     if (lane == 0) {
+      const unsigned q = (unsigned)(warp - kMmaWarp);
       unsigned gc = 0;
       for (int w = blockIdx.x; w < nitems; w += gridDim.x)
         for (int g = 0; g < G; ++g, ++gc) {
+          if (gc % kMmaWarps != q) continue;
           const int b = buf(gc);
           g_mbar_wait(ready(b), par(gc), p.err);
           if (gc >= kNB) g_mbar_wait(tfree(b), par(gc - kNB), p.err);
@@ -499,7 +507,7 @@ __global__ void __launch_bounds__(kGThreads, 1) proj_kernel(const __grid_constan
   // compute warps and the MMA warp: every accumulator was read after its MMA completed (the folds waited on
   // them), so the tensor memory can go
   tc_before();
-  asm volatile("bar.sync 3, %0;\n" ::"n"(kCompute + 32) : "memory");
+  asm volatile("bar.sync 3, %0;\n" ::"n"(kCompute + 32 * kMmaWarps) : "memory");
   if (warp == 0) {
     tc_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(kTmemCols) : "memory");
