@@ -87,3 +87,19 @@ def test_workspace_sizes(pkg):
     assert lib.w2a16_moe_layer_workspace_bytes(1, 4096, 1536, 8) >= 8 * 1536 * 4
     # the INT8 GEMV reduces its K slices inside a thread-block cluster: no scratch beyond a token amount
     assert 0 < lib.w2a16_int8_workspace_bytes(1, 4096, 4096) <= 4096
+
+
+def test_batched_workspace_sizes(pkg):
+    """The batched layer's workspace query: the per-token size below 64 tokens (the per-token path is the
+    faster one there), at least that and room for route tables, h and y rows from 64 tokens, no more growth
+    of the batched part past one 128-token launch, and never less than the per-token path needs."""
+    lib = pkg._native.lib()
+    H, I, k = 4096, 1536, 8
+    per = lambda M: lib.w2a16_moe_layer_workspace_bytes(M, H, I, k)
+    bat = lambda M: lib.w2a16_moe_layer_workspace_bytes_batched(M, H, I, k)
+    for M in (1, 15, 16, 32, 63):
+        assert bat(M) == per(M), M
+    rows = 64 * k
+    assert bat(64) >= per(64) and bat(64) >= rows * (I * 2 + H * 4)
+    assert bat(64) < bat(128) == bat(256)
+    assert bat(1024) == max(per(1024), bat(128))     # the size serves both paths
