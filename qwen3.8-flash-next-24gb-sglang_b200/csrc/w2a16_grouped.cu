@@ -20,7 +20,7 @@
 //   * warps 0-3 read the accumulators (tcgen05.ld) and fold them into registers:
 //     acc += s * (D - (128 + zp) * sum x), the reference's zero-point fold (gemv/moe_gemv_int2_tab.py:61-66)
 //     applied per group with its scale.
-// Three operand and accumulator buffers rotate between groups, handed over with mbarriers (operands ready,
+// Four operand and accumulator buffers rotate between groups, handed over with mbarriers (operands ready,
 // MMA done, accumulator read), so every role works on a different group at a time. Within each 16-value word
 // the MMA's K order is permuted (position 2j = value j, 2j + 1 = value j + 8, which is what one LOP3 per pair
 // yields); the B operand is staged in the same order. At decode sizes an expert has only a few rows per call,
@@ -59,8 +59,8 @@ constexpr int kMaxGroupedRows = 1024;            // routed rows per launch
 constexpr int kGroupedChunk = 128;               // tokens per launch
 constexpr int kSlotLimit = 1 << 20;              // slot ids the arena tensor maps accept
 constexpr unsigned kGWait = 1u << 17;            // suspending mbarrier tries before a wait gives up
-constexpr int kNB = 3;                           // operand / accumulator buffers in flight
-constexpr int kTmemCols = 256;                   // A: kNB buffers of kAcols columns; then kNB accumulators of kGN
+constexpr int kNB = 4;                           // operand / accumulator buffers in flight
+constexpr int kTmemCols = 512;                   // A: kNB buffers of kAcols columns; then kNB accumulators of kGN
 // kind::f16 instruction descriptor: fp32 accumulator, bf16 A and B, both K-major, N = 16, M = 128
 constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kGN >> 3) << 17) |
                             ((uint32_t)(kTileCols >> 4) << 24);
