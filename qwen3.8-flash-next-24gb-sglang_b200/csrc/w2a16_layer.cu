@@ -1209,13 +1209,15 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-// One tensor map over a slot arena: dims / strides innermost first, the last dimension the slot.
+// One tensor map over a slot arena: dims / strides innermost first, the last dimension the slot. L2 promotion
+// of 128 bytes, the width of a box row (32 words): wider promotion (256 bytes) fetched the neighbouring
+// columns, which other CTAs load themselves, and cost 0.6 us per config-1 layer.
 bool encode_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* base, const cuuint64_t* dims,
                 const cuuint64_t* strides, const cuuint32_t* box) {
   const cuuint32_t es[4] = {1, 1, 1, 1};
   return tensor_map_encoder()(m, dt, (cuuint32_t)rank, const_cast<void*>(base), dims, strides, box, es,
                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // The six arena maps; cached per thread on everything they depend on (the arena never moves between
