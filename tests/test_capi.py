@@ -103,3 +103,22 @@ def test_batched_workspace_sizes(pkg):
     assert bat(64) >= per(64) and bat(64) >= rows * (I * 2 + H * 4)
     assert bat(64) < bat(128) == bat(256)
     assert bat(1024) == max(per(1024), bat(128))     # the size serves both paths
+
+
+def test_layer_path_choice_workspace(pkg):
+    """moe_decode_layer's `batched` choice is carried by the workspace size it hands the library: the
+    library's choice (batched from 64 tokens), forced from 16 tokens, or never."""
+    ml = pkg.moe_layer
+    lib = pkg._native.lib()
+    H, I, k = 4096, 1536, 8
+    per = lambda M: lib.w2a16_moe_layer_workspace_bytes(M, H, I, k)
+    for M in (1, 16, 40, 64, 200):
+        assert ml._workspace_bytes(M, H, I, k, 0) == per(M)
+        auto = ml._workspace_bytes(M, H, I, k, -1)
+        assert auto == max(per(M), lib.w2a16_moe_layer_workspace_bytes_batched(M, H, I, k))
+        forced = ml._workspace_bytes(M, H, I, k, 1)
+        assert forced >= auto
+    assert ml._workspace_bytes(16, H, I, k, -1) == per(16)        # per-token below 64 tokens
+    assert ml._workspace_bytes(16, H, I, k, 1) > per(16)          # room for the batched path from 16
+    assert ml._workspace_bytes(64, H, I, k, -1) > per(64)         # the batched path from 64
+    assert ml.BATCHED_MIN_TOKENS == 64
