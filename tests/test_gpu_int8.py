@@ -25,3 +25,18 @@ def test_int8_grouped_scales_and_repeat(pkg, golden, dev):
     for _ in range(2):
         y = pkg.int8_gemv(x.to(dev), qw, sc)
         assert O.max_rel_err(y.float().cpu(), ref) < 1e-2
+
+
+def test_int8_lm_head_sized(pkg, dev):
+    """An lm_head-sized projection, K = 4096 -> N = 151,936 (1,187 column blocks of 128), with g128 scales
+    and the checkpoint's zero point 128: a spread of column blocks checked against the oracle."""
+    K, N, M = 4096, 151936, 2
+    qw, sc1 = pkg.synth.make_int8_dense(K, N, seed=9, device=dev, gen_device=dev)
+    sc = (sc1.float().repeat(K // 128, 1) * torch.linspace(0.5, 1.5, K // 128, device=dev)[:, None]).to(torch.float16)
+    x = pkg.synth.make_activation(M, K, seed=9, device=dev, gen_device=dev)
+    y = pkg.int8_gemv(x, qw, sc)
+    torch.cuda.synchronize()
+    blocks = torch.tensor([0, 1, 500, 1000, 1186])
+    cols = (blocks[:, None] * 128 + torch.arange(128)[None]).reshape(-1).to(dev)
+    ref = O.int8_gemv(x.cpu(), qw[:, cols].cpu(), sc[:, cols].cpu())
+    assert O.max_rel_err(y[:, cols].float().cpu(), ref) < 1e-2
