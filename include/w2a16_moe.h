@@ -22,8 +22,9 @@
  *   w = (q - zp) * s.
  *
  * Device-side error word (`err`, optional, uint32 in device memory): bit 0 is set when an expert id
- * lies outside [0, num_experts), or when an arena slot id is 2^20 or larger; such rows contribute
- * zero. Bit 1 is set when a bounded wait inside a kernel gave up. Bit 2 is set when the decode layer's
+ * lies outside [0, num_experts), or when a slot table entry is num_slots or more (negative entries
+ * mean "not resident" and are not errors); such rows contribute zero and nothing outside the arena is
+ * read. Bit 1 is set when a bounded wait inside a kernel gave up. Bit 2 is set when the decode layer's
  * shared-memory ring is not 128-byte aligned (its copies are then skipped). The library never traps or
  * aborts.
  */
@@ -83,10 +84,11 @@ int w2a16_moe_gemv_tab(const void* a, int64_t stride_am,
  * (gemv/row_arena.py:34-123, table writes gemv/expert_elastic.py:157, :220, :242;
  * placed tables patches/placement.py:208-227): expert e lives at
  *   codes_base  + slots[e] * codes_slot_bytes   (likewise scales, zeros)
- * and slots[e] == -1 marks a non-resident expert whose rows contribute zero.
+ * and slots[e] == -1 marks a non-resident expert whose rows contribute zero. The arena holds
+ * num_slots slots; an entry of num_slots or more is treated like -1 and sets bit 0 of `err`.
  */
 int w2a16_moe_gemv_slots(const void* a, int64_t stride_am,
-                         const int32_t* slots, int num_experts,
+                         const int32_t* slots, int num_experts, int num_slots,
                          const void* codes_base, int64_t codes_slot_bytes,
                          const void* scales_base, int64_t scales_slot_bytes,
                          const void* zeros_base, int64_t zeros_slot_bytes,
@@ -101,16 +103,24 @@ size_t w2a16_moe_layer_workspace_bytes(int M, int H, int I, int top_k);
 
 /*
  * No counterpart in the reference (its batched path is the same Triton GEMV per routed row).
- * Workspace bytes with which w2a16_moe_decode_layer_slots takes its batched path where that path is the
- * faster one: from 64 tokens it returns the batched path's size (the routed rows grouped by expert, every
- * resident expert streamed once for all of its rows, the products on the tensor cores; route tables,
- * h [rows, I] bf16 and y rows [rows, H] fp32 for up to 128 tokens at a time); below 64 tokens it returns
- * w2a16_moe_layer_workspace_bytes (the per-token path). Any workspace at least as large as the batched
- * path's size for M tokens makes calls with M >= 16 take it; a smaller one runs the per-token path, as
- * does the int64-table entry point. The batched path keeps out of the per-token path's persistent
- * workspace words, so one workspace serves calls of either path.
+ * Workspace bytes of the batched path for M tokens (M >= 16): the routed rows grouped by expert, every
+ * resident expert streamed once for all of its rows, the products on the tensor cores (route tables,
+ * h [rows, I] bf16 and y rows [rows, H] fp32 for up to 128 tokens at a time), never less than
+ * w2a16_moe_layer_workspace_bytes. Below 16 tokens it returns w2a16_moe_layer_workspace_bytes. The
+ * batched path keeps out of the per-token path's persistent workspace words, so one workspace serves
+ * calls of either path.
  */
 size_t w2a16_moe_layer_workspace_bytes_batched(int M, int H, int I, int top_k);
+
+/* Path choice of the slot-table decode layer (w2a16_moe_decode_layer_slots_ex). AUTO follows the token
+ * count: the per-token path below W2A16_BATCHED_AUTO_TOKENS tokens, the batched path from there on when the
+ * workspace holds its buffers (else the per-token path). BATCHED takes the batched path from 16 tokens and
+ * returns W2A16_ERR_WORKSPACE when the workspace is too small for it (W2A16_ERR_SHAPE below 16 tokens or for
+ * shapes it does not support). PER_TOKEN always takes the per-token path. */
+#define W2A16_PATH_AUTO 0
+#define W2A16_PATH_PER_TOKEN 1
+#define W2A16_PATH_BATCHED 2
+#define W2A16_BATCHED_AUTO_TOKENS 64
 
 /*
  * Full decode MoE layer: gate_up GEMV, SiLU(gate) * up, down GEMV * routed weight, sum over the
@@ -135,10 +145,11 @@ int w2a16_moe_decode_layer_tab(const void* x, int M, int H, int I, int top_k,
                                void* y, void* workspace, size_t workspace_bytes,
                                unsigned int* err, void* stream);
 
-/* The decode layer over an int32 slot table into expert arenas (slot -1 = not resident). */
+/* The decode layer over an int32 slot table into expert arenas of num_slots slots (slot -1 = not resident;
+ * an entry of num_slots or more is treated like -1 and sets bit 0 of `err`). Path choice W2A16_PATH_AUTO. */
 int w2a16_moe_decode_layer_slots(const void* x, int M, int H, int I, int top_k,
                                  const int32_t* topk_ids, const float* topk_w,
-                                 const int32_t* slots, int num_experts,
+                                 const int32_t* slots, int num_experts, int num_slots,
                                  const void* codes13, int64_t codes13_slot_bytes,
                                  const void* scales13, int64_t scales13_slot_bytes,
                                  const void* zeros13, int64_t zeros13_slot_bytes,
@@ -148,6 +159,20 @@ int w2a16_moe_decode_layer_slots(const void* x, int M, int H, int I, int top_k,
                                  int scale_bf16, float routed_scaling_factor,
                                  void* y, void* workspace, size_t workspace_bytes,
                                  unsigned int* err, void* stream);
+
+/* w2a16_moe_decode_layer_slots with an explicit path choice (W2A16_PATH_*); no counterpart in the reference. */
+int w2a16_moe_decode_layer_slots_ex(const void* x, int M, int H, int I, int top_k,
+                                    const int32_t* topk_ids, const float* topk_w,
+                                    const int32_t* slots, int num_experts, int num_slots,
+                                    const void* codes13, int64_t codes13_slot_bytes,
+                                    const void* scales13, int64_t scales13_slot_bytes,
+                                    const void* zeros13, int64_t zeros13_slot_bytes,
+                                    const void* codes2, int64_t codes2_slot_bytes,
+                                    const void* scales2, int64_t scales2_slot_bytes,
+                                    const void* zeros2, int64_t zeros2_slot_bytes,
+                                    int scale_bf16, float routed_scaling_factor,
+                                    void* y, void* workspace, size_t workspace_bytes, int path,
+                                    unsigned int* err, void* stream);
 
 /*
  * No counterpart in the reference: this entry point exists only in this library.
@@ -160,15 +185,17 @@ int w2a16_moe_decode_layer_slots(const void* x, int M, int H, int I, int top_k,
  * array of W2A16_NOALLOC_SCRATCH_BYTES (4 MiB) inside the library that every GPU loading the library
  * holds until the process exits; layers needing more (w2a16_moe_layer_workspace_bytes(M, H, I, top_k)
  * > W2A16_NOALLOC_SCRATCH_BYTES; at I=1536, top-8 that is M > 146) return W2A16_ERR_WORKSPACE.
- * The first call on a device looks up that array's device address for the calling thread's current
- * device (which must own `stream`); make that first call before any stream capture. All calls share
- * the one array: calls that overlap on the GPU (different streams, or concurrent graph replays) race
+ * The first call in each CUDA context (once per device, and again after a device reset, which makes a
+ * new context) looks up that array's device address for the calling thread's current device (which must
+ * own `stream`); make that first call before any stream capture. The path choice is the one of
+ * w2a16_moe_decode_layer_slots with this much workspace (per-token below W2A16_BATCHED_AUTO_TOKENS tokens).
+ * All calls share the one array: calls that overlap on the GPU (different streams, or concurrent graph replays) race
  * and must not be issued.
  */
 #define W2A16_NOALLOC_SCRATCH_BYTES (4u << 20)
 int w2a16_moe_decode_layer_slots_noalloc(const void* x, int M, int H, int I, int top_k,
                                          const int32_t* topk_ids, const float* topk_w,
-                                         const int32_t* slots, int num_experts,
+                                         const int32_t* slots, int num_experts, int num_slots,
                                          const void* codes13, int64_t codes13_slot_bytes,
                                          const void* scales13, int64_t scales13_slot_bytes,
                                          const void* zeros13, int64_t zeros13_slot_bytes,

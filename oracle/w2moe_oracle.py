@@ -27,7 +27,7 @@ GROUP = 128
 __all__ = [
     "pack_2bit_along_last", "pack_words_along_k", "to_word_ncontig", "unpack_words",
     "pack_zeros", "zeros_to_ncontig", "unpack_zeros_nc", "dequant", "gemv_tab", "gemv_byte_tab",
-    "route_topk", "moe_layer", "moe_layer_routed_only", "int8_pack", "int8_unpack", "int8_gemv",
+    "route_topk", "moe_layer", "moe_layer_routed_only", "moe_layer_by_expert", "int8_pack", "int8_unpack", "int8_gemv",
     "bf16_round", "max_rel_err", "norm_rel_err", "time_cpu_layer", "cpu_info", "routed_experts_from_arena",
     "moe_layer_from_arena",
 ]
@@ -242,6 +242,42 @@ def routed_experts_from_arena(arena, ids) -> dict:
         experts[e] = (pick(arena.codes13), pick(arena.scales13), pick(arena.zeros13),
                       pick(arena.codes2), pick(arena.scales2), pick(arena.zeros2))
     return experts
+
+
+def moe_layer_by_expert(arena, x, topk_ids, topk_w, routed_scaling_factor: float = 1.0) -> torch.Tensor:
+    """fp32 [M, H]: the math of :func:`moe_layer_routed_only` (the reference's fp32 layer,
+    gemv/test_gemv_tab.py:73-76, with the composite of patches/ncontig_gemv.py:218-238) in expert order:
+    each distinct routed, resident expert is copied off the device and dequantised once and applied to
+    every token routed to it, so whole batches of tokens at full size can be checked. Per token the top-k
+    contributions are added in routing order, as in the token-order loop."""
+    M = x.shape[0]
+    ids = topk_ids.cpu().reshape(M, -1)
+    w = topk_w.cpu().reshape(M, -1)
+    k = ids.shape[1]
+    slots = arena.slots.cpu()
+    xs = x.cpu().float()
+    H = xs.shape[1]
+    contrib = torch.zeros(M, k, H, dtype=torch.float32)
+    for e in sorted(set(ids.reshape(-1).tolist())):
+        sl = int(slots[e]) if 0 <= e < slots.numel() else -1
+        if sl < 0 or sl >= arena.codes13.shape[0]:
+            continue
+        pick = lambda t: None if t is None else t[sl].cpu()
+        W13 = dequant(pick(arena.codes13), pick(arena.scales13), pick(arena.zeros13))
+        W2 = dequant(pick(arena.codes2), pick(arena.scales2), pick(arena.zeros2))
+        I = W13.shape[-1] // 2
+        where = (ids == e).nonzero().tolist()
+        toks = sorted({m for m, _ in where})
+        gu = xs[toks] @ W13                                  # [t, 2I]
+        h = _silu(gu[:, :I]) * gu[:, I:]
+        yd = h @ W2                                          # [t, H]
+        row = {m: i for i, m in enumerate(toks)}
+        for m, j in where:
+            contrib[m, j] = float(w[m, j]) * yd[row[m]]
+    y = torch.zeros(M, H, dtype=torch.float32)
+    for j in range(k):
+        y += contrib[:, j]
+    return y * float(routed_scaling_factor)
 
 
 def moe_layer_from_arena(arena, x, topk_ids, topk_w, routed_scaling_factor: float = 1.0) -> torch.Tensor:

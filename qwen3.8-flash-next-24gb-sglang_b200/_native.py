@@ -12,6 +12,10 @@ import threading
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "lib", "libw2a16_moe.so")
 
+# path choice of w2a16_moe_decode_layer_slots_ex (include/w2a16_moe.h)
+PATH_AUTO, PATH_PER_TOKEN, PATH_BATCHED = 0, 1, 2
+BATCHED_AUTO_TOKENS = 64
+
 STATUS = {
     0: "ok", 1: "unsupported shape", 2: "misaligned stride or base address", 3: "CUDA launch failed",
     4: "invalid argument", 5: "workspace missing or too small", 6: "no usable sm_100 device",
@@ -24,18 +28,22 @@ SIGNATURES = {
     "w2a16_status_string": (ctypes.c_char_p, [c_i32]),
     "w2a16_moe_gemv_tab": (c_i32, [c_vp, c_i64, c_vp, c_vp, c_vp, c_i32, c_vp, c_vp, c_vp, c_i64,
                                    c_i32, c_i32, c_i32, c_i64, c_i64, c_i64, c_i32, c_i32, c_i32, c_vp, c_vp]),
-    "w2a16_moe_gemv_slots": (c_i32, [c_vp, c_i64, c_vp, c_i32, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64,
+    "w2a16_moe_gemv_slots": (c_i32, [c_vp, c_i64, c_vp, c_i32, c_i32, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64,
                                      c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp]),
     "w2a16_moe_layer_workspace_bytes": (c_sz, [c_i32, c_i32, c_i32, c_i32]),
     "w2a16_moe_layer_workspace_bytes_batched": (c_sz, [c_i32, c_i32, c_i32, c_i32]),
     "w2a16_moe_decode_layer_tab": (c_i32, [c_vp, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp, c_i32,
                                            c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i32, c_f32,
                                            c_vp, c_vp, c_sz, c_vp, c_vp]),
-    "w2a16_moe_decode_layer_slots": (c_i32, [c_vp, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp, c_vp, c_i32,
+    "w2a16_moe_decode_layer_slots": (c_i32, [c_vp, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp, c_vp, c_i32, c_i32,
                                              c_vp, c_i64, c_vp, c_i64, c_vp, c_i64,
                                              c_vp, c_i64, c_vp, c_i64, c_vp, c_i64,
                                              c_i32, c_f32, c_vp, c_vp, c_sz, c_vp, c_vp]),
-    "w2a16_moe_decode_layer_slots_noalloc": (c_i32, [c_vp, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp, c_vp, c_i32,
+    "w2a16_moe_decode_layer_slots_ex": (c_i32, [c_vp, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp, c_vp, c_i32, c_i32,
+                                                c_vp, c_i64, c_vp, c_i64, c_vp, c_i64,
+                                                c_vp, c_i64, c_vp, c_i64, c_vp, c_i64,
+                                                c_i32, c_f32, c_vp, c_vp, c_sz, c_i32, c_vp, c_vp]),
+    "w2a16_moe_decode_layer_slots_noalloc": (c_i32, [c_vp, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp, c_vp, c_i32, c_i32,
                                                      c_vp, c_i64, c_vp, c_i64, c_vp, c_i64,
                                                      c_vp, c_i64, c_vp, c_i64, c_vp, c_i64,
                                                      c_i32, c_f32, c_vp, c_vp, c_vp]),

@@ -10,7 +10,8 @@
 //   1. write the local partial into row my_rank of slot e & 1 of EVERY rank's buffer (NVLink stores);
 //   2. one system-scope acq_rel fence after the CTA barrier, then store e into flag[my_rank] of every rank
 //      (release);
-//   3. wait until this rank's own flags hold e from every rank (acquire, bounded);
+//   3. wait until this rank's own flags hold e or later from every rank (acquire, bounded; signed distance,
+//      because a faster rank may already have finished call e and raised its flag to e + 1);
 //   4. sum the world rows of this rank's own slot in rank order 0..N-1 in fp32 -> bf16 out (local reads;
 //      the same order on every rank, so every rank gets bit-identical sums).
 // A rank writes call e's rows only after it saw every rank's call e-1 flag, which each rank raises only
@@ -67,7 +68,9 @@ __global__ void __launch_bounds__(kArThreads, 1) allreduce_kernel(ArParams p) {
     st_release_sys(peer_flags + p.rank, e);
     const unsigned* own_flags = reinterpret_cast<const unsigned*>(p.bufs[p.rank] + p.flag_off);
     unsigned it = 0;
-    while (ld_acquire_sys(own_flags + threadIdx.x) != e) {  // rank threadIdx.x's call-e row is in place
+    // rank threadIdx.x's call-e row is in place once its flag reached e: a flag already at e + 1 means that
+    // rank finished call e too (it cannot reach e + 2 before this rank has read call e's slot)
+    while ((int)(ld_acquire_sys(own_flags + threadIdx.x) - e) < 0) {
       if (++it > kArSpinLimit) {
         flag_error(p.err, 2u);
         break;

@@ -15,10 +15,10 @@ ExpertMap table_map(const int64_t* wtab, const int64_t* stab, const int64_t* zta
   return m;
 }
 
-ExpertMap slot_map(const int32_t* slots, int E, const void* cb, int64_t cs, const void* sb, int64_t ss,
+ExpertMap slot_map(const int32_t* slots, int E, int S, const void* cb, int64_t cs, const void* sb, int64_t ss,
                    const void* zb, int64_t zs) {
   ExpertMap m{};
-  m.slots = slots; m.E = E;
+  m.slots = slots; m.E = E; m.S = S;
   m.wbase = static_cast<const char*>(cb); m.wstride = cs;
   m.sbase = static_cast<const char*>(sb); m.sstride = ss;
   m.zbase = static_cast<const char*>(zb); m.zstride = zs;
@@ -63,16 +63,16 @@ int w2a16_moe_gemv_tab(const void* a, int64_t stride_am, const int64_t* wtab, co
   return gemv_plain(g);
 }
 
-int w2a16_moe_gemv_slots(const void* a, int64_t stride_am, const int32_t* slots, int num_experts,
+int w2a16_moe_gemv_slots(const void* a, int64_t stride_am, const int32_t* slots, int num_experts, int num_slots,
                          const void* codes_base, int64_t codes_slot_bytes, const void* scales_base,
                          int64_t scales_slot_bytes, const void* zeros_base, int64_t zeros_slot_bytes,
                          const int32_t* topk_ids, const float* topk_w, void* c, int64_t stride_cm, int R, int N,
                          int K, int top_k, int mul_routed_weight, int scale_bf16, unsigned int* err, void* stream) {
-  if (!slots || num_experts <= 0 || !codes_base || !scales_base) return W2A16_ERR_ARG;
+  if (!slots || num_experts <= 0 || num_slots <= 0 || !codes_base || !scales_base) return W2A16_ERR_ARG;
   if (!a16(codes_base) || !a16(scales_base) || codes_slot_bytes % 16 || scales_slot_bytes % 16) return W2A16_ERR_ALIGN;
   GemvArgs g{};
   g.a = a; g.stride_am = stride_am;
-  g.map = slot_map(slots, num_experts, codes_base, codes_slot_bytes, scales_base, scales_slot_bytes, zeros_base,
+  g.map = slot_map(slots, num_experts, num_slots, codes_base, codes_slot_bytes, scales_base, scales_slot_bytes, zeros_base,
                    zeros_slot_bytes);
   g.ids = topk_ids; g.topk_w = topk_w; g.out = c; g.stride_om = stride_cm;
   g.R = R; g.N = N; g.K = K; g.top_k = top_k;
@@ -87,7 +87,7 @@ size_t w2a16_moe_layer_workspace_bytes(int M, int H, int I, int top_k) {
 
 size_t w2a16_moe_layer_workspace_bytes_batched(int M, int H, int I, int top_k) {
   const size_t a = layer_workspace_bytes(M, H, I, top_k);
-  if (M < kGroupedAutoTokens) return a;
+  if (M < kGroupedMinTokens) return a;
   const size_t b = grouped_workspace_bytes(M, H, I, top_k);
   return a > b ? a : b;
 }
@@ -108,15 +108,17 @@ int w2a16_moe_decode_layer_tab(const void* x, int M, int H, int I, int top_k, co
   return decode_layer_fused(a);
 }
 
-int w2a16_moe_decode_layer_slots(const void* x, int M, int H, int I, int top_k, const int32_t* topk_ids,
-                                 const float* topk_w, const int32_t* slots, int num_experts, const void* codes13,
-                                 int64_t codes13_slot_bytes, const void* scales13, int64_t scales13_slot_bytes,
-                                 const void* zeros13, int64_t zeros13_slot_bytes, const void* codes2,
-                                 int64_t codes2_slot_bytes, const void* scales2, int64_t scales2_slot_bytes,
-                                 const void* zeros2, int64_t zeros2_slot_bytes, int scale_bf16,
-                                 float routed_scaling_factor, void* y, void* workspace, size_t workspace_bytes,
-                                 unsigned int* err, void* stream) {
-  if (!slots || num_experts <= 0 || !codes13 || !scales13 || !codes2 || !scales2) return W2A16_ERR_ARG;
+int w2a16_moe_decode_layer_slots_ex(const void* x, int M, int H, int I, int top_k, const int32_t* topk_ids,
+                                    const float* topk_w, const int32_t* slots, int num_experts, int num_slots,
+                                    const void* codes13, int64_t codes13_slot_bytes, const void* scales13,
+                                    int64_t scales13_slot_bytes, const void* zeros13, int64_t zeros13_slot_bytes,
+                                    const void* codes2, int64_t codes2_slot_bytes, const void* scales2,
+                                    int64_t scales2_slot_bytes, const void* zeros2, int64_t zeros2_slot_bytes,
+                                    int scale_bf16, float routed_scaling_factor, void* y, void* workspace,
+                                    size_t workspace_bytes, int path, unsigned int* err, void* stream) {
+  if (!slots || num_experts <= 0 || num_slots <= 0 || !codes13 || !scales13 || !codes2 || !scales2)
+    return W2A16_ERR_ARG;
+  if (path != W2A16_PATH_AUTO && path != W2A16_PATH_PER_TOKEN && path != W2A16_PATH_BATCHED) return W2A16_ERR_ARG;
   if ((zeros13 == nullptr) != (zeros2 == nullptr)) return W2A16_ERR_ARG;
   if (!a16(codes13) || !a16(scales13) || !a16(codes2) || !a16(scales2)) return W2A16_ERR_ALIGN;
   if (codes13_slot_bytes % 16 || scales13_slot_bytes % 16 || codes2_slot_bytes % 16 || scales2_slot_bytes % 16)
@@ -125,20 +127,39 @@ int w2a16_moe_decode_layer_slots(const void* x, int M, int H, int I, int top_k, 
     return W2A16_ERR_ALIGN;
   LayerArgs a{};
   a.x = x; a.M = M; a.H = H; a.I = I; a.top_k = top_k; a.ids = topk_ids; a.topk_w = topk_w;
-  a.map13 = slot_map(slots, num_experts, codes13, codes13_slot_bytes, scales13, scales13_slot_bytes, zeros13,
-                     zeros13_slot_bytes);
-  a.map2 = slot_map(slots, num_experts, codes2, codes2_slot_bytes, scales2, scales2_slot_bytes, zeros2,
+  a.map13 = slot_map(slots, num_experts, num_slots, codes13, codes13_slot_bytes, scales13, scales13_slot_bytes,
+                     zeros13, zeros13_slot_bytes);
+  a.map2 = slot_map(slots, num_experts, num_slots, codes2, codes2_slot_bytes, scales2, scales2_slot_bytes, zeros2,
                     zeros2_slot_bytes);
   a.scale_bf16 = scale_bf16; a.routed_scaling = routed_scaling_factor; a.y = y;
   a.workspace = workspace; a.workspace_bytes = workspace_bytes; a.err = err; a.stream = as_stream(stream);
-  // M >= 16 with a workspace of w2a16_moe_layer_workspace_bytes_batched: experts grouped over the tokens on
-  // the tensor cores (each expert streamed once); otherwise, or when the arena maps do not qualify, the
-  // per-token fused layer.
-  if (grouped_eligible(a)) {
+  // The batched path (experts grouped over the tokens, each streamed once, products on the tensor cores) by
+  // token count: from W2A16_BATCHED_AUTO_TOKENS tokens in AUTO mode when the workspace holds its buffers, from
+  // 16 tokens when asked for; otherwise the per-token fused layer.
+  if (path == W2A16_PATH_BATCHED) {
+    const int st = grouped_check(a);
+    return st == kOk ? decode_layer_grouped(a) : st;
+  }
+  if (path == W2A16_PATH_AUTO && M >= W2A16_BATCHED_AUTO_TOKENS && grouped_check(a) == kOk) {
     const int st = decode_layer_grouped(a);
     if (st != kErrShape) return st;
   }
   return decode_layer_fused(a);
+}
+
+int w2a16_moe_decode_layer_slots(const void* x, int M, int H, int I, int top_k, const int32_t* topk_ids,
+                                 const float* topk_w, const int32_t* slots, int num_experts, int num_slots,
+                                 const void* codes13, int64_t codes13_slot_bytes, const void* scales13,
+                                 int64_t scales13_slot_bytes, const void* zeros13, int64_t zeros13_slot_bytes,
+                                 const void* codes2, int64_t codes2_slot_bytes, const void* scales2,
+                                 int64_t scales2_slot_bytes, const void* zeros2, int64_t zeros2_slot_bytes,
+                                 int scale_bf16, float routed_scaling_factor, void* y, void* workspace,
+                                 size_t workspace_bytes, unsigned int* err, void* stream) {
+  return w2a16_moe_decode_layer_slots_ex(x, M, H, I, top_k, topk_ids, topk_w, slots, num_experts, num_slots, codes13,
+                                         codes13_slot_bytes, scales13, scales13_slot_bytes, zeros13,
+                                         zeros13_slot_bytes, codes2, codes2_slot_bytes, scales2, scales2_slot_bytes,
+                                         zeros2, zeros2_slot_bytes, scale_bf16, routed_scaling_factor, y, workspace,
+                                         workspace_bytes, W2A16_PATH_AUTO, err, stream);
 }
 
 int w2a16_to_word_ncontig(const void* src_u8, void* dst_i32, int E, int N, int K, void* stream) {

@@ -40,8 +40,8 @@ enum Status : int {
   kErrDevice = 6,
 };
 
-// Device-side error word: bit 0 = an expert id outside [0, E) (or an arena slot id >= 2^20), bit 1 =
-// a bounded wait gave up, bit 2 = a misaligned shared-memory ring (copies skipped).
+// Device-side error word: bit 0 = an expert id outside [0, E) or an arena slot id outside [-1, S) (the row
+// contributes zero), bit 1 = a bounded wait gave up, bit 2 = a misaligned shared-memory ring (copies skipped).
 __device__ __forceinline__ void flag_error(unsigned* err, unsigned bit) {
   if (err) atomicOr(err, bit);
 }
@@ -220,7 +220,9 @@ __device__ __forceinline__ void prep_group_regs(const float (&v)[4], int gl, XTa
 
 // ----------------------------------------------------------------------------- expert addressing
 // Either the reference's int64 address tables (make_tables, gemv/moe_gemv_int2_tab.py:88-97) or the
-// arena form: base + slot[e] * stride, slot -1 = expert not resident -> the row contributes zero.
+// arena form: base + slot[e] * stride, slot -1 = expert not resident -> the row contributes zero. An arena
+// holds S slots; a slot id of S or more is treated like -1 and sets bit 0 of the error word, so a corrupt
+// slot table never reads past the arena.
 struct ExpertMap {
   const int64_t* wtab;
   const int64_t* stab;
@@ -233,6 +235,7 @@ struct ExpertMap {
   int64_t sstride;
   int64_t zstride;
   int E;
+  int S;            // arena slots (slot form only)
   int has_zeros;
 
   __device__ __forceinline__ bool resolve(int e, const uint32_t*& w, const char*& s, const uint8_t*& z,
@@ -244,6 +247,10 @@ struct ExpertMap {
     if (slots != nullptr) {
       const int sl = slots[e];
       if (sl < 0) return false;
+      if (sl >= S) {
+        flag_error(err, 1u);
+        return false;
+      }
       w = reinterpret_cast<const uint32_t*>(wbase + (int64_t)sl * wstride);
       s = sbase + (int64_t)sl * sstride;
       z = has_zeros ? reinterpret_cast<const uint8_t*>(zbase + (int64_t)sl * zstride) : nullptr;
@@ -256,8 +263,13 @@ struct ExpertMap {
   }
 
   // Arena form with the slot of expert e already looked up (e in [0, E) checked by the caller).
-  __device__ __forceinline__ bool resolve_slot(int sl, const uint32_t*& w, const char*& s, const uint8_t*& z) const {
+  __device__ __forceinline__ bool resolve_slot(int sl, const uint32_t*& w, const char*& s, const uint8_t*& z,
+                                               unsigned* err) const {
     if (sl < 0) return false;
+    if (sl >= S) {
+      flag_error(err, 1u);
+      return false;
+    }
     w = reinterpret_cast<const uint32_t*>(wbase + (int64_t)sl * wstride);
     s = sbase + (int64_t)sl * sstride;
     z = has_zeros ? reinterpret_cast<const uint8_t*>(zbase + (int64_t)sl * zstride) : nullptr;

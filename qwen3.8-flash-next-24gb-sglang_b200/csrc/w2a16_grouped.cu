@@ -57,7 +57,6 @@ constexpr int kGUStage = 8832, kGUScale = 8192, kGUZero = 8704;
 constexpr int kDNStage = 17664, kDNScale = 16384, kDNZero = 17408;
 constexpr int kMaxGroupedRows = 1024;            // routed rows per launch
 constexpr int kGroupedChunk = 128;               // tokens per launch
-constexpr int kSlotLimit = 1 << 20;              // slot ids the arena tensor maps accept
 constexpr unsigned kGWait = 1u << 17;            // suspending mbarrier tries before a wait gives up
 constexpr int kNB = 4;                           // operand / accumulator buffers in flight
 constexpr int kTmemCols = 512;                   // A: kNB buffers of kAcols columns; then kNB accumulators of kGN
@@ -155,7 +154,7 @@ __device__ __forceinline__ uint64_t kmajor_desc(uint32_t addr) {
 __device__ __forceinline__ int canon_off(int row, int half) { return (row >> 3) * 256 + half * 128 + (row & 7) * 16; }
 
 // ----------------------------------------------------------------------------------------------- routing
-__global__ void __launch_bounds__(1024) route_kernel(const int32_t* ids, const int32_t* slots, int E, int R,
+__global__ void __launch_bounds__(1024) route_kernel(const int32_t* ids, const int32_t* slots, int E, int S, int R,
                                                      int* route, unsigned* err) {
   __shared__ int key[kMaxGroupedRows];
   __shared__ int srt[kMaxGroupedRows];
@@ -169,7 +168,7 @@ __global__ void __launch_bounds__(1024) route_kernel(const int32_t* ids, const i
       flag_error(err, 1u);
     } else {
       sl = slots[e];
-      if (sl >= kSlotLimit) {
+      if (sl >= S) {                                   // past the arena: masked, flagged
         flag_error(err, 1u);
         sl = -1;
       }
@@ -515,7 +514,7 @@ __global__ void __launch_bounds__(kGThreads, 1) proj_kernel(const __grid_constan
 }
 
 // y[m, c] = routed_scaling * sum over the token's live routed rows (routing order) of y rows.
-__global__ void sum_kernel(const float* yrows, const int32_t* ids, const int32_t* slots, int E, int M, int H,
+__global__ void sum_kernel(const float* yrows, const int32_t* ids, const int32_t* slots, int E, int S, int M, int H,
                            int top_k, float rsf, __nv_bfloat16* y) {
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (int64_t)M * H) return;
@@ -525,7 +524,7 @@ __global__ void sum_kernel(const float* yrows, const int32_t* ids, const int32_t
     const int r = m * top_k + j, e = ids[r];
     if (e < 0 || e >= E) continue;
     const int sl = slots[e];
-    if (sl >= 0 && sl < kSlotLimit) a += yrows[(int64_t)r * H + c];
+    if (sl >= 0 && sl < S) a += yrows[(int64_t)r * H + c];
   }
   y[idx] = __float2bfloat16(a * rsf);
 }
@@ -549,15 +548,15 @@ size_t grouped_workspace_bytes(int M, int H, int I, int top_k) {
          align256(R * H * 4);
 }
 
-bool grouped_eligible(const LayerArgs& a) {
-  if (a.M < kGroupedMinTokens || a.top_k <= 0 || a.top_k > kMaxGroupedRows) return false;
-  if (a.map13.slots == nullptr || a.map13.slots != a.map2.slots || a.map13.E != a.map2.E) return false;
-  if (a.H % kTileCols != 0 || a.I % 64 != 0) return false;
-  if (reinterpret_cast<uintptr_t>(a.x) & 15u) return false;
-  if (a.workspace == nullptr || (reinterpret_cast<uintptr_t>(a.workspace) & 255u) ||
-      a.workspace_bytes < grouped_workspace_bytes(a.M, a.H, a.I, a.top_k))
-    return false;
-  return true;
+int grouped_check(const LayerArgs& a) {
+  if (a.M < kGroupedMinTokens || a.top_k <= 0 || a.top_k > kMaxGroupedRows) return kErrShape;
+  if (a.map13.slots == nullptr || a.map13.slots != a.map2.slots || a.map13.E != a.map2.E) return kErrShape;
+  if (a.H % kTileCols != 0 || a.I % 64 != 0) return kErrShape;
+  if (reinterpret_cast<uintptr_t>(a.x) & 15u) return kErrAlign;
+  if (a.workspace == nullptr || a.workspace_bytes < grouped_workspace_bytes(a.M, a.H, a.I, a.top_k))
+    return kErrWorkspace;
+  if (reinterpret_cast<uintptr_t>(a.workspace) & 255u) return kErrAlign;
+  return kOk;
 }
 
 int decode_layer_grouped(const LayerArgs& a) {
@@ -587,7 +586,7 @@ int decode_layer_grouped(const LayerArgs& a) {
     const int mc = a.M - m0 < mc_max ? a.M - m0 : mc_max;
     const int R = mc * a.top_k;
     const int32_t* ids = a.ids + (size_t)m0 * a.top_k;
-    route_kernel<<<1, 1024, 0, a.stream>>>(ids, a.map13.slots, a.map13.E, R, route, a.err);
+    route_kernel<<<1, 1024, 0, a.stream>>>(ids, a.map13.slots, a.map13.E, a.map13.S, R, route, a.err);
     ProjParams gu{};
     gu.tm[0] = tm[0]; gu.tm[1] = tm[1]; gu.tm[2] = tm[2];
     gu.route = route; gu.R = R;
@@ -606,7 +605,7 @@ int decode_layer_grouped(const LayerArgs& a) {
     dn.topk_w = a.topk_w + (size_t)m0 * a.top_k; dn.yrows = yrows; dn.err = a.err;
     proj_kernel<false><<<sms, kGThreads, proj_smem(false), a.stream>>>(dn);
     const int64_t n = (int64_t)mc * a.H;
-    sum_kernel<<<(unsigned)((n + 255) / 256), 256, 0, a.stream>>>(yrows, ids, a.map13.slots, a.map13.E, mc, a.H,
+    sum_kernel<<<(unsigned)((n + 255) / 256), 256, 0, a.stream>>>(yrows, ids, a.map13.slots, a.map13.E, a.map13.S, mc, a.H,
                                                                   a.top_k, a.routed_scaling,
                                                                   static_cast<__nv_bfloat16*>(a.y) + (size_t)m0 * a.H);
     if (cudaGetLastError() != cudaSuccess) return kErrLaunch;

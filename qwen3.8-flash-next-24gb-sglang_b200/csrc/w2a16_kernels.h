@@ -47,14 +47,13 @@ int decode_layer_fused(const LayerArgs& a);
 // down); false when the arena does not qualify (no slot table, H or I not a multiple of 64, no encoder).
 bool layer_arena_maps(const LayerArgs& a, CUtensorMap (&tm)[6]);
 
-// Batched layer on the tensor cores (w2a16_grouped.cu): M >= kGroupedMinTokens, slot arenas only.
+// Batched layer on the tensor cores (w2a16_grouped.cu): M >= kGroupedMinTokens, slot arenas only. The C ABI's
+// automatic choice takes it from W2A16_BATCHED_AUTO_TOKENS tokens, where it is the faster one.
 constexpr int kGroupedMinTokens = 16;
-// From this many tokens the batched path is the faster one (measured at H=4096, I=1536, E=256, top-8: 0.87x
-// of the per-token path at 48 tokens, 1.07x at 64, 1.84x at 128), so the batched workspace size asks for it.
-constexpr int kGroupedAutoTokens = 64;
 size_t grouped_workspace_bytes(int M, int H, int I, int top_k);
-// 1 when the grouped path takes this call (slot arena, M large enough, the workspace holds its buffers).
-bool grouped_eligible(const LayerArgs& a);
+// kOk when the grouped path can take this call; kErrShape (token count, table form or shape), kErrAlign or
+// kErrWorkspace (the workspace does not hold its buffers) otherwise.
+int grouped_check(const LayerArgs& a);
 int decode_layer_grouped(const LayerArgs& a);
 int allreduce_peers_bf16(const void* in, void* out, int n, int n_max, const uint64_t* bufs, size_t flag_off, int rank,
                          int world, unsigned* epoch, unsigned* err, cudaStream_t stream);

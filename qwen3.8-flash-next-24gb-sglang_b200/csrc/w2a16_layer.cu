@@ -49,7 +49,6 @@ constexpr int kStageBytes = 4480;
 constexpr int kScaleOff = 4096;
 constexpr int kZeroOff = 4352;
 constexpr int kMinStages = 16, kMaxStages = 48;             // multiples of kIssuers
-constexpr int kSlotExtent = 1 << 20;                         // slot ids the arena tensor maps accept
 
 constexpr unsigned kSpinLimit = 1u << 22;                    // polls before a wait gives up
 constexpr unsigned kWaitLimit = 1u << 17;                    // suspending mbarrier tries before a wait gives up
@@ -573,7 +572,7 @@ __device__ __forceinline__ int4 item_desc(const Geo& g, const LiveRows& lv, cons
                                           SlotOf slot_of, int i) {
   const Work w = cta_item(g, lv, L0, cta, i);
   const int sl = w.dead ? -1 : slot_of(w.r, w.kind);
-  const bool live = sl >= 0 && sl < kSlotExtent;
+  const bool live = sl >= 0;                                  // slot_of returns -1 for slots >= S
   return make_int4(live ? w.kind : 0, sl, w.b, w.kp);
 }
 
@@ -931,15 +930,15 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
       const bool in = e >= 0 && e < p.map13.E;
       if (!in) flag_error(p.err, 1u);
       const int sl = in ? sltab[e] : -1;
-      rp.ok[0] = in && p.map13.resolve_slot(sl, rp.w[0], rp.s[0], rp.z[0]);
-      rp.ok[1] = in && p.map2.resolve_slot(sl, rp.w[1], rp.s[1], rp.z[1]);
-      rp.slot = sl;
+      rp.ok[0] = in && p.map13.resolve_slot(sl, rp.w[0], rp.s[0], rp.z[0], p.err);
+      rp.ok[1] = in && p.map2.resolve_slot(sl, rp.w[1], rp.s[1], rp.z[1], nullptr);
+      rp.slot = sl < p.map13.S ? sl : -1;
     } else {
       rp.ok[0] = p.map13.resolve(e, rp.w[0], rp.s[0], rp.z[0], p.err);
       rp.ok[1] = p.map2.resolve(e, rp.w[1], rp.s[1], rp.z[1], p.err);
       rp.slot = (p.map13.slots != nullptr && e >= 0 && e < p.map13.E) ? p.map13.slots[e] : -1;
+      if (rp.slot >= p.map13.S) rp.slot = -1;                 // (resolve flagged it)
     }
-    if (kTma && rp.slot >= kSlotExtent) flag_error(p.err, 1u);
     rows[r] = rp;
   };
   if (one_warp) {
@@ -1064,7 +1063,7 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
       __syncwarp();
       const bool in = lane < g.R && e >= 0 && e < p.map13.E;
       const int sl = in ? pstab[e] : -1;
-      const bool live = in && sl >= 0;
+      const bool live = in && sl >= 0 && sl < p.map13.S;      // the rule resolve_slot applies
       const unsigned bal = __ballot_sync(0xffffffffu, live);
       pslot[lane] = live ? sl : -1;
       if (live) prow[__popc(bal & ((1u << lane) - 1u))] = lane;
@@ -1235,11 +1234,11 @@ bool arena_maps(const LayerArgs& a, CUtensorMap (&tm)[6]) {
   struct Key {
     const void* b[6];
     int64_t st[6];
-    int H, I;
+    int H, I, S;
     bool operator==(const Key& o) const {
       for (int k = 0; k < 6; ++k)
         if (b[k] != o.b[k] || st[k] != o.st[k]) return false;
-      return H == o.H && I == o.I;
+      return H == o.H && I == o.I && S == o.S;
     }
   };
   static thread_local Key last{};
@@ -1247,11 +1246,12 @@ bool arena_maps(const LayerArgs& a, CUtensorMap (&tm)[6]) {
   static thread_local CUtensorMap cache[6];
   const Key k{{a.map13.wbase, a.map13.sbase, a.map13.zbase, a.map2.wbase, a.map2.sbase, a.map2.zbase},
               {a.map13.wstride, a.map13.sstride, a.map13.zstride, a.map2.wstride, a.map2.sstride, a.map2.zstride},
-              a.H, a.I};
+              a.H, a.I, a.map13.S};
   if (!(have && last == k)) {
     have = false;
     if (!tensor_map_encoder()) return false;
-    const cuuint64_t I = (cuuint64_t)a.I, H = (cuuint64_t)a.H, S = kSlotExtent;
+    // the slot dimension is the arena's real slot count: a copy can never leave the arena
+    const cuuint64_t I = (cuuint64_t)a.I, H = (cuuint64_t)a.H, S = (cuuint64_t)a.map13.S;
     const bool hz = a.map13.has_zeros != 0;
     {  // gate_up: (column within half, half, row, slot)
       const cuuint64_t dc[4] = {I, 2, H / 16, S}, sc[3] = {I * 4, 2 * I * 4, (cuuint64_t)a.map13.wstride};
@@ -1289,7 +1289,7 @@ bool arena_maps(const LayerArgs& a, CUtensorMap (&tm)[6]) {
 // Copy-engine mode needs a slot arena, 16-byte strides in every map (H and I multiples of 64) and the
 // driver's tensor-map encoder.
 bool tma_eligible(const LayerArgs& a) {
-  if (a.map13.slots == nullptr || a.map2.slots == nullptr) return false;
+  if (a.map13.slots == nullptr || a.map2.slots == nullptr || a.map13.S <= 0 || a.map13.S != a.map2.S) return false;
   if (a.H % 64 != 0 || a.I % 64 != 0) return false;
   return tensor_map_encoder() != nullptr;
 }

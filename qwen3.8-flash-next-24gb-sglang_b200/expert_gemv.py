@@ -176,7 +176,7 @@ def _gemv_slots(a: torch.Tensor, slots: torch.Tensor, codes: torch.Tensor, scale
     c = torch.empty((R, N), dtype=torch.bfloat16, device=a.device)
     if R == 0:
         return c
-    _native.call("w2a16_moe_gemv_slots", a.data_ptr(), a.stride(0), slots.data_ptr(), slots.numel(),
+    _native.call("w2a16_moe_gemv_slots", a.data_ptr(), a.stride(0), slots.data_ptr(), slots.numel(), codes.shape[0],
                  codes.data_ptr(), codes.stride(0) * 4, scales.data_ptr(), scales.stride(0) * scales.element_size(),
                  _p(zeros), 0 if zeros is None else zeros.stride(0), topk_ids.data_ptr(), _p(topk_w),
                  c.data_ptr(), c.stride(0), R, N, K, top_k, int(mul_routed_weight),

@@ -79,6 +79,16 @@ class PeerAllReduce:
         torch.cuda.synchronize(device)
         dist.barrier(group=self.group)
 
+    def check(self) -> int:
+        """Read and clear the kernel's device error word (bit 1: a flag wait gave up, i.e. a rank did not
+        arrive within the wait limit). Synchronises with the device: call it between steps, outside graph
+        capture. Raises RuntimeError when a bit is set, so a stalled peer does not go unnoticed."""
+        v = int(self.err.item())
+        if v:
+            self.err.zero_()
+            raise RuntimeError(f"peer all-reduce: device error word {v:#x} (bit 1 = a rank's flag never arrived)")
+        return v
+
     def __call__(self, y: torch.Tensor) -> torch.Tensor:
         if y.dtype != torch.bfloat16 or not y.is_contiguous() or y.numel() > self.n_max:
             raise ValueError("PeerAllReduce takes a contiguous bf16 tensor of at most n_max elements")

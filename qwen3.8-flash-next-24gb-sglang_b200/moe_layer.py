@@ -66,8 +66,13 @@ class ExpertArena:
             raise ValueError("scales must be f16 or bf16 (both tensors the same)")
         if (self.zeros13 is None) != (self.zeros2 is None):
             raise ValueError("zeros13 and zeros2 must both be given or both be None")
+        S = self.codes13.shape[0]
+        for n in ("scales13", "codes2", "scales2", "zeros13", "zeros2"):
+            t = getattr(self, n)
+            if t is not None and t.shape[0] != S:
+                raise ValueError(f"{n} holds {t.shape[0]} slots, codes13 {S}: every arena tensor needs the same slots")
         if self.slots is None:
-            self.slots = torch.arange(self.codes13.shape[0], dtype=torch.int32, device=self.codes13.device)
+            self.slots = torch.arange(S, dtype=torch.int32, device=self.codes13.device)
         if self.slots.dtype != torch.int32 or not self.slots.is_cuda:
             raise ValueError("slots must be an int32 CUDA tensor")
 
@@ -103,23 +108,31 @@ class ExpertArena:
 _WS_BYTES = {}
 
 
-BATCHED_MIN_TOKENS = 64   # the library's own choice: the batched path from this many tokens
+BATCHED_MIN_TOKENS = _native.BATCHED_AUTO_TOKENS   # the library's own choice: the batched path from here
+BATCHED_FORCE_MIN_TOKENS = 16                      # the batched path's smallest token count
+
+
+def _path(M: int, batched: int) -> int:
+    """C-ABI path choice for a slot-form call. batched -1: the library's choice by token count (the batched
+    path from BATCHED_MIN_TOKENS tokens, where it is the faster one); 1: the batched path from 16 tokens (the
+    per-token path below); 0: the per-token path."""
+    if batched == 0 or (batched == 1 and M < BATCHED_FORCE_MIN_TOKENS):
+        return _native.PATH_PER_TOKEN
+    return _native.PATH_BATCHED if batched == 1 else _native.PATH_AUTO
 
 
 def _workspace_bytes(M: int, H: int, I: int, top_k: int, batched: int = -1) -> int:
-    """Workspace bytes of a slot-form layer call. batched -1: the library's choice (the batched path from
-    BATCHED_MIN_TOKENS tokens, where it is the faster one); 1: the batched path from 16 tokens; 0: the
-    per-token path."""
+    """Workspace bytes of a slot-form layer call taking the path _path(M, batched) chooses: the batched path's
+    size where that path runs, else the per-token path's."""
     key = (M, H, I, top_k, batched)
     n = _WS_BYTES.get(key)
     if n is None:
         lib = _native.lib()
-        if batched == 0:
-            n = int(lib.w2a16_moe_layer_workspace_bytes(M, H, I, top_k))
+        path = _path(M, batched)
+        if path == _native.PATH_BATCHED or (path == _native.PATH_AUTO and M >= BATCHED_MIN_TOKENS):
+            n = int(lib.w2a16_moe_layer_workspace_bytes_batched(M, H, I, top_k))
         else:
-            Mq = max(M, BATCHED_MIN_TOKENS) if batched == 1 else M
-            n = max(int(lib.w2a16_moe_layer_workspace_bytes_batched(Mq, H, I, top_k)),
-                    int(lib.w2a16_moe_layer_workspace_bytes(M, H, I, top_k)))
+            n = int(lib.w2a16_moe_layer_workspace_bytes(M, H, I, top_k))
         _WS_BYTES[key] = n
     return n
 
@@ -137,14 +150,14 @@ def _decode_layer_slots_impl(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: to
     nbytes = _workspace_bytes(M, H, I, top_k, batched)
     ws = layer_workspace(x.device, nbytes)
     esz = scales13.element_size()
-    _native.call("w2a16_moe_decode_layer_slots", x.data_ptr(), M, H, I, top_k, topk_ids.data_ptr(),
-                 topk_w.data_ptr(), slots.data_ptr(), slots.numel(),
+    _native.call("w2a16_moe_decode_layer_slots_ex", x.data_ptr(), M, H, I, top_k, topk_ids.data_ptr(),
+                 topk_w.data_ptr(), slots.data_ptr(), slots.numel(), codes13.shape[0],
                  codes13.data_ptr(), codes13.stride(0) * 4, scales13.data_ptr(), scales13.stride(0) * esz,
                  _p(zeros13), 0 if zeros13 is None else zeros13.stride(0),
                  codes2.data_ptr(), codes2.stride(0) * 4, scales2.data_ptr(), scales2.stride(0) * esz,
                  _p(zeros2), 0 if zeros2 is None else zeros2.stride(0),
                  int(scales13.dtype == torch.bfloat16), float(routed_scaling_factor), y.data_ptr(),
-                 ws.data_ptr(), nbytes, _err_word(x.device).data_ptr(), _stream(x.device))
+                 ws.data_ptr(), nbytes, _path(M, batched), _err_word(x.device).data_ptr(), _stream(x.device))
     return y
 
 

@@ -24,6 +24,16 @@ def test_header_declares_entry_points():
         assert n in names
 
 
+def test_path_constants_mirror_header(pkg):
+    txt = open(HEADER).read()
+    defs = dict(re.findall(r"#define (W2A16_[A-Z_]+) (\d+)", txt))
+    nat = pkg._native
+    assert int(defs["W2A16_PATH_AUTO"]) == nat.PATH_AUTO
+    assert int(defs["W2A16_PATH_PER_TOKEN"]) == nat.PATH_PER_TOKEN
+    assert int(defs["W2A16_PATH_BATCHED"]) == nat.PATH_BATCHED
+    assert int(defs["W2A16_BATCHED_AUTO_TOKENS"]) == nat.BATCHED_AUTO_TOKENS
+
+
 def test_library_exports_every_declared_symbol(pkg):
     lib = pkg._native.lib()
     missing = [n for n in header_functions() if not hasattr(lib, n)]
@@ -60,18 +70,23 @@ def test_argument_errors_return_status(pkg):
                                 1, 0, 1, None, None)
     assert st == 0
     # decode layer: workspace too small
-    st = lib.w2a16_moe_decode_layer_slots(fake, 1, 256, 256, 2, fake, fake, fake, 4, fake, 4096, fake, 256,
+    st = lib.w2a16_moe_decode_layer_slots(fake, 1, 256, 256, 2, fake, fake, fake, 4, 4, fake, 4096, fake, 256,
                                           None, 0, fake, 4096, fake, 256, None, 0, 0, 1.0, fake, fake, 16,
                                           None, None)
     assert st == 5
     # decode layer: H not a multiple of 128
-    st = lib.w2a16_moe_decode_layer_slots(fake, 1, 200, 256, 2, fake, fake, fake, 4, fake, 4096, fake, 256,
+    st = lib.w2a16_moe_decode_layer_slots(fake, 1, 200, 256, 2, fake, fake, fake, 4, 4, fake, 4096, fake, 256,
                                           None, 0, fake, 4096, fake, 256, None, 0, 0, 1.0, fake, fake, 1 << 20,
                                           None, None)
     assert st == 1
+    # decode layer: an arena without slots
+    st = lib.w2a16_moe_decode_layer_slots(fake, 1, 256, 256, 2, fake, fake, fake, 4, 0, fake, 4096, fake, 256,
+                                          None, 0, fake, 4096, fake, 256, None, 0, 0, 1.0, fake, fake, 1 << 20,
+                                          None, None)
+    assert st == 4
     # slot form: misaligned arena base
-    st = lib.w2a16_moe_gemv_slots(fake, 128, fake, 4, ctypes.c_void_p(0x1004), 64, fake, 64, None, 0, fake, None,
-                                  fake, 8, 1, 8, 128, 1, 0, 1, None, None)
+    st = lib.w2a16_moe_gemv_slots(fake, 128, fake, 4, 4, ctypes.c_void_p(0x1004), 64, fake, 64, None, 0, fake,
+                                  None, fake, 8, 1, 8, 128, 1, 0, 1, None, None)
     assert st == 2
     # int8: bad group
     st = lib.w2a16_int8_gemv(fake, 256, fake, fake, 100, 128, 1, 256, 64, fake, 64, fake, 1 << 20, None)
@@ -90,35 +105,57 @@ def test_workspace_sizes(pkg):
 
 
 def test_batched_workspace_sizes(pkg):
-    """The batched layer's workspace query: the per-token size below 64 tokens (the per-token path is the
-    faster one there), at least that and room for route tables, h and y rows from 64 tokens, no more growth
-    of the batched part past one 128-token launch, and never less than the per-token path needs."""
+    """The batched layer's workspace query: the per-token size below 16 tokens (the batched path's smallest
+    token count), from 16 tokens at least that and room for route tables, h and y rows, no more growth of
+    the batched part past one 128-token launch, and never less than the per-token path needs."""
     lib = pkg._native.lib()
     H, I, k = 4096, 1536, 8
     per = lambda M: lib.w2a16_moe_layer_workspace_bytes(M, H, I, k)
     bat = lambda M: lib.w2a16_moe_layer_workspace_bytes_batched(M, H, I, k)
-    for M in (1, 15, 16, 32, 63):
+    for M in (1, 8, 15):
         assert bat(M) == per(M), M
-    rows = 64 * k
-    assert bat(64) >= per(64) and bat(64) >= rows * (I * 2 + H * 4)
-    assert bat(64) < bat(128) == bat(256)
+    for M in (16, 64):
+        rows = M * k
+        assert bat(M) >= per(M) and bat(M) >= rows * (I * 2 + H * 4)
+    assert bat(16) < bat(64) < bat(128) == bat(256)
     assert bat(1024) == max(per(1024), bat(128))     # the size serves both paths
 
 
-def test_layer_path_choice_workspace(pkg):
-    """moe_decode_layer's `batched` choice is carried by the workspace size it hands the library: the
-    library's choice (batched from 64 tokens), forced from 16 tokens, or never."""
+def _slots_ex(lib, M, path, ws_bytes, H=4096, I=1536, k=8):
+    fake = ctypes.c_void_p(0x1000)
+    return lib.w2a16_moe_decode_layer_slots_ex(fake, M, H, I, k, fake, fake, fake, 256, 256, fake, 4096, fake, 256,
+                                               None, 0, fake, 4096, fake, 256, None, 0, 0, 1.0, fake, fake,
+                                               ws_bytes, path, None, None)
+
+
+def test_explicit_path_errors(pkg):
+    """w2a16_moe_decode_layer_slots_ex refuses, before any device work: an unknown path (argument), the
+    batched path below 16 tokens (shape) or with a workspace smaller than its size (workspace)."""
+    nat = pkg._native
+    lib = nat.lib()
+    assert _slots_ex(lib, 16, 7, 1 << 30) == 4
+    assert _slots_ex(lib, 8, nat.PATH_BATCHED, 1 << 30) == 1
+    per16 = lib.w2a16_moe_layer_workspace_bytes(16, 4096, 1536, 8)
+    assert _slots_ex(lib, 16, nat.PATH_BATCHED, per16) == 5
+    # the per-token path with too small a workspace is refused the same way (no launch)
+    assert _slots_ex(lib, 16, nat.PATH_PER_TOKEN, 64) == 5
+
+
+def test_layer_path_choice(pkg):
+    """moe_decode_layer's `batched` argument maps to the C ABI's path choice by token count: the library's
+    automatic choice (batched from 64 tokens), the batched path from 16 tokens, or never; the workspace it
+    hands over is sized for the path taken."""
     ml = pkg.moe_layer
-    lib = pkg._native.lib()
+    nat = pkg._native
+    lib = nat.lib()
     H, I, k = 4096, 1536, 8
     per = lambda M: lib.w2a16_moe_layer_workspace_bytes(M, H, I, k)
-    for M in (1, 16, 40, 64, 200):
+    bat = lambda M: lib.w2a16_moe_layer_workspace_bytes_batched(M, H, I, k)
+    for M in (1, 15, 16, 40, 64, 200):
+        assert ml._path(M, 0) == nat.PATH_PER_TOKEN
+        assert ml._path(M, -1) == nat.PATH_AUTO
+        assert ml._path(M, 1) == (nat.PATH_BATCHED if M >= 16 else nat.PATH_PER_TOKEN)
         assert ml._workspace_bytes(M, H, I, k, 0) == per(M)
-        auto = ml._workspace_bytes(M, H, I, k, -1)
-        assert auto == max(per(M), lib.w2a16_moe_layer_workspace_bytes_batched(M, H, I, k))
-        forced = ml._workspace_bytes(M, H, I, k, 1)
-        assert forced >= auto
-    assert ml._workspace_bytes(16, H, I, k, -1) == per(16)        # per-token below 64 tokens
-    assert ml._workspace_bytes(16, H, I, k, 1) > per(16)          # room for the batched path from 16
-    assert ml._workspace_bytes(64, H, I, k, -1) > per(64)         # the batched path from 64
-    assert ml.BATCHED_MIN_TOKENS == 64
+        assert ml._workspace_bytes(M, H, I, k, -1) == (bat(M) if M >= 64 else per(M))
+        assert ml._workspace_bytes(M, H, I, k, 1) == (bat(M) if M >= 16 else per(M))
+    assert ml.BATCHED_MIN_TOKENS == nat.BATCHED_AUTO_TOKENS == 64

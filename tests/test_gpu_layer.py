@@ -56,20 +56,56 @@ def test_config3_m4(pkg, dev):
     assert O.max_rel_err(y.float().cpu(), oracle_layer(arena, x, ids, w)) < TOL
 
 
-@pytest.mark.parametrize("M", [16, 64])
-def test_config3_batched_tokens(pkg, dev, M):
-    """Config 3, M=16 and M=64 tokens at full size (uniform-random logits). The layer runs them in token
-    chunks through the same kernel; each token's output depends only on its own routing, so a spread of
-    tokens is checked against the oracle (dequantising 8 experts per checked token)."""
+@pytest.mark.parametrize("M,batched", [(16, None), (16, True), (64, None)])
+def test_config3_batched_tokens(pkg, dev, M, batched):
+    """Config 3, M=16 and M=64 tokens at full size (uniform-random logits), every token against the oracle.
+    M=16 runs both ways: the library's choice (the per-token kernel below 64 tokens) and the batched
+    tensor-core path forced (tcgen05 MMAs over each expert's grouped rows, as the configuration names it);
+    M=64 takes the batched path by the library's own choice."""
     E, H, I, k = 256, 4096, 1536, 8
     arena = pkg.synth.make_arena(E, H, I, seed=5, device=dev, gen_device=dev)
     x = pkg.synth.make_activation(M, H, seed=5, device=dev, gen_device=dev)
     ids, w = pkg.synth.route_softmax(M, E, k, seed=5, device=dev, gen_device=dev, uniform_logits=True)
-    y = pkg.moe_decode_layer(x, ids, w, arena)
+    y = pkg.moe_decode_layer(x, ids, w, arena, batched=batched)
     torch.cuda.synchronize()
-    for m in sorted({0, 1, M // 2, M - 1}):
-        ref = oracle_layer(arena, x[m:m + 1], ids[m:m + 1], w[m:m + 1])
-        assert O.max_rel_err(y[m:m + 1].float().cpu(), ref) < TOL, m
+    ref = O.moe_layer_by_expert(arena, x, ids, w)
+    for m in range(M):
+        assert O.max_rel_err(y[m:m + 1].float().cpu(), ref[m:m + 1]) < TOL, m
+
+
+def test_slot_past_arena_is_masked(pkg, dev):
+    """A slot table entry of S or more (the arena holds S slots) reads nothing outside the arena: the row
+    contributes zero exactly as slot -1 does, and bit 0 of the device error word is set. Both the fused
+    layer and the slot GEMV."""
+    E, S, H, I, M, k = 16, 12, 1024, 512, 2, 4
+    slots = torch.arange(E, dtype=torch.int32) % S
+    slots[3] = -1
+    arena = pkg.synth.make_arena(S, H, I, seed=31, zeros=True, device=dev, gen_device="cpu", slots=slots)
+    x = pkg.synth.make_activation(M, H, seed=31, device=dev, gen_device="cpu")
+    ids = torch.tensor([[5, 7, 3, 1], [7, 0, 2, 9]], dtype=torch.int32, device=dev)
+    w = torch.full((M, k), 0.25, dtype=torch.float32, device=dev)
+    pkg.last_device_error(dev)
+    masked = arena.slots.clone()
+    masked[7] = -1
+    y_ref = pkg.moe_decode_layer(x, ids, w, pkg.ExpertArena(arena.codes13, arena.scales13, arena.codes2,
+                                                          arena.scales2, arena.zeros13, arena.zeros2, masked))
+    torch.cuda.synchronize()
+    assert pkg.last_device_error(dev) == 0
+    bad = arena.slots.clone()
+    bad[7] = S + 1000000
+    bad_arena = pkg.ExpertArena(arena.codes13, arena.scales13, arena.codes2, arena.scales2, arena.zeros13,
+                                arena.zeros2, bad)
+    y_bad = pkg.moe_decode_layer(x, ids, w, bad_arena)
+    torch.cuda.synchronize()
+    assert torch.equal(y_bad, y_ref)
+    assert pkg.last_device_error(dev) & 1
+    g_ref = pkg.moe_gemv_int2_slots(x, masked.to(dev), arena.codes13, arena.scales13, ids, w, top_k=k,
+                                    zeros=arena.zeros13)
+    g_bad = pkg.moe_gemv_int2_slots(x, bad.to(dev), arena.codes13, arena.scales13, ids, w, top_k=k,
+                                    zeros=arena.zeros13)
+    torch.cuda.synchronize()
+    assert torch.equal(g_bad, g_ref)
+    assert pkg.last_device_error(dev) & 1
 
 
 def test_config2_resident_slots_full_size(pkg, dev):

@@ -119,3 +119,29 @@ def test_slot_masking_semantics():
     o = O.gemv_tab(a, w, s, ids, None, 3, False, slots=slots)
     assert torch.equal(o[2], torch.zeros(N))                     # expert 1 not resident
     assert torch.allclose(o[0], O.gemv_tab(a, w, s, torch.tensor([2], dtype=torch.int32), None, 1, False)[0])
+
+
+def test_expert_order_oracle_matches_token_order():
+    """moe_layer_by_expert (each expert dequantised once, for whole token batches) computes the same
+    layer as the token-order loop moe_layer_routed_only, masked and out-of-arena slots included."""
+    from types import SimpleNamespace
+    gen = torch.Generator().manual_seed(9)
+    E, S, H, I, M, k = 8, 6, 256, 128, 5, 3
+    rw = lambda *sh: torch.randint(-(2 ** 31), 2 ** 31, sh, dtype=torch.int32, generator=gen)
+    ar = SimpleNamespace(codes13=rw(S, H // 16, 2 * I), scales13=(torch.rand(S, H // 128, 2 * I, generator=gen) * 0.02).half(),
+                         zeros13=torch.randint(0, 256, (S, H // 128, 2 * I // 4), dtype=torch.uint8, generator=gen),
+                         codes2=rw(S, I // 16, H), scales2=(torch.rand(S, I // 128, H, generator=gen) * 0.02).half(),
+                         zeros2=torch.randint(0, 256, (S, I // 128, H // 4), dtype=torch.uint8, generator=gen),
+                         slots=torch.tensor([0, 1, -1, 2, 3, 4, 5, 99], dtype=torch.int32))
+    x = torch.randn(M, H, generator=gen).to(torch.bfloat16)
+    ids = torch.stack([torch.randperm(E, generator=gen)[:k] for _ in range(M)]).to(torch.int32)
+    w = torch.softmax(torch.randn(M, k, generator=gen), -1)
+    experts = {}
+    for e in range(E):
+        sl = int(ar.slots[e])
+        if 0 <= sl < S:
+            experts[e] = (ar.codes13[sl], ar.scales13[sl], ar.zeros13[sl], ar.codes2[sl], ar.scales2[sl],
+                          ar.zeros2[sl])
+    a = O.moe_layer_routed_only(x, experts, ids, w, 1.5)
+    b = O.moe_layer_by_expert(ar, x, ids, w, 1.5)
+    assert torch.allclose(a, b, rtol=1e-5, atol=1e-6)

@@ -24,7 +24,7 @@ def _call_noalloc(pkg, x, ids, w, arena, y, M=None, H=None, I=None):
     I = arena.I if I is None else I
     return lib.w2a16_moe_decode_layer_slots_noalloc(
         x.data_ptr(), M, H, I, ids.shape[1], ids.data_ptr(), w.data_ptr(), arena.slots.data_ptr(),
-        arena.E, arena.codes13.data_ptr(), arena.codes13.stride(0) * 4, arena.scales13.data_ptr(),
+        arena.E, arena.S, arena.codes13.data_ptr(), arena.codes13.stride(0) * 4, arena.scales13.data_ptr(),
         arena.scales13.stride(0) * esz, arena.zeros13.data_ptr(), arena.zeros13.stride(0),
         arena.codes2.data_ptr(), arena.codes2.stride(0) * 4, arena.scales2.data_ptr(),
         arena.scales2.stride(0) * esz, arena.zeros2.data_ptr(), arena.zeros2.stride(0),
@@ -45,6 +45,25 @@ def test_noalloc_entry_matches_workspace_entry(pkg, dev):
         torch.cuda.synchronize()
         assert O.max_rel_err(y.float().cpu(), ref.float().cpu()) <= TOL
         assert torch.isfinite(y.float()).all()
+
+
+@pytest.mark.parametrize("M", [16, 64])
+def test_noalloc_entry_full_size_token_batches(pkg, dev, M):
+    """Config-3 shapes (H=4096, I=1536, E=256, top-8) at 16 and 64 tokens, two calls in a row: the no-alloc
+    entry takes the per-token path below 64 tokens like the regular entry (its choice follows the token
+    count, not the size of its array), and at 64 tokens, where the batched path's buffers do not fit the
+    array, the per-token path too; both agree with the regular entry within the layer tolerance."""
+    E, H, I, k = 256, 4096, 1536, 8
+    arena = pkg.synth.make_arena(E, H, I, seed=21, zeros=True, device=dev, gen_device=dev)
+    x = pkg.synth.make_activation(M, H, seed=21, device=dev, gen_device=dev)
+    ids, w = pkg.synth.route_softmax(M, E, k, seed=21, device=dev, gen_device=dev, uniform_logits=True)
+    ref = pkg.moe_decode_layer(x, ids, w, arena)
+    for _ in range(2):
+        y = torch.full_like(ref, float("nan"))
+        assert _call_noalloc(pkg, x, ids, w, arena, y) == 0
+        torch.cuda.synchronize()
+        assert torch.isfinite(y.float()).all()
+        assert O.max_rel_err(y.float().cpu(), ref.float().cpu()) <= TOL
 
 
 def test_noalloc_entry_rejects_oversized_layers(pkg, dev):
