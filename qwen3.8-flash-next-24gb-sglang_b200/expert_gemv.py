@@ -152,11 +152,34 @@ def _to_word_fake(src):
     return src.new_empty((E, KB // 4, N), dtype=torch.int32)
 
 
+def _to_word_host(src: torch.Tensor) -> torch.Tensor:
+    """The relayout of a host tensor, run by the same CUDA kernel: the GPU reads the pinned source and writes a
+    pinned result through unified addressing (no CPU arithmetic). A pageable source is first copied into
+    pinned memory. Synchronises the stream before returning, as the host result is used right away."""
+    if not torch.cuda.is_available():
+        raise RuntimeError("to_word_ncontig of a host tensor runs on the GPU through unified addressing; "
+                           "no CUDA device is available (there is no CPU path)")
+    E, N, KB = src.shape
+    pinned = src if src.is_pinned() else src.pin_memory()
+    out = torch.empty((E, KB // 4, N), dtype=torch.int32).pin_memory()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    stream = torch.cuda.current_stream(dev)
+    _native.call("w2a16_to_word_ncontig", pinned.data_ptr(), out.data_ptr(), E, N, KB * 4, stream.cuda_stream)
+    stream.synchronize()
+    return out
+
+
 def to_word_ncontig(qweight_u8_nk: torch.Tensor) -> torch.Tensor:
     """Loader layout uint8 [E, N, K/4] -> int32 [E, K/16, N], bit-exact (gemv/moe_gemv_int2_tab.py:100-109):
-    byte kb of row n becomes byte kb % 4 of word kb // 4 at column n. Runs as a CUDA kernel."""
-    _check_cuda("qweight_u8_nk", qweight_u8_nk, torch.uint8)
+    byte kb of row n becomes byte kb % 4 of word kb // 4 at column n. Runs as a CUDA kernel. A CUDA tensor
+    gives a CUDA tensor (asynchronous, current stream); a host tensor -- the reference relayouts offloaded
+    experts that live in pinned host memory (patches/ncontig_gemv.py:195-201) -- gives a pinned host tensor,
+    the kernel reading and writing host memory over the bus (the call waits for it)."""
+    if qweight_u8_nk.dtype != torch.uint8:
+        raise ValueError(f"qweight_u8_nk must be uint8, got {qweight_u8_nk.dtype}")
     assert qweight_u8_nk.dim() == 3 and qweight_u8_nk.shape[2] % 4 == 0, qweight_u8_nk.shape
+    if not qweight_u8_nk.is_cuda:
+        return _to_word_host(qweight_u8_nk.contiguous())
     return _to_word(qweight_u8_nk.contiguous())
 
 

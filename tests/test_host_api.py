@@ -18,7 +18,11 @@ def test_cpu_tensors_are_rejected(pkg):
                               torch.zeros(1, dtype=torch.int32), None, 8, 128, 8, 8, top_k=1,
                               mul_routed_weight=False)
     with pytest.raises(ValueError):
-        pkg.to_word_ncontig(torch.zeros(1, 8, 4, dtype=torch.uint8))
+        pkg.to_word_ncontig(torch.zeros(1, 8, 4, dtype=torch.int32))
+    if not torch.cuda.is_available():
+        # a host tensor is relayouted by the CUDA kernel over unified addressing; without a device it raises
+        with pytest.raises(RuntimeError):
+            pkg.to_word_ncontig(torch.zeros(1, 8, 4, dtype=torch.uint8))
     with pytest.raises(ValueError):
         pkg.int8_gemv(torch.zeros(1, 128, dtype=torch.bfloat16), torch.zeros(32, 8, dtype=torch.int32),
                       torch.zeros(1, 8, dtype=torch.float16))
@@ -40,3 +44,32 @@ def test_synth_distributions(pkg):
     import oracle as O
     q = O.int8_unpack(qw) - 128
     assert int(q.min()) >= -127 and int(q.max()) <= 127 and sc.shape == (1, 64)
+
+
+def test_gemv_gate_mirrors_the_reference(pkg):
+    """MoeWNA16Method.apply's gate (patches/ncontig_gemv.py:249-253): word layout, 2-bit, at most 16 tokens,
+    SGLANG_MOE_GEMV unset or "1"."""
+    from types import SimpleNamespace
+    word = SimpleNamespace(_b_n_contig=True)
+    byte = SimpleNamespace()
+    g = pkg.use_gemv
+    assert g(word, 1, env={}) and g(word, 16, env={}) and g(word, 16, env={"SGLANG_MOE_GEMV": "1"})
+    assert not g(word, 17, env={})
+    assert not g(word, 1, env={"SGLANG_MOE_GEMV": "0"})
+    assert not g(word, 1, weight_bits=4, env={})
+    assert not g(byte, 1, env={})
+    assert pkg.moe_method.GEMV_MAX_TOKENS == 16
+
+
+def test_relayout_switch_leaves_layer_untouched(pkg, monkeypatch):
+    """SGLANG_MOE_NCONTIG=0 (and non-2-bit layers) skip the relayout, as the reference does
+    (patches/ncontig_gemv.py:177-180); nothing runs, so no GPU is needed."""
+    from types import SimpleNamespace
+    t = torch.zeros(2, 8, 4, dtype=torch.uint8)
+    layer = SimpleNamespace(w13_qweight=t, w2_qweight=t, w13_scales=t, w2_scales=t)
+    monkeypatch.setenv("SGLANG_MOE_NCONTIG", "0")
+    pkg.MoeWNA16Method().process_weights_after_loading(layer)
+    assert layer.w13_qweight is t and not getattr(layer, "_b_n_contig", False)
+    monkeypatch.setenv("SGLANG_MOE_NCONTIG", "1")
+    pkg.MoeWNA16Method(weight_bits=4).process_weights_after_loading(layer)
+    assert layer.w13_qweight is t and not getattr(layer, "_b_n_contig", False)
