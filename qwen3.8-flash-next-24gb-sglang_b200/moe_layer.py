@@ -140,11 +140,12 @@ def _workspace_bytes(M: int, H: int, I: int, top_k: int, batched: int = -1) -> i
 def _decode_layer_slots_impl(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor, slots: torch.Tensor,
                              codes13: torch.Tensor, scales13: torch.Tensor, zeros13: Optional[torch.Tensor],
                              codes2: torch.Tensor, scales2: torch.Tensor, zeros2: Optional[torch.Tensor],
-                             routed_scaling_factor: float, batched: int = -1) -> torch.Tensor:
+                             routed_scaling_factor: float, batched: int = -1,
+                             out: Optional[torch.Tensor] = None) -> torch.Tensor:
     M, H = x.shape
     top_k = topk_ids.shape[1]
     I = codes13.shape[2] // 2
-    y = torch.empty((M, H), dtype=torch.bfloat16, device=x.device)
+    y = torch.empty((M, H), dtype=torch.bfloat16, device=x.device) if out is None else out
     if M == 0:
         return y
     nbytes = _workspace_bytes(M, H, I, top_k, batched)
@@ -187,19 +188,29 @@ def _routing(x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor
 
 
 def moe_decode_layer(x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor, arena: ExpertArena,
-                     routed_scaling_factor: float = 1.0, batched: Optional[bool] = None) -> torch.Tensor:
+                     routed_scaling_factor: float = 1.0, batched: Optional[bool] = None,
+                     out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """y[m] = routed_scaling_factor * sum_j w[m, j] * down_e(silu(gate_e(x_m)) * up_e(x_m)),
     e = topk_ids[m, j] looked up through ``arena.slots``. x bf16 [M, H] -> bf16 [M, H].
 
     ``batched``: None lets the library choose (the batched path -- routed rows grouped by expert, each
     expert streamed once, products on the tensor cores -- from 64 tokens, where it is faster than the
-    per-token path); True takes it from 16 tokens; False always takes the per-token path."""
+    per-token path); True takes it from 16 tokens; False always takes the per-token path. ``out`` (bf16
+    [M, H], contiguous, on x's device) receives the result instead of a new tensor -- a decode loop that
+    chains layers through fixed buffers then runs no copy kernel between them."""
     x, ids, w = _routing(x, topk_ids, topk_weights)
-    # eager calls skip the custom-op dispatcher (tens of microseconds of host time); traced/compiled code
-    # goes through the registered op
-    op = _decode_layer_slots if torch.compiler.is_compiling() else _decode_layer_slots_impl
-    return op(x, ids, w, arena.slots, arena.codes13, arena.scales13, arena.zeros13, arena.codes2, arena.scales2,
-              arena.zeros2, float(routed_scaling_factor), -1 if batched is None else int(bool(batched)))
+    b = -1 if batched is None else int(bool(batched))
+    args = (x, ids, w, arena.slots, arena.codes13, arena.scales13, arena.zeros13, arena.codes2, arena.scales2,
+            arena.zeros2, float(routed_scaling_factor), b)
+    if torch.compiler.is_compiling():
+        # traced/compiled code goes through the registered op (functional: the result is copied into out)
+        y = _decode_layer_slots(*args)
+        return y if out is None else out.copy_(y)
+    if out is not None and (out.shape != x.shape or out.dtype != torch.bfloat16 or not out.is_contiguous()
+                            or out.device != x.device):
+        raise ValueError("out must be a contiguous bf16 tensor shaped like x on x's device")
+    # eager calls skip the custom-op dispatcher (tens of microseconds of host time)
+    return _decode_layer_slots_impl(*args, out=out)
 
 
 @torch.library.custom_op("w2a16_moe::decode_layer_tab", mutates_args=())
