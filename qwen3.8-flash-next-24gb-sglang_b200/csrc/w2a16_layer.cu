@@ -50,6 +50,21 @@ constexpr int kScaleOff = 4096;
 constexpr int kZeroOff = 4352;
 constexpr int kMinStages = 16, kMaxStages = 48;             // multiples of kIssuers
 
+// K-split mode (decode sizes: at most kKsMaxRows routed rows). A CTA multiplies the h-blocks it finishes by
+// the matching K-slice of its rows' down projections right away, so the down weights and their products
+// stream with the gate_up items; per-CTA partial outputs are summed after one grid barrier. Down items
+// are (run of <= 4 owned h-blocks of one row, 128 output columns): codes (2 word rows per block) x 512 B at
+// 0, the scale rows of the <= 2 quantization groups the run touches at 4096, their zero-point rows at
+// 4608.
+constexpr int kKsStageBytes = 4736;
+constexpr int kKsScaleOff = 4096, kKsZeroOff = 4608;
+constexpr int kKsCols = 128;                                 // output columns of a down item
+constexpr int kKsMaxOwned = 12;                              // h-blocks one CTA finishes
+constexpr int kKsMaxSub = 8;                                 // runs of <= 4 owned blocks
+constexpr int kKsMaxRows = 32;                               // routed rows of a K-split launch
+constexpr int kKsMaxGrid = 160;                              // CTAs whose partials the workspace holds
+constexpr int kKsMaxSeg = 2;                                 // tokens one CTA's owned blocks belong to
+
 constexpr unsigned kSpinLimit = 1u << 22;                    // polls before a wait gives up
 constexpr unsigned kWaitLimit = 1u << 17;                    // suspending mbarrier tries before a wait gives up
 
@@ -116,7 +131,7 @@ __host__ __device__ __forceinline__ size_t htab_bytes(int I) {
 }
 
 struct SmemPlan {
-  size_t tabs, mail1, mail2, rows, misc, live, slots, preg, total;
+  size_t tabs, mail1, mail2, rows, misc, live, slots, preg, ks, total;
 };
 constexpr int kMaxStagedSlots = 2048;                        // slot tables up to 8 KB are staged
 constexpr int kMaxPrivSlots = 512;                           // producers keep private copies up to 2 KB
@@ -139,13 +154,14 @@ struct RowPtr {
   float wt;      // routing weight
 };
 
-SmemPlan smem_plan(const Geo& g) {
+// ks: K-split mode (no down-unit h tables or partials; its own block s.ks, sized where KsShared is defined).
+SmemPlan smem_plan(const Geo& g, bool ks = false) {
   SmemPlan s{};
   const size_t t1 = (size_t)g.M * token_table_bytes(g.H);
-  const size_t t2 = (size_t)g.top_k * htab_bytes(g.I);         // one down unit's h tables at a time
+  const size_t t2 = ks ? 0 : (size_t)g.top_k * htab_bytes(g.I);   // one down unit's h tables at a time
   s.tabs = t1 > t2 ? t1 : t2;
   s.mail1 = (size_t)g.max_range * 64 * 4;
-  s.mail2 = (size_t)g.s2 * 32 * 4;
+  s.mail2 = ks ? 0 : (size_t)g.s2 * 32 * 4;
   s.rows = ((size_t)g.R * sizeof(RowPtr) + 15) & ~size_t(15);
   s.misc = 64;                                                  // mbarrier, head counter, generation
   // LiveRows arrays and the live-row bit words
@@ -160,6 +176,12 @@ struct FusedParams {
   // copy-engine mode: tensor maps over the slot arena -- gate_up codes / scales / zero points (4-D:
   // column within half, half, row, slot) and down codes / scales / zero points (3-D: column, row, slot)
   CUtensorMap tm[6];
+  // K-split mode: down codes with boxes of 128 columns x 2, 4, 6, 8 word rows, down scales and zero points
+  // with boxes of 1 and 2 group rows
+  CUtensorMap tmk[8];
+  float* part;           // K-split: [grid][ks_segs][H] fp32 partial outputs
+  int ks_segs;           // K-split: segments per CTA the partial buffer holds (min(M, kKsMaxSeg))
+  size_t off_ks;
   int nstage;
   size_t off_stages, off_bars;
   const __nv_bfloat16* x;
@@ -646,6 +668,256 @@ __device__ void produce(const FusedParams& p, const LiveRows& lv, SlotOf slot_of
     }
 }
 
+// ----------------------------------------------------------------------------- K-split mode
+// The CTA's plan: the h-blocks it finishes ("owned": those whose first gate_up item lies in its range), cut
+// into runs of <= 4 consecutive blocks of one routed row, and the tokens ("segments") those rows belong
+// to. Down items are numbered segment by segment; within a segment by output block (128 columns), then
+// run, so the items one warp accumulates for one (segment, output block) unit are consecutive.
+struct KsPlan {
+  int ready;                         // set once the plan is in place (the producers wait for it)
+  int bs, nown;                      // first owned block (over the live rows), owned blocks
+  int nseg, nsub, ndown, nunits;
+  int seg_tok[kKsMaxSeg], seg_sub0[kKsMaxSeg], seg_nsub[kKsMaxSeg], seg_base[kKsMaxSeg];
+  int sub_row[kKsMaxSub], sub_lb0[kKsMaxSub], sub_nb[kKsMaxSub], sub_w0[kKsMaxSub];
+  int blk_need[kKsMaxOwned];         // gate_up items of each owned block inside this CTA's range
+};
+struct KsShared {
+  KsPlan plan;
+  int blk_cnt[kKsMaxOwned];          // reduced gate_up items per owned block
+  int ready[kKsMaxOwned];            // owned block's h table written
+  int next;                          // next work index of the CTA (dynamic assignment to warps)
+  alignas(16) uint32_t hpairs[kKsMaxOwned][2 * kXRegs];   // h of each owned block: fixed-point pairs, 2 word rows
+  int hm64x[kKsMaxOwned];
+  float hscl[kKsMaxOwned];
+  float red[kWarps][32];             // final reduction: one partial sum per warp and column
+};
+
+// Lane 0 of one warp: the plan of this CTA (every quantity derived from the live rows and the ranges, the
+// same in every warp that builds it).
+__device__ void ks_build_plan(const Geo& g, const LiveRows& lv, int cta, int nob, KsPlan& pl) {
+  const WarpList L = warp_list(g, lv, cta, 0);
+  const int bs = L.range > 0 ? (L.a + g.kp1 - 1) / g.kp1 : 0;
+  const int be = L.range > 0 ? (L.b + g.kp1 - 1) / g.kp1 : 0;
+  pl.bs = bs;
+  pl.nown = min(be - bs, kKsMaxOwned);               // (the host guarantees be - bs <= kKsMaxOwned)
+  pl.nseg = 0;
+  pl.nsub = 0;
+  int last_rc = -1;
+  for (int j = 0; j < pl.nown; ++j) {
+    const int gb = bs + j;
+    const int rc = fdiv(gb, g.d_nb1), hb = gb - rc * g.nb1;
+    const int r = lv.rowmap[rc], m = fdiv(r, g.d_topk);
+    const int hi = min(L.b, (gb + 1) * g.kp1);
+    pl.blk_need[j] = hi - gb * g.kp1;
+    const bool fresh = pl.nsub == 0 || rc != last_rc || pl.sub_nb[pl.nsub - 1] == 4;
+    if (fresh && pl.nsub < kKsMaxSub) {
+      if (pl.nseg == 0 || pl.seg_tok[pl.nseg - 1] != m) {
+        if (pl.nseg == kKsMaxSeg) break;               // (the host guarantees at most two tokens)
+        pl.seg_tok[pl.nseg] = m;
+        pl.seg_sub0[pl.nseg] = pl.nsub;
+        pl.seg_nsub[pl.nseg] = 0;
+        ++pl.nseg;
+      }
+      pl.sub_row[pl.nsub] = r;
+      pl.sub_lb0[pl.nsub] = j;
+      pl.sub_nb[pl.nsub] = 1;
+      pl.sub_w0[pl.nsub] = 2 * hb;
+      ++pl.seg_nsub[pl.nseg - 1];
+      ++pl.nsub;
+    } else if (!fresh) {
+      ++pl.sub_nb[pl.nsub - 1];
+    }
+    last_rc = rc;
+  }
+  pl.ndown = 0;
+  for (int s2 = 0; s2 < pl.nseg; ++s2) {
+    pl.seg_base[s2] = pl.ndown;
+    pl.ndown += nob * pl.seg_nsub[s2];
+  }
+  pl.nunits = pl.nseg * nob;
+}
+
+// Down item d of the plan -> (segment, output block, run).
+__device__ __forceinline__ void ks_item(const KsPlan& pl, int nob, int d, int& seg, int& cb, int& sub) {
+  seg = (pl.nseg > 1 && d >= pl.seg_base[1]) ? 1 : 0;
+  const int within = d - pl.seg_base[seg], ns = pl.seg_nsub[seg];
+  cb = within / ns;
+  sub = pl.seg_sub0[seg] + (within - cb * ns);
+}
+
+// h of an owned block (lane l holds element l) -> the CTA's fixed-point table of that block: one exponent
+// for the 32 values, pairs packed as in the activation tables (word row l / 16).
+__device__ __forceinline__ void htab_local(KsShared& ks, int j, float h, int lane) {
+  const float mx = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(h))));
+  const int e = (mx > 0.f ? frexp_exponent(mx) : 0) - 15;
+  const int q = max(-32767, min(32767, __float2int_rn(h * pow2f(-e))));
+  const int s = __reduce_add_sync(0xffffffffu, q);
+  const int hi = __shfl_xor_sync(0xffffffffu, q, 4);
+  if ((lane & 4) == 0) {
+    const int c = lane & 15, kw = lane >> 4;
+    ks.hpairs[j][kw * kXRegs + (c & 3) * 2 + (c >> 3)] = (uint32_t)(q & 0xFFFF) | ((uint32_t)hi << 16);
+  }
+  if (lane == 0) {
+    ks.hm64x[j] = -64 * s;
+    ks.hscl[j] = pow2f(e - 6);
+  }
+}
+
+// One down item from its ring stage: lane l, output columns cb * 128 + 4l .. +3, the run's word rows (two per
+// owned block) against the blocks' h tables; returns the item's 4 sums (before the routing weight).
+__device__ __forceinline__ void ks_dot(const unsigned char* st, const KsShared& ks, int lb0, int nb, int w0, bool sbf,
+                                       bool has_z, int lane, float (&v)[4]) {
+  float f[4] = {0.f, 0.f, 0.f, 0.f};
+  const int g0 = w0 >> 3;
+  for (int j = 0; j < nb; ++j) {
+    const int wr = w0 + 2 * j, gi = (wr >> 3) - g0;
+    int acc[4][4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) acc[c][k] = 0;
+#pragma unroll
+    for (int kk = 0; kk < 2; ++kk) {
+      const uint4 w = *reinterpret_cast<const uint4*>(st + (size_t)(2 * j + kk) * (kKsCols * 4) + lane * 16);
+      const uint4* xp = reinterpret_cast<const uint4*>(&ks.hpairs[lb0 + j][kk * kXRegs]);
+      const uint4 xa = xp[0], xb = xp[1];
+      const uint32_t xr[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+      word_dot(w.x, xr, acc[0]);
+      word_dot(w.y, xr, acc[1]);
+      word_dot(w.z, xr, acc[2]);
+      word_dot(w.w, xr, acc[3]);
+    }
+    const int m64x = ks.hm64x[lb0 + j];
+    const float scl = ks.hscl[lb0 + j];
+    const uint32_t zb = has_z ? (uint32_t)st[kKsZeroOff + gi * (kKsCols / 4) + lane] : 0u;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int zp = has_z ? (int)((zb >> (2 * c)) & 3u) : 2;
+      f[c] += (float)(combine_classes(acc[c]) + zp * m64x) * scl;
+    }
+    // the run ends here or the next block starts a new quantization group: apply this group's scales
+    if (j == nb - 1 || ((wr + 2) >> 3) != (wr >> 3)) {
+      float sc[4];
+      scales4(*reinterpret_cast<const uint2*>(st + kKsScaleOff + gi * (kKsCols * 2) + lane * 8), sbf, sc);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        v[c] += f[c] * sc[c];
+        f[c] = 0.f;
+      }
+    }
+  }
+}
+
+// Item i of a range of n1 items cut into grid1 ranges (the first n1 % grid1 one item longer) -> its CTA.
+__device__ __forceinline__ int range_owner(int n1, int grid1, int i) {
+  const int q = n1 / grid1, rem = n1 - q * grid1;
+  return i < rem * (q + 1) ? i / (q + 1) : rem + (i - rem * (q + 1)) / q;
+}
+
+// K-split mode's producers: the same issuing scheme as produce() over the CTA's gate_up range followed by the
+// plan's down items. The plan comes from warp 0; a producer waits for it (bounded) only when a batch of
+// descriptors first reaches past the gate_up range.
+template <class SlotOf>
+__device__ void produce_ks(const FusedParams& p, const LiveRows& lv, SlotOf slot_of, int cta, unsigned char* stages,
+                           uint32_t bars, int* tags, int pr, int lane, const KsShared* ks) {
+  const Geo& g = p.geo;
+  const WarpList L0 = warp_list(g, lv, cta, 0);
+  const int nob = g.H / kKsCols;
+  int n = L0.range;                                           // grows by the down items once the plan is read
+  bool have_plan = false;
+  int nw = n > pr ? (n - pr + kProducers - 1) / kProducers : 0;
+  const int ns = p.nstage;
+  const bool hz = p.map13.has_zeros != 0;
+  const bool aligned = (smem_u32(stages) & 127u) == 0;
+  if (!aligned && lane == 0) flag_error(p.err, 4u);
+  const bool issuer = lane < kIssuers / kProducers;
+  const uint64_t pol = evict_first_policy();
+  int4 batch = make_int4(0, 0, 0, 0);
+  // Down-item descriptor from the plan (kind 3 | blocks << 4 | groups << 8, slot, output block, first word row).
+  auto down_desc = [&](int d) {
+    int seg, cb, sub;
+    ks_item(ks->plan, nob, d, seg, cb, sub);
+    const int nb = ks->plan.sub_nb[sub], w0 = ks->plan.sub_w0[sub];
+    const int ng = ((w0 + 2 * nb - 1) >> 3) - (w0 >> 3) + 1;
+    const int sl = slot_of(ks->plan.sub_row[sub], 2);
+    return make_int4(sl >= 0 ? (3 | (nb << 4) | (ng << 8)) : 0, sl, cb, w0);
+  };
+  // Bounded wait for warp 0's plan (error bit 1 when it never comes); true when it is there.
+  auto wait_plan = [&]() {
+    unsigned it = 0;
+    while (ld_volatile_shared(&ks->plan.ready) == 0) {
+      if (++it > kSpinLimit) {
+        flag_error(p.err, 2u);
+        return false;
+      }
+    }
+    __threadfence_block();
+    return true;
+  };
+  constexpr int kPending = 15;                                // a down item decoded before the plan existed
+  for (int j0 = 0;; j0 += kIssuers / kProducers) {
+    if (!have_plan && j0 >= nw) {                             // the gate_up range is issued: now the down items
+      bool ok = true;
+      if (lane == 0) ok = wait_plan();
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      __syncwarp();
+      __threadfence_block();
+      n = L0.range + (ok ? ks->plan.ndown : 0);
+      nw = n > pr ? (n - pr + kProducers - 1) / kProducers : 0;
+      have_plan = true;
+    }
+    if (j0 >= nw) break;
+    if ((j0 & 31) == 0) {
+      const int ii = pr + kProducers * (j0 + lane);
+      const bool ready = have_plan || ld_volatile_shared(&ks->plan.ready) != 0;
+      if (ready) __threadfence_block();
+      batch = make_int4(0, 0, 0, 0);
+      if (ii < L0.range) batch = item_desc(g, lv, L0, cta, slot_of, ii);
+      else batch = ready ? down_desc(ii - L0.range) : make_int4(kPending, 0, 0, 0);
+    }
+    const int src = (j0 & 31) + (lane & 1);
+    int4 it;
+    it.x = __shfl_sync(0xffffffffu, batch.x, src);
+    it.y = __shfl_sync(0xffffffffu, batch.y, src);
+    it.z = __shfl_sync(0xffffffffu, batch.z, src);
+    it.w = __shfl_sync(0xffffffffu, batch.w, src);
+    const int j = j0 + lane;
+    if (issuer && j < nw) {
+      const int i = pr + kProducers * j;
+      if ((it.x & 15) == kPending) it = wait_plan() ? down_desc(i - L0.range) : make_int4(0, 0, 0, 0);
+      const int st = i % ns, round = i / ns;
+      const uint32_t full = bars + st * 8, empty = bars + (ns + st) * 8;
+      if (round > 0) mbar_wait(empty, (unsigned)(round - 1) & 1u, p.err);
+      st_volatile_shared(tags + st, i);
+      const int kind = it.x & 15;
+      if (!aligned || kind == 0) {
+        mbar_arrive(full);
+      } else {
+        const uint32_t dst = smem_u32(stages + (size_t)st * kKsStageBytes);
+        if (kind == 1) {
+          mbar_arrive_tx(full, (unsigned)(kScaleOff + 256 + (hz ? 64 : 0)));
+          const int zx = (8 * it.z) & ~15;
+          tma_load_4d(dst, &p.tm[0], it.z * 32, 0, 16 * it.w, it.y, full, pol);
+          tma_load_4d(dst + kScaleOff, &p.tm[1], it.z * 32, 0, 2 * it.w, it.y, full, pol);
+          if (hz) tma_load_4d(dst + kZeroOff, &p.tm[2], zx, 0, 2 * it.w, it.y, full, pol);
+        } else {                                              // kind 3: K-split down item
+          const int nb = (it.x >> 4) & 15, ng = (it.x >> 8) & 3, w0 = it.w, cb = it.z;
+          mbar_arrive_tx(full, (unsigned)(2 * nb * kKsCols * 4 + ng * kKsCols * 2 + (hz ? ng * kKsCols / 4 : 0)));
+          tma_load_3d(dst, &p.tmk[nb - 1], cb * kKsCols, w0, it.y, full, pol);
+          tma_load_3d(dst + kKsScaleOff, &p.tmk[4 + ng - 1], cb * kKsCols, w0 >> 3, it.y, full, pol);
+          if (hz) tma_load_3d(dst + kKsZeroOff, &p.tmk[6 + ng - 1], cb * (kKsCols / 4), w0 >> 3, it.y, full, pol);
+        }
+      }
+    }
+    __syncwarp();
+  }
+  if (issuer)
+    for (int s0 = pr + kProducers * lane; s0 < ns && s0 < n; s0 += kIssuers) {
+      const int last = s0 + ((n - 1 - s0) / ns) * ns;
+      mbar_wait(bars + s0 * 8, (unsigned)(last / ns) & 1u, p.err);
+    }
+}
+
 // 4 columns x 1 group of this lane from a ring stage. Gate_up stages hold 256-byte word rows (32 gate |
 // 32 up columns), scales [group][half][32] and zero windows [group][half][16 B]; down stages 128-byte
 // rows, scales [group][32] and windows [group][16 B].
@@ -875,10 +1147,215 @@ __device__ __forceinline__ void unit_tables(const FusedParams& p, const LiveRows
   csync();
 }
 
+// ----------------------------------------------------------------------------- K-split mode, reducing warps
+// Owned block gb (local index j) after its last local gate_up item: (gate, up) sums of its items in item order,
+// plus the tail sums the next CTA published when the block runs into it (bounded wait on the epoch tag), h =
+// silu(gate) * up into the CTA's h tables, then the block's ready flag.
+__device__ void ks_finish_block(const FusedParams& p, const WarpList& L, int cta, int lane, const float* mail1,
+                                KsShared& ks, int gb, int j, int need, unsigned epoch) {
+  const Geo& g = p.geo;
+  const int t0 = gb * g.kp1 - L.a;
+  float gs = 0.f, us = 0.f;
+  for (int i = 0; i < need; ++i) {
+    gs += mail1[(size_t)(t0 + i) * 64 + lane];
+    us += mail1[(size_t)(t0 + i) * 64 + 32 + lane];
+  }
+  if ((gb + 1) * g.kp1 > L.b) {
+    const unsigned long long* slot = p.hand + (size_t)(cta + 1) * 64;
+    unsigned long long vg = 0, vu = 0;
+    unsigned it = 0;
+    while (true) {
+      vg = ld_relaxed_u64(slot + lane);
+      vu = ld_relaxed_u64(slot + 32 + lane);
+      if ((unsigned)(vg >> 32) == epoch && (unsigned)(vu >> 32) == epoch) break;
+      if (++it > kSpinLimit) {
+        flag_error(p.err, 2u);
+        break;
+      }
+      __nanosleep(32);
+    }
+    __syncwarp();
+    gs += __uint_as_float((unsigned)vg);
+    us += __uint_as_float((unsigned)vu);
+  }
+  htab_local(ks, j, silu(gs) * us, lane);
+  __syncwarp();
+  if (lane == 0) {
+    __threadfence_block();
+    st_volatile_shared(&ks.ready[j], 1);
+  }
+}
+
+// After the grid barrier: y[m, 32 columns] of unit (token m, column chunk) = routed_scaling * the sum of the
+// partials of the CTAs owning token m's blocks (warp w takes CTAs c0 + w, c0 + w + 16, ...; the warps' sums
+// are added in warp order: a fixed order, so results are reproducible).
+__device__ void ks_reduce(const FusedParams& p, const LiveRows& lv, int cta, int warp, int lane, KsShared& ks) {
+  const Geo& g = p.geo;
+  const int nch = g.H / 32;
+  const int units = g.M * nch;
+  const int q = lv.grid1 > 0 ? lv.n1 / lv.grid1 : 0, rem = lv.n1 - q * lv.grid1;
+  for (int uu = cta; uu < units; uu += gridDim.x) {
+    const int m = uu / nch, ch = uu - m * nch;
+    int r0 = 0;
+    for (int mm = 0; mm < m; ++mm) r0 += lv.tokcnt[mm];
+    const int cnt = lv.tokcnt[m];
+    float acc = 0.f;
+    if (cnt > 0) {
+      const int b0 = r0 * g.nb1, b1 = (r0 + cnt) * g.nb1;
+      const int c0 = range_owner(lv.n1, lv.grid1, b0 * g.kp1);
+      const int c1 = range_owner(lv.n1, lv.grid1, (b1 - 1) * g.kp1);
+      for (int c = c0 + warp; c <= c1; c += kWarps) {
+        // token m is segment 0 of CTA c when it is the token of c's first owned block
+        const int ac = c * q + min(c, rem);
+        const int bsc = (ac + g.kp1 - 1) / g.kp1;
+        const int mc = fdiv(lv.rowmap[fdiv(bsc, g.d_nb1)], g.d_topk);
+        acc += __ldcg(p.part + ((size_t)c * p.ks_segs + (m == mc ? 0 : 1)) * g.H + ch * 32 + lane);
+      }
+    }
+    ks.red[warp][lane] = acc;
+    csync();
+    if (warp == 0) {
+      float sum = 0.f;
+      for (int w = 0; w < kWarps; ++w) sum += ks.red[w][lane];
+      p.y[(int64_t)m * g.H + ch * 32 + lane] = __float2bfloat16(sum * p.rsf);
+    }
+    csync();
+  }
+}
+
+// The reducing warps of K-split mode after the prologue: warp 0 writes the plan; every warp takes work
+// indices from the CTA's counter -- gate_up items of the range first (in ring order), then down units
+// (segment, 128 output columns), whose items (the runs of owned blocks) wait for their blocks' h and are
+// accumulated in registers with the rows' routing weights; then the grid barrier and the final sums.
+__device__ void ks_layer(const FusedParams& p, const LiveRows& lv, const WarpList& L, int cta, int warp, int lane,
+                         unsigned char* smem, unsigned char* stages, uint32_t bars, int* tags, float* mail1,
+                         const RowPtr* rows, unsigned* misc) {
+  const Geo& g = p.geo;
+  KsShared& ks = *reinterpret_cast<KsShared*>(smem + p.off_ks);
+  const int nob = g.H / kKsCols;
+  const unsigned epoch = misc[3] + 1u;
+  const int range = L.range;
+  const int head_k = L.a % g.kp1 ? min(g.kp1 - L.a % g.kp1, range) : 0;   // items finishing the previous CTA's block
+  const int bs = range > 0 ? (L.a + g.kp1 - 1) / g.kp1 : 0;
+  const int ns = p.nstage;
+  const bool sbf = p.scale_bf16 != 0, hz = p.map13.has_zeros != 0;
+  if (warp == 0) {
+    if (lane == 0) {
+      ks_build_plan(g, lv, cta, nob, ks.plan);
+      __threadfence_block();
+      st_volatile_shared(&ks.plan.ready, 1);
+    }
+    __syncwarp();
+  }
+  auto take = [&](int seq) {                                  // the item's stage, once its copies landed
+    const int st = seq % ns;
+    if (lane == 0) {
+      wait_tag(tags, st, seq, p.err);
+      mbar_wait(bars + st * 8, (unsigned)(seq / ns) & 1u, p.err);
+    }
+    __syncwarp();
+    return static_cast<const unsigned char*>(stages + (size_t)st * kKsStageBytes);
+  };
+  auto release = [&](int seq) {
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bars + (ns + seq % ns) * 8);
+  };
+  int nunits = -1;
+  while (true) {
+    int t = 0;
+    if (lane == 0) t = atomicAdd(&ks.next, 1);
+    t = __shfl_sync(0xffffffffu, t, 0);
+    if (t < range) {
+      const int i = L.a + t;
+      Work w{};
+      w.kind = 1;
+      const int rc = fdiv(i, g.d_row1);
+      w.r = lv.rowmap[rc];
+      const int rem = i - rc * (g.nb1 * g.kp1);
+      w.b = fdiv(rem, g.d_kp1);
+      w.kp = rem - w.b * g.kp1;
+      w.slot = t;
+      const ItemRegs none{};
+      process_work<true, 1>(p, w, lane, none, take(t), smem, mail1, nullptr, rows);
+      release(t);
+      if (t < head_k) head_item_done(p, lv, L, cta, lane, mail1, head_k, epoch, misc + 2);
+      const int gb = fdiv(i, g.d_kp1);
+      if (gb >= bs) {
+        const int j = gb - bs;
+        const int need = min(L.b, (gb + 1) * g.kp1) - gb * g.kp1;
+        unsigned last = 0u;
+        if (lane == 0) {
+          __threadfence_block();
+          last = atomicAdd(&ks.blk_cnt[j], 1) == need - 1;
+          __threadfence_block();
+        }
+        if (__shfl_sync(0xffffffffu, last, 0)) ks_finish_block(p, L, cta, lane, mail1, ks, gb, j, need, epoch);
+      }
+      continue;
+    }
+    if (nunits < 0) {                                         // the plan (written right after the prologue)
+      if (lane == 0) {
+        unsigned it = 0;
+        while (ld_volatile_shared(&ks.plan.ready) == 0)
+          if (++it > kSpinLimit) {
+            flag_error(p.err, 2u);
+            break;
+          }
+        __threadfence_block();
+      }
+      __syncwarp();
+      nunits = ld_volatile_shared(&ks.plan.ready) ? ks.plan.nunits : 0;
+    }
+    const int u = t - range;
+    if (u >= nunits) break;
+    const KsPlan& pl = ks.plan;
+    const int seg = u / nob, cb = u - seg * nob;
+    const int nsub = pl.seg_nsub[seg];
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int tl = 0; tl < nsub; ++tl) {
+      const int sub = pl.seg_sub0[seg] + tl;
+      const int seq = range + pl.seg_base[seg] + cb * nsub + tl;
+      const int lb0 = pl.sub_lb0[sub], nb = pl.sub_nb[sub];
+      if (lane == 0) {                                        // the run's h-blocks are finished (bounded waits)
+        for (int jj = lb0; jj < lb0 + nb; ++jj) {
+          unsigned it = 0;
+          while (ld_volatile_shared(&ks.ready[jj]) == 0)
+            if (++it > kSpinLimit) {
+              flag_error(p.err, 2u);
+              break;
+            }
+        }
+        __threadfence_block();
+      }
+      const unsigned char* st = take(seq);
+      float v[4] = {0.f, 0.f, 0.f, 0.f};
+      ks_dot(st, ks, lb0, nb, pl.sub_w0[sub], sbf, hz, lane, v);
+      release(seq);
+      const float wr = rows[pl.sub_row[sub]].wt;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) acc[c] += v[c] * wr;
+    }
+    *reinterpret_cast<float4*>(p.part + ((size_t)cta * p.ks_segs + seg) * g.H + cb * kKsCols + lane * 4) =
+        make_float4(acc[0], acc[1], acc[2], acc[3]);
+  }
+  csync();
+  if (threadIdx.x == 0) grid_barrier(p.bar_count, p.bar_gen, epoch - 1u, gridDim.x, p.err);
+  csync();
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+  ks_reduce(p, lv, cta, warp, lane, ks);
+}
+
 // kTma = false: register mode (any expert map), 512 threads; every lane loads its item data itself.
-// kTma = true: copy-engine mode (slot arenas), 512 reducing threads + one producer warp.
-template <bool kTma>
+// kTma = true: copy-engine mode (slot arenas), 512 reducing threads + 4 producer warps.
+// kKs = true (copy-engine mode only): K-split down projection -- the reducing warps take the CTA's work
+// (gate_up items, then (token, 128 output columns) down units) from a shared counter; the warp that reduces
+// the last item of an owned h-block finishes it into the CTA's h tables; down units accumulate the owned
+// blocks' products in registers and store the CTA's partial outputs; after the grid barrier the CTAs sum the
+// partials of each token in CTA order (deterministic) into y.
+template <bool kTma, bool kKs = false>
 __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_kernel(const __grid_constant__ FusedParams p) {
+  static_assert(!kKs || kTma, "K-split mode streams through the copy engine");
+  constexpr size_t kStage = kKs ? kKsStageBytes : kStageBytes;
   extern __shared__ __align__(128) unsigned char smem[];
   const Geo& g = p.geo;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -901,9 +1378,22 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
       if (b < p.nstage) tags[b] = -1;
     }
     if (pt == 0) mbar_init(hbar, 1);                          // the h-table copies' barrier
+    if constexpr (kKs) {                                      // work counter, block counts and flags, plan flag
+      KsShared& ks = *reinterpret_cast<KsShared*>(smem + p.off_ks);
+      if (pt < kKsMaxOwned) {
+        ks.blk_cnt[pt] = 0;
+        ks.ready[pt] = 0;
+      }
+      if (pt == 32) {
+        ks.next = 0;
+        ks.plan.ready = 0;
+      }
+    }
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     if (pt < 6 && (p.map13.has_zeros || (pt != 2 && pt != 5)))
       asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&p.tm[pt])) : "memory");
+    if (kKs && pt >= 64 && pt < 72 && (p.map13.has_zeros || pt < 70))
+      asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&p.tmk[pt - 64])) : "memory");
   }
   // Launched with programmatic stream serialisation, this CTA may start while the previous kernel of the
   // stream is finishing: everything above touches only shared memory and the kernel's own parameters;
@@ -1079,12 +1569,19 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
       __syncwarp();
       const int nblk = __popc(bal) * g.nb1;
       const LiveRows plv{prow, ptokrow, ptokcnt, nullptr, nblk * g.kp1, max(1, min((int)gridDim.x, nblk))};
-      produce(p, plv, [&](int r, int) { return pslot[r]; }, cta, stages, bars, tags, pw, lane);
+      if constexpr (kKs)
+        produce_ks(p, plv, [&](int r, int) { return pslot[r]; }, cta, stages, bars, tags, pw, lane,
+                   reinterpret_cast<const KsShared*>(smem + p.off_ks));
+      else
+        produce(p, plv, [&](int r, int) { return pslot[r]; }, cta, stages, bars, tags, pw, lane);
     } else {
       bar_wait(2, 32 * (kProducers + 1));                     // routing compacted by warp 0
       const LiveRows lv{rowmap, tokrow, tokcnt, slotrow, (int)misc[4], (int)misc[5]};
-      produce(p, lv, [&](int r, int kind) { const RowPtr& rp = rows[r]; return rp.ok[kind - 1] ? rp.slot : -1; }, cta,
-              stages, bars, tags, pw, lane);
+      auto slot_of = [&](int r, int kind) { const RowPtr& rp = rows[r]; return rp.ok[kind - 1] ? rp.slot : -1; };
+      if constexpr (kKs)
+        produce_ks(p, lv, slot_of, cta, stages, bars, tags, pw, lane, reinterpret_cast<const KsShared*>(smem + p.off_ks));
+      else
+        produce(p, lv, slot_of, cta, stages, bars, tags, pw, lane);
     }
     return;
    }
@@ -1093,6 +1590,9 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
   else csync();
   const LiveRows lv{rowmap, tokrow, tokcnt, slotrow, (int)misc[4], (int)misc[5]};
   const WarpList L = warp_list(g, lv, cta, warp);
+  if constexpr (kKs) {
+    ks_layer(p, lv, L, cta, warp, lane, smem, stages, bars, tags, mail1, rows, misc);
+  } else {
   for (int idx = threadIdx.x; idx < g.max_units * g.top_k; idx += kThreads) {   // rows of the CTA's down units
     const int q = fdiv(idx, g.d_topk), jr = idx - q * g.top_k, u = cta + g.grid * q;
     int row = -1;
@@ -1133,7 +1633,7 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
         mbar_wait(bars + st * 8, (unsigned)(w.seq / p.nstage) & 1u, p.err);
       }
       __syncwarp();
-      process_work<true, K>(p, w, lane, cur, stages + (size_t)st * kStageBytes, smem, mail1, mail2, rows);
+      process_work<true, K>(p, w, lane, cur, stages + (size_t)st * kStage, smem, mail1, mail2, rows);
       __syncwarp();
       if (lane == 0) mbar_arrive(bars + (p.nstage + st) * 8);
       if constexpr (K == 1)
@@ -1164,6 +1664,7 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
       p.y[(int64_t)m * g.H + b * 32 + lane] = __float2bfloat16(acc * p.rsf);
     }
   }
+  }  // (kKs == false)
 }
 
 }  // namespace
@@ -1172,13 +1673,28 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
 // only grow and are equal between calls, so zero-filling before the first call is all they need),
 // kMaxGrid x 512 bytes of hand-off words (tagged with past epochs, never reset; zero qualifies), then the
 // down tables of the routed rows [R][htab_bytes(I)] (2.25 I bytes each).
+// K-split mode puts its partial outputs after the hand-off words instead: [kKsMaxGrid][min(M, kKsMaxSeg)][H]
+// fp32. layer_workspace_bytes covers both modes (what a caller should pass); layer_workspace_min_bytes is
+// what the layer accepts (the K-split mode is then taken only when its partials fit).
 constexpr int kMaxGrid = 256;
 constexpr size_t kHandBytes = (size_t)kMaxGrid * 64 * 8;
-size_t layer_workspace_bytes(int M, int H, int I, int top_k) {
+constexpr size_t kHeadBytes = 256 + kHandBytes;
+size_t layer_workspace_min_bytes(int M, int H, int I, int top_k) {
   (void)H;
-  const size_t head = 256 + kHandBytes;
-  if (M <= 0 || I <= 0 || top_k <= 0) return head;
-  return head + (size_t)M * top_k * htab_bytes(I);
+  if (M <= 0 || I <= 0 || top_k <= 0) return kHeadBytes;
+  return kHeadBytes + (size_t)M * top_k * htab_bytes(I);
+}
+bool ks_shape_ok(int M, int H, int I, int top_k) {
+  return M > 0 && top_k > 0 && M * top_k <= kKsMaxRows && H % kKsCols == 0 && I % kGroup == 0;
+}
+size_t ks_workspace_bytes(int M, int H) {
+  return kHeadBytes + (size_t)kKsMaxGrid * (M < kKsMaxSeg ? M : kKsMaxSeg) * H * 4;
+}
+size_t layer_workspace_bytes(int M, int H, int I, int top_k) {
+  const size_t a = layer_workspace_min_bytes(M, H, I, top_k);
+  if (!ks_shape_ok(M, H, I, top_k)) return a;
+  const size_t b = ks_workspace_bytes(M, H);
+  return a > b ? a : b;
 }
 
 namespace {
@@ -1191,16 +1707,25 @@ struct TmaPlan {
   int nstage;
   size_t stages, rest, total;
 };
-TmaPlan tma_plan(const Geo& g) {
+SmemPlan smem_plan_mode(const Geo& g, bool ks) {
+  SmemPlan s = smem_plan(g, ks);
+  if (ks) {
+    s.ks = (sizeof(KsShared) + 15) & ~size_t(15);
+    s.total += s.ks;
+  }
+  return s;
+}
+TmaPlan tma_plan(const Geo& g, bool ks = false) {
   TmaPlan t{};
   const size_t cap = 227 * 1024;
-  t.rest = smem_plan(g).total;
+  const size_t sb = ks ? kKsStageBytes : kStageBytes;
+  t.rest = smem_plan_mode(g, ks).total;
   const size_t fixed = t.rest + 2 * kMaxStages * 8 + kMaxStages * 4;
-  int ns = fixed < cap ? (int)((cap - fixed) / kStageBytes) : 0;
+  int ns = fixed < cap ? (int)((cap - fixed) / sb) : 0;
   if (ns > kMaxStages) ns = kMaxStages;
   ns -= ns % kIssuers;
   t.nstage = ns >= kMinStages ? ns : 0;
-  t.stages = (size_t)t.nstage * kStageBytes;
+  t.stages = (size_t)t.nstage * sb;
   t.total = t.stages + t.rest + 2 * (size_t)t.nstage * 8 + (size_t)t.nstage * 4;
   return t;
 }
@@ -1286,6 +1811,52 @@ bool arena_maps(const LayerArgs& a, CUtensorMap (&tm)[6]) {
   return true;
 }
 
+// K-split mode's down maps over the same arena: codes with boxes of 128 columns x 2, 4, 6, 8 word rows (runs of
+// 1..4 h-blocks), scales and zero points with boxes of 128 columns x 1 or 2 group rows. Cached like the six.
+bool ks_arena_maps(const LayerArgs& a, CUtensorMap (&tmk)[8]) {
+  struct Key {
+    const void* b[3];
+    int64_t st[3];
+    int H, I, S;
+    bool operator==(const Key& o) const {
+      for (int k = 0; k < 3; ++k)
+        if (b[k] != o.b[k] || st[k] != o.st[k]) return false;
+      return H == o.H && I == o.I && S == o.S;
+    }
+  };
+  static thread_local Key last{};
+  static thread_local bool have = false;
+  static thread_local CUtensorMap cache[8];
+  const Key k{{a.map2.wbase, a.map2.sbase, a.map2.zbase}, {a.map2.wstride, a.map2.sstride, a.map2.zstride},
+              a.H, a.I, a.map2.S};
+  if (!(have && last == k)) {
+    have = false;
+    if (!tensor_map_encoder()) return false;
+    const cuuint64_t I = (cuuint64_t)a.I, H = (cuuint64_t)a.H, S = (cuuint64_t)a.map2.S;
+    const cuuint64_t dc[3] = {H, I / 16, S}, sc[2] = {H * 4, (cuuint64_t)a.map2.wstride};
+    for (int nb = 1; nb <= 4; ++nb) {
+      const cuuint32_t bc[3] = {(cuuint32_t)kKsCols, (cuuint32_t)(2 * nb), 1};
+      if (!encode_map(&cache[nb - 1], CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, a.map2.wbase, dc, sc, bc)) return false;
+    }
+    const cuuint64_t ds[3] = {H, I / kGroup, S}, ss[2] = {H * 2, (cuuint64_t)a.map2.sstride};
+    for (int ng = 1; ng <= 2; ++ng) {
+      const cuuint32_t bs[3] = {(cuuint32_t)kKsCols, (cuuint32_t)ng, 1};
+      if (!encode_map(&cache[4 + ng - 1], CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, a.map2.sbase, ds, ss, bs)) return false;
+    }
+    if (a.map2.has_zeros) {
+      const cuuint64_t dz[3] = {H / 4, I / kGroup, S}, sz[2] = {H / 4, (cuuint64_t)a.map2.zstride};
+      for (int ng = 1; ng <= 2; ++ng) {
+        const cuuint32_t bz[3] = {(cuuint32_t)(kKsCols / 4), (cuuint32_t)ng, 1};
+        if (!encode_map(&cache[6 + ng - 1], CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, a.map2.zbase, dz, sz, bz)) return false;
+      }
+    }
+    last = k;
+    have = true;
+  }
+  for (int k2 = 0; k2 < 8; ++k2) tmk[k2] = cache[k2];
+  return true;
+}
+
 // Copy-engine mode needs a slot arena, 16-byte strides in every map (H and I multiples of 64) and the
 // driver's tensor-map encoder.
 bool tma_eligible(const LayerArgs& a) {
@@ -1304,17 +1875,18 @@ Geo layer_geo(const LayerArgs& a, int M, int grid_cap) {
 }
 
 int launch_fused(const LayerArgs& a, int M, const void* x, const int32_t* ids, const float* w, void* y,
-                        int grid_cap, bool tma) {
+                        int grid_cap, bool tma, bool ks) {
   const Geo g = layer_geo(a, M, grid_cap);
-  const SmemPlan sp = smem_plan(g);
+  const SmemPlan sp = smem_plan_mode(g, ks);
   FusedParams p{};
   p.x = static_cast<const __nv_bfloat16*>(x); p.ids = ids; p.topk_w = w;
   p.map13 = a.map13; p.map2 = a.map2; p.scale_bf16 = a.scale_bf16; p.rsf = a.routed_scaling;
   p.y = static_cast<__nv_bfloat16*>(y); p.geo = g; p.err = a.err;
   size_t base = 0, total = sp.total;
   if (tma) {
-    const TmaPlan tp = tma_plan(g);
+    const TmaPlan tp = tma_plan(g, ks);
     if (tp.nstage == 0 || !arena_maps(a, p.tm)) return kErrShape;
+    if (ks && !ks_arena_maps(a, p.tmk)) return kErrShape;
     p.nstage = tp.nstage;
     p.off_stages = 0;
     base = tp.stages;
@@ -1329,13 +1901,16 @@ int launch_fused(const LayerArgs& a, int M, const void* x, const int32_t* ids, c
   p.off_live = p.off_misc + sp.misc;
   p.off_slots = p.off_live + sp.live;
   p.off_preg = p.off_slots + sp.slots;
+  p.off_ks = p.off_preg + sp.preg;
   unsigned* ctl = static_cast<unsigned*>(a.workspace);
   p.bar_count = ctl;
   p.bar_gen = ctl + 32;
   p.hand = reinterpret_cast<unsigned long long*>(static_cast<unsigned char*>(a.workspace) + 256);
-  p.htab = static_cast<unsigned char*>(a.workspace) + 256 + kHandBytes;
+  p.htab = static_cast<unsigned char*>(a.workspace) + kHeadBytes;
+  p.part = reinterpret_cast<float*>(static_cast<unsigned char*>(a.workspace) + kHeadBytes);
+  p.ks_segs = M < kKsMaxSeg ? M : kKsMaxSeg;
 
-  auto kern = tma ? fused_layer_kernel<true> : fused_layer_kernel<false>;
+  auto kern = ks ? fused_layer_kernel<true, true> : (tma ? fused_layer_kernel<true> : fused_layer_kernel<false>);
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)total) != cudaSuccess)
     return kErrLaunch;
   cudaLaunchConfig_t cfg{};
@@ -1357,11 +1932,24 @@ int launch_fused(const LayerArgs& a, int M, const void* x, const int32_t* ids, c
 
 bool layer_arena_maps(const LayerArgs& a, CUtensorMap (&tm)[6]) { return tma_eligible(a) && arena_maps(a, tm); }
 
+// K-split mode for this launch: slot arena in copy-engine mode, at most kKsMaxRows routed rows, a CTA finishing
+// at most kKsMaxOwned h-blocks of at most two routed rows (so of at most kKsMaxSeg tokens), a grid whose partials
+// the workspace holds, and a ring of at least kMinStages stages.
+bool ks_eligible(const LayerArgs& a, int M, int grid_cap) {
+  if (!ks_shape_ok(M, a.H, a.I, a.top_k)) return false;
+  if (a.workspace_bytes < ks_workspace_bytes(M, a.H)) return false;
+  const Geo g = layer_geo(a, M, grid_cap);
+  if (g.grid > kKsMaxGrid) return false;
+  const int owned = (g.max_range + g.kp1 - 1) / g.kp1;        // block starts inside the longest range
+  if (owned > kKsMaxOwned || owned > g.nb1 + 1) return false;
+  return tma_plan(g, true).nstage > 0;
+}
+
 int decode_layer_fused(const LayerArgs& a) {
   if (a.M <= 0) return kOk;
   if (a.H % kGroup != 0 || a.I % kGroup != 0 || a.top_k <= 0) return kErrShape;
   if (!a.x || !a.ids || !a.topk_w || !a.y) return kErrArg;
-  if (!a.workspace || a.workspace_bytes < layer_workspace_bytes(a.M, a.H, a.I, a.top_k)) return kErrWorkspace;
+  if (!a.workspace || a.workspace_bytes < layer_workspace_min_bytes(a.M, a.H, a.I, a.top_k)) return kErrWorkspace;
   if (reinterpret_cast<uintptr_t>(a.workspace) & 255u) return kErrAlign;
 
   static thread_local int cached_dev = -1, cached_cap = 0;
@@ -1385,9 +1973,10 @@ int decode_layer_fused(const LayerArgs& a) {
   if (!fits(mmax)) return kErrShape;
   for (int m0 = 0; m0 < a.M; m0 += mmax) {
     const int mc = a.M - m0 < mmax ? a.M - m0 : mmax;
+    const bool ks = tma && ks_eligible(a, mc, cached_cap);
     const int st = launch_fused(a, mc, static_cast<const __nv_bfloat16*>(a.x) + (size_t)m0 * a.H,
                                 a.ids + (size_t)m0 * a.top_k, a.topk_w + (size_t)m0 * a.top_k,
-                                static_cast<__nv_bfloat16*>(a.y) + (size_t)m0 * a.H, cached_cap, tma);
+                                static_cast<__nv_bfloat16*>(a.y) + (size_t)m0 * a.H, cached_cap, tma, ks);
     if (st != kOk) return st;
   }
   return kOk;
