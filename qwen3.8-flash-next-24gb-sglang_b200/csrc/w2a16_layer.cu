@@ -856,7 +856,9 @@ __device__ void produce_ks(const FusedParams& p, const LiveRows& lv, SlotOf slot
   };
   constexpr int kPending = 15;                                // a down item decoded before the plan existed
   for (int j0 = 0;; j0 += kIssuers / kProducers) {
-    if (!have_plan && j0 >= nw) {                             // the gate_up range is issued: now the down items
+    // before an iteration whose issuing lanes reach past the gate_up range (j0 + 1 >= nw), the true item count:
+    // otherwise a lane's item between the old and the new bound would be skipped
+    if (!have_plan && j0 + kIssuers / kProducers - 1 >= nw) {
       bool ok = true;
       if (lane == 0) ok = wait_plan();
       ok = __shfl_sync(0xffffffffu, ok, 0);
