@@ -51,16 +51,14 @@ constexpr int kZeroOff = 4352;
 constexpr int kMinStages = 16, kMaxStages = 48;             // multiples of kIssuers
 
 // K-split mode (decode sizes: at most kKsMaxRows routed rows). A CTA multiplies the h-blocks it finishes by
-// the matching K-slice of its rows' down projections right away, so the down weights and their products
-// stream with the gate_up items; per-CTA partial outputs are summed after one grid barrier. Down items
-// are (run of <= 4 owned h-blocks of one row, 128 output columns): codes (2 word rows per block) x 512 B at
-// 0, the scale rows of the <= 2 quantization groups the run touches at 4096, their zero-point rows at
-// 4608.
-constexpr int kKsStageBytes = 4736;
-constexpr int kKsScaleOff = 4096, kKsZeroOff = 4608;
-constexpr int kKsCols = 128;                                 // output columns of a down item
+// the matching K-slice of its rows' down projections, so no h crosses CTAs and the down products need no
+// barrier of their own; per-CTA partial outputs are summed after one grid barrier. The down slice of a run
+// of consecutive owned blocks of one routed row ("piece") is contiguous in the arena (2 word rows per block,
+// plus the scale and zero-point rows of the groups it touches), so each piece arrives in the CTA's down
+// buffer by 2-3 bulk copies issued right after the routing, streaming alongside the gate_up ring.
+constexpr int kKsCols = 128;                                 // output columns of a down unit
 constexpr int kKsMaxOwned = 12;                              // h-blocks one CTA finishes
-constexpr int kKsMaxSub = 8;                                 // runs of <= 4 owned blocks
+constexpr int kKsMaxPiece = 2;                               // routed rows one CTA's owned blocks belong to
 constexpr int kKsMaxRows = 32;                               // routed rows of a K-split launch
 constexpr int kKsMaxGrid = 160;                              // CTAs whose partials the workspace holds
 constexpr int kKsMaxSeg = 2;                                 // tokens one CTA's owned blocks belong to
@@ -176,9 +174,8 @@ struct FusedParams {
   // copy-engine mode: tensor maps over the slot arena -- gate_up codes / scales / zero points (4-D:
   // column within half, half, row, slot) and down codes / scales / zero points (3-D: column, row, slot)
   CUtensorMap tm[6];
-  // K-split mode: down codes with boxes of 128 columns x 2, 4, 6, 8 word rows, down scales and zero points
-  // with boxes of 1 and 2 group rows
-  CUtensorMap tmk[8];
+  size_t off_kd;         // K-split: the down buffer (kd_bytes) in shared memory
+  int kd_bytes;
   float* part;           // K-split: [grid][ks_segs][H] fp32 partial outputs
   int ks_segs;           // K-split: segments per CTA the partial buffer holds (min(M, kKsMaxSeg))
   size_t off_ks;
@@ -606,12 +603,13 @@ __device__ __forceinline__ int4 item_desc(const Geo& g, const LiveRows& lv, cons
 // issuer. Each item is one tensor copy of codes (4 KB), one of scales and one of zero-point windows,
 // completing on the stage's `full` barrier; a stage is refilled once the warp that reduced it arrived on
 // its `empty` barrier. Items of a non-resident expert complete their phase on the arrival alone.
-template <class SlotOf>
+// kGateOnly (K-split mode): the ring carries the gate_up range only.
+template <bool kGateOnly, class SlotOf>
 __device__ void produce(const FusedParams& p, const LiveRows& lv, SlotOf slot_of, int cta, unsigned char* stages,
                         uint32_t bars, int* tags, int pr, int lane) {
   const Geo& g = p.geo;
   const WarpList L0 = warp_list(g, lv, cta, 0);
-  const int n = L0.range + L0.nu * g.s2;
+  const int n = kGateOnly ? L0.range : L0.range + L0.nu * g.s2;
   const int nw = n > pr ? (n - pr + kProducers - 1) / kProducers : 0;   // items of this warp: pr + kProducers*j
   const int ns = p.nstage;
   const bool hz = p.map13.has_zeros != 0;
@@ -670,18 +668,21 @@ __device__ void produce(const FusedParams& p, const LiveRows& lv, SlotOf slot_of
 
 // ----------------------------------------------------------------------------- K-split mode
 // The CTA's plan: the h-blocks it finishes ("owned": those whose first gate_up item lies in its range), cut
-// into runs of <= 4 consecutive blocks of one routed row, and the tokens ("segments") those rows belong
-// to. Down items are numbered segment by segment; within a segment by output block (128 columns), then
-// run, so the items one warp accumulates for one (segment, output block) unit are consecutive.
+// into pieces (runs of one routed row), the tokens ("segments") those rows belong to, and where each piece's
+// down slice lies in the down buffer: codes of all pieces first, then their scale rows, then their zero rows.
+// Down units are (segment, 128 output columns), segment-major.
 struct KsPlan {
-  int ready;                         // set once the plan is in place (the producers wait for it)
+  int ready;                         // set once the plan is in place
   int bs, nown;                      // first owned block (over the live rows), owned blocks
-  int nseg, nsub, ndown, nunits;
-  int seg_tok[kKsMaxSeg], seg_sub0[kKsMaxSeg], seg_nsub[kKsMaxSeg], seg_base[kKsMaxSeg];
-  int sub_row[kKsMaxSub], sub_lb0[kKsMaxSub], sub_nb[kKsMaxSub], sub_w0[kKsMaxSub];
-  int blk_need[kKsMaxOwned];         // gate_up items of each owned block inside this CTA's range
+  int nseg, npiece, nunits, ok;      // ok = 0: the plan did not fit its limits (error bit 2, no down work)
+  int seg_tok[kKsMaxSeg], seg_p0[kKsMaxSeg], seg_np[kKsMaxSeg];
+  int piece_row[kKsMaxPiece], piece_lb0[kKsMaxPiece], piece_nb[kKsMaxPiece], piece_w0[kKsMaxPiece];
+  int piece_g0[kKsMaxPiece], piece_ng[kKsMaxPiece];
+  int piece_code[kKsMaxPiece], piece_scale[kKsMaxPiece], piece_zero[kKsMaxPiece];   // byte offsets
+  int kd_total;                      // bytes of the down buffer this CTA fills
 };
 struct KsShared {
+  unsigned long long kd_bar;         // mbarrier: the down buffer's bulk copies landed
   KsPlan plan;
   int blk_cnt[kKsMaxOwned];          // reduced gate_up items per owned block
   int ready[kKsMaxOwned];            // owned block's h table written
@@ -692,57 +693,66 @@ struct KsShared {
   float red[kWarps][32];             // final reduction: one partial sum per warp and column
 };
 
-// Lane 0 of one warp: the plan of this CTA (every quantity derived from the live rows and the ranges, the
-// same in every warp that builds it).
-__device__ void ks_build_plan(const Geo& g, const LiveRows& lv, int cta, int nob, KsPlan& pl) {
+// Lane 0 of one warp: the plan of this CTA (derived from the live rows and the ranges only).
+__device__ void ks_build_plan(const Geo& g, const LiveRows& lv, int cta, int nob, bool hz, int kd_cap, KsPlan& pl) {
   const WarpList L = warp_list(g, lv, cta, 0);
   const int bs = L.range > 0 ? (L.a + g.kp1 - 1) / g.kp1 : 0;
   const int be = L.range > 0 ? (L.b + g.kp1 - 1) / g.kp1 : 0;
   pl.bs = bs;
-  pl.nown = min(be - bs, kKsMaxOwned);               // (the host guarantees be - bs <= kKsMaxOwned)
+  pl.nown = be - bs;
+  pl.ok = pl.nown <= kKsMaxOwned;
   pl.nseg = 0;
-  pl.nsub = 0;
+  pl.npiece = 0;
   int last_rc = -1;
-  for (int j = 0; j < pl.nown; ++j) {
+  for (int j = 0; pl.ok && j < pl.nown; ++j) {
     const int gb = bs + j;
     const int rc = fdiv(gb, g.d_nb1), hb = gb - rc * g.nb1;
-    const int r = lv.rowmap[rc], m = fdiv(r, g.d_topk);
-    const int hi = min(L.b, (gb + 1) * g.kp1);
-    pl.blk_need[j] = hi - gb * g.kp1;
-    const bool fresh = pl.nsub == 0 || rc != last_rc || pl.sub_nb[pl.nsub - 1] == 4;
-    if (fresh && pl.nsub < kKsMaxSub) {
+    if (rc != last_rc) {
+      const int r = lv.rowmap[rc], m = fdiv(r, g.d_topk);
+      if (pl.npiece == kKsMaxPiece) {
+        pl.ok = 0;
+        break;
+      }
       if (pl.nseg == 0 || pl.seg_tok[pl.nseg - 1] != m) {
-        if (pl.nseg == kKsMaxSeg) break;               // (the host guarantees at most two tokens)
+        if (pl.nseg == kKsMaxSeg) {
+          pl.ok = 0;
+          break;
+        }
         pl.seg_tok[pl.nseg] = m;
-        pl.seg_sub0[pl.nseg] = pl.nsub;
-        pl.seg_nsub[pl.nseg] = 0;
+        pl.seg_p0[pl.nseg] = pl.npiece;
+        pl.seg_np[pl.nseg] = 0;
         ++pl.nseg;
       }
-      pl.sub_row[pl.nsub] = r;
-      pl.sub_lb0[pl.nsub] = j;
-      pl.sub_nb[pl.nsub] = 1;
-      pl.sub_w0[pl.nsub] = 2 * hb;
-      ++pl.seg_nsub[pl.nseg - 1];
-      ++pl.nsub;
-    } else if (!fresh) {
-      ++pl.sub_nb[pl.nsub - 1];
+      pl.piece_row[pl.npiece] = r;
+      pl.piece_lb0[pl.npiece] = j;
+      pl.piece_nb[pl.npiece] = 1;
+      pl.piece_w0[pl.npiece] = 2 * hb;
+      ++pl.seg_np[pl.nseg - 1];
+      ++pl.npiece;
+    } else {
+      ++pl.piece_nb[pl.npiece - 1];
     }
     last_rc = rc;
   }
-  pl.ndown = 0;
-  for (int s2 = 0; s2 < pl.nseg; ++s2) {
-    pl.seg_base[s2] = pl.ndown;
-    pl.ndown += nob * pl.seg_nsub[s2];
+  int off = 0;
+  for (int q = 0; q < pl.npiece; ++q) {
+    const int w0 = pl.piece_w0[q], nb = pl.piece_nb[q];
+    pl.piece_g0[q] = w0 >> 3;
+    pl.piece_ng[q] = ((w0 + 2 * nb - 1) >> 3) - (w0 >> 3) + 1;
+    pl.piece_code[q] = off;
+    off += 2 * nb * g.H * 4;
   }
-  pl.nunits = pl.nseg * nob;
-}
-
-// Down item d of the plan -> (segment, output block, run).
-__device__ __forceinline__ void ks_item(const KsPlan& pl, int nob, int d, int& seg, int& cb, int& sub) {
-  seg = (pl.nseg > 1 && d >= pl.seg_base[1]) ? 1 : 0;
-  const int within = d - pl.seg_base[seg], ns = pl.seg_nsub[seg];
-  cb = within / ns;
-  sub = pl.seg_sub0[seg] + (within - cb * ns);
+  for (int q = 0; q < pl.npiece; ++q) {
+    pl.piece_scale[q] = off;
+    off += pl.piece_ng[q] * g.H * 2;
+  }
+  for (int q = 0; q < pl.npiece; ++q) {
+    pl.piece_zero[q] = off;
+    if (hz) off += pl.piece_ng[q] * (g.H / 4);
+  }
+  if (off > kd_cap) pl.ok = 0;
+  pl.kd_total = pl.ok ? off : 0;
+  pl.nunits = pl.ok ? pl.nseg * nob : 0;
 }
 
 // h of an owned block (lane l holds element l) -> the CTA's fixed-point table of that block: one exponent
@@ -763,12 +773,17 @@ __device__ __forceinline__ void htab_local(KsShared& ks, int j, float h, int lan
   }
 }
 
-// One down item from its ring stage: lane l, output columns cb * 128 + 4l .. +3, the run's word rows (two per
-// owned block) against the blocks' h tables; returns the item's 4 sums (before the routing weight).
-__device__ __forceinline__ void ks_dot(const unsigned char* st, const KsShared& ks, int lb0, int nb, int w0, bool sbf,
-                                       bool has_z, int lane, float (&v)[4]) {
+// Piece q's contribution to output columns cb * 128 + 4 lane .. +3 from the down buffer: its word rows (two per
+// owned block) against the blocks' h tables, each quantization group's scales applied once its blocks are
+// summed; returns the 4 sums before the routing weight.
+__device__ __forceinline__ void ks_piece_dot(const unsigned char* kd, const KsShared& ks, const KsPlan& pl, int q,
+                                             int cb, int H, bool sbf, bool has_z, int lane, float (&v)[4]) {
+  const int nb = pl.piece_nb[q], w0 = pl.piece_w0[q], g0 = pl.piece_g0[q], lb0 = pl.piece_lb0[q];
+  const size_t rowb = (size_t)H * 4;
+  const unsigned char* code = kd + pl.piece_code[q] + (size_t)cb * (kKsCols * 4) + lane * 16;
+  const unsigned char* scl = kd + pl.piece_scale[q] + (size_t)cb * (kKsCols * 2) + lane * 8;
+  const unsigned char* zr = kd + pl.piece_zero[q] + (size_t)cb * (kKsCols / 4) + lane;
   float f[4] = {0.f, 0.f, 0.f, 0.f};
-  const int g0 = w0 >> 3;
   for (int j = 0; j < nb; ++j) {
     const int wr = w0 + 2 * j, gi = (wr >> 3) - g0;
     int acc[4][4];
@@ -778,7 +793,7 @@ __device__ __forceinline__ void ks_dot(const unsigned char* st, const KsShared& 
       for (int k = 0; k < 4; ++k) acc[c][k] = 0;
 #pragma unroll
     for (int kk = 0; kk < 2; ++kk) {
-      const uint4 w = *reinterpret_cast<const uint4*>(st + (size_t)(2 * j + kk) * (kKsCols * 4) + lane * 16);
+      const uint4 w = *reinterpret_cast<const uint4*>(code + (size_t)(2 * j + kk) * rowb);
       const uint4* xp = reinterpret_cast<const uint4*>(&ks.hpairs[lb0 + j][kk * kXRegs]);
       const uint4 xa = xp[0], xb = xp[1];
       const uint32_t xr[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
@@ -788,17 +803,16 @@ __device__ __forceinline__ void ks_dot(const unsigned char* st, const KsShared& 
       word_dot(w.w, xr, acc[3]);
     }
     const int m64x = ks.hm64x[lb0 + j];
-    const float scl = ks.hscl[lb0 + j];
-    const uint32_t zb = has_z ? (uint32_t)st[kKsZeroOff + gi * (kKsCols / 4) + lane] : 0u;
+    const float sx = ks.hscl[lb0 + j];
+    const uint32_t zb = has_z ? (uint32_t)zr[(size_t)gi * (H / 4)] : 0u;
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       const int zp = has_z ? (int)((zb >> (2 * c)) & 3u) : 2;
-      f[c] += (float)(combine_classes(acc[c]) + zp * m64x) * scl;
+      f[c] += (float)(combine_classes(acc[c]) + zp * m64x) * sx;
     }
-    // the run ends here or the next block starts a new quantization group: apply this group's scales
-    if (j == nb - 1 || ((wr + 2) >> 3) != (wr >> 3)) {
+    if (j == nb - 1 || ((wr + 2) >> 3) != (wr >> 3)) {       // the group's blocks are summed: its scales
       float sc[4];
-      scales4(*reinterpret_cast<const uint2*>(st + kKsScaleOff + gi * (kKsCols * 2) + lane * 8), sbf, sc);
+      scales4(*reinterpret_cast<const uint2*>(scl + (size_t)gi * (H * 2)), sbf, sc);
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         v[c] += f[c] * sc[c];
@@ -812,112 +826,6 @@ __device__ __forceinline__ void ks_dot(const unsigned char* st, const KsShared& 
 __device__ __forceinline__ int range_owner(int n1, int grid1, int i) {
   const int q = n1 / grid1, rem = n1 - q * grid1;
   return i < rem * (q + 1) ? i / (q + 1) : rem + (i - rem * (q + 1)) / q;
-}
-
-// K-split mode's producers: the same issuing scheme as produce() over the CTA's gate_up range followed by the
-// plan's down items. The plan comes from warp 0; a producer waits for it (bounded) only when a batch of
-// descriptors first reaches past the gate_up range.
-template <class SlotOf>
-__device__ void produce_ks(const FusedParams& p, const LiveRows& lv, SlotOf slot_of, int cta, unsigned char* stages,
-                           uint32_t bars, int* tags, int pr, int lane, const KsShared* ks) {
-  const Geo& g = p.geo;
-  const WarpList L0 = warp_list(g, lv, cta, 0);
-  const int nob = g.H / kKsCols;
-  int n = L0.range;                                           // grows by the down items once the plan is read
-  bool have_plan = false;
-  int nw = n > pr ? (n - pr + kProducers - 1) / kProducers : 0;
-  const int ns = p.nstage;
-  const bool hz = p.map13.has_zeros != 0;
-  const bool aligned = (smem_u32(stages) & 127u) == 0;
-  if (!aligned && lane == 0) flag_error(p.err, 4u);
-  const bool issuer = lane < kIssuers / kProducers;
-  const uint64_t pol = evict_first_policy();
-  int4 batch = make_int4(0, 0, 0, 0);
-  // Down-item descriptor from the plan (kind 3 | blocks << 4 | groups << 8, slot, output block, first word row).
-  auto down_desc = [&](int d) {
-    int seg, cb, sub;
-    ks_item(ks->plan, nob, d, seg, cb, sub);
-    const int nb = ks->plan.sub_nb[sub], w0 = ks->plan.sub_w0[sub];
-    const int ng = ((w0 + 2 * nb - 1) >> 3) - (w0 >> 3) + 1;
-    const int sl = slot_of(ks->plan.sub_row[sub], 2);
-    return make_int4(sl >= 0 ? (3 | (nb << 4) | (ng << 8)) : 0, sl, cb, w0);
-  };
-  // Bounded wait for warp 0's plan (error bit 1 when it never comes); true when it is there.
-  auto wait_plan = [&]() {
-    unsigned it = 0;
-    while (ld_volatile_shared(&ks->plan.ready) == 0) {
-      if (++it > kSpinLimit) {
-        flag_error(p.err, 2u);
-        return false;
-      }
-    }
-    __threadfence_block();
-    return true;
-  };
-  constexpr int kPending = 15;                                // a down item decoded before the plan existed
-  for (int j0 = 0;; j0 += kIssuers / kProducers) {
-    // before an iteration whose issuing lanes reach past the gate_up range (j0 + 1 >= nw), the true item count:
-    // otherwise a lane's item between the old and the new bound would be skipped
-    if (!have_plan && j0 + kIssuers / kProducers - 1 >= nw) {
-      bool ok = true;
-      if (lane == 0) ok = wait_plan();
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      __syncwarp();
-      __threadfence_block();
-      n = L0.range + (ok ? ks->plan.ndown : 0);
-      nw = n > pr ? (n - pr + kProducers - 1) / kProducers : 0;
-      have_plan = true;
-    }
-    if (j0 >= nw) break;
-    if ((j0 & 31) == 0) {
-      const int ii = pr + kProducers * (j0 + lane);
-      const bool ready = have_plan || ld_volatile_shared(&ks->plan.ready) != 0;
-      if (ready) __threadfence_block();
-      batch = make_int4(0, 0, 0, 0);
-      if (ii < L0.range) batch = item_desc(g, lv, L0, cta, slot_of, ii);
-      else batch = ready ? down_desc(ii - L0.range) : make_int4(kPending, 0, 0, 0);
-    }
-    const int src = (j0 & 31) + (lane & 1);
-    int4 it;
-    it.x = __shfl_sync(0xffffffffu, batch.x, src);
-    it.y = __shfl_sync(0xffffffffu, batch.y, src);
-    it.z = __shfl_sync(0xffffffffu, batch.z, src);
-    it.w = __shfl_sync(0xffffffffu, batch.w, src);
-    const int j = j0 + lane;
-    if (issuer && j < nw) {
-      const int i = pr + kProducers * j;
-      if ((it.x & 15) == kPending) it = wait_plan() ? down_desc(i - L0.range) : make_int4(0, 0, 0, 0);
-      const int st = i % ns, round = i / ns;
-      const uint32_t full = bars + st * 8, empty = bars + (ns + st) * 8;
-      if (round > 0) mbar_wait(empty, (unsigned)(round - 1) & 1u, p.err);
-      st_volatile_shared(tags + st, i);
-      const int kind = it.x & 15;
-      if (!aligned || kind == 0) {
-        mbar_arrive(full);
-      } else {
-        const uint32_t dst = smem_u32(stages + (size_t)st * kKsStageBytes);
-        if (kind == 1) {
-          mbar_arrive_tx(full, (unsigned)(kScaleOff + 256 + (hz ? 64 : 0)));
-          const int zx = (8 * it.z) & ~15;
-          tma_load_4d(dst, &p.tm[0], it.z * 32, 0, 16 * it.w, it.y, full, pol);
-          tma_load_4d(dst + kScaleOff, &p.tm[1], it.z * 32, 0, 2 * it.w, it.y, full, pol);
-          if (hz) tma_load_4d(dst + kZeroOff, &p.tm[2], zx, 0, 2 * it.w, it.y, full, pol);
-        } else {                                              // kind 3: K-split down item
-          const int nb = (it.x >> 4) & 15, ng = (it.x >> 8) & 3, w0 = it.w, cb = it.z;
-          mbar_arrive_tx(full, (unsigned)(2 * nb * kKsCols * 4 + ng * kKsCols * 2 + (hz ? ng * kKsCols / 4 : 0)));
-          tma_load_3d(dst, &p.tmk[nb - 1], cb * kKsCols, w0, it.y, full, pol);
-          tma_load_3d(dst + kKsScaleOff, &p.tmk[4 + ng - 1], cb * kKsCols, w0 >> 3, it.y, full, pol);
-          if (hz) tma_load_3d(dst + kKsZeroOff, &p.tmk[6 + ng - 1], cb * (kKsCols / 4), w0 >> 3, it.y, full, pol);
-        }
-      }
-    }
-    __syncwarp();
-  }
-  if (issuer)
-    for (int s0 = pr + kProducers * lane; s0 < ns && s0 < n; s0 += kIssuers) {
-      const int last = s0 + ((n - 1 - s0) / ns) * ns;
-      mbar_wait(bars + s0 * 8, (unsigned)(last / ns) & 1u, p.err);
-    }
 }
 
 // 4 columns x 1 group of this lane from a ring stage. Gate_up stages hold 256-byte word rows (32 gate |
@@ -1206,13 +1114,24 @@ __device__ void ks_reduce(const FusedParams& p, const LiveRows& lv, int cta, int
       const int b0 = r0 * g.nb1, b1 = (r0 + cnt) * g.nb1;
       const int c0 = range_owner(lv.n1, lv.grid1, b0 * g.kp1);
       const int c1 = range_owner(lv.n1, lv.grid1, (b1 - 1) * g.kp1);
-      for (int c = c0 + warp; c <= c1; c += kWarps) {
-        // token m is segment 0 of CTA c when it is the token of c's first owned block
-        const int ac = c * q + min(c, rem);
-        const int bsc = (ac + g.kp1 - 1) / g.kp1;
-        const int mc = fdiv(lv.rowmap[fdiv(bsc, g.d_nb1)], g.d_topk);
-        acc += __ldcg(p.part + ((size_t)c * p.ks_segs + (m == mc ? 0 : 1)) * g.H + ch * 32 + lane);
+      constexpr int kPer = (kKsMaxGrid + kWarps - 1) / kWarps;   // partials one warp adds per column
+      float v[kPer];
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) {                        // every load issued before the first add
+        const int c = c0 + warp + i * kWarps;
+        v[i] = 0.f;
+        if (c <= c1) {
+          int seg = 0;                                          // token m is segment 0 of CTA c unless c's
+          if (p.ks_segs > 1) {                                  // first owned block belongs to an earlier token
+            const int ac = c * q + min(c, rem);
+            const int bsc = (ac + g.kp1 - 1) / g.kp1;
+            seg = fdiv(lv.rowmap[fdiv(bsc, g.d_nb1)], g.d_topk) == m ? 0 : 1;
+          }
+          v[i] = __ldcg(p.part + ((size_t)c * p.ks_segs + seg) * g.H + ch * 32 + lane);
+        }
       }
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) acc += v[i];
     }
     ks.red[warp][lane] = acc;
     csync();
@@ -1225,27 +1144,48 @@ __device__ void ks_reduce(const FusedParams& p, const LiveRows& lv, int cta, int
   }
 }
 
-// The reducing warps of K-split mode after the prologue: warp 0 writes the plan; every warp takes work
-// indices from the CTA's counter -- gate_up items of the range first (in ring order), then down units
-// (segment, 128 output columns), whose items (the runs of owned blocks) wait for their blocks' h and are
-// accumulated in registers with the rows' routing weights; then the grid barrier and the final sums.
+// The reducing warps of K-split mode after the prologue: warp 0 writes the plan and starts the down buffer's
+// bulk copies; every warp takes work indices from the CTA's counter -- gate_up items of the range first (in
+// ring order), then down units (segment, 128 output columns), which wait for their blocks' h and the down
+// buffer and accumulate the pieces' products with the rows' routing weights in registers; then the grid
+// barrier and the final sums.
 __device__ void ks_layer(const FusedParams& p, const LiveRows& lv, const WarpList& L, int cta, int warp, int lane,
                          unsigned char* smem, unsigned char* stages, uint32_t bars, int* tags, float* mail1,
                          const RowPtr* rows, unsigned* misc) {
   const Geo& g = p.geo;
   KsShared& ks = *reinterpret_cast<KsShared*>(smem + p.off_ks);
+  const unsigned char* kd = smem + p.off_kd;
+  const uint32_t kd_bar = smem_u32(&ks.kd_bar);
   const int nob = g.H / kKsCols;
   const unsigned epoch = misc[3] + 1u;
   const int range = L.range;
   const int head_k = L.a % g.kp1 ? min(g.kp1 - L.a % g.kp1, range) : 0;   // items finishing the previous CTA's block
   const int bs = range > 0 ? (L.a + g.kp1 - 1) / g.kp1 : 0;
   const int ns = p.nstage;
-  const bool sbf = p.scale_bf16 != 0, hz = p.map13.has_zeros != 0;
+  const bool sbf = p.scale_bf16 != 0, hz = p.map2.has_zeros != 0;
   if (warp == 0) {
     if (lane == 0) {
-      ks_build_plan(g, lv, cta, nob, ks.plan);
+      KsPlan& pl = ks.plan;
+      ks_build_plan(g, lv, cta, nob, hz, p.kd_bytes, pl);
+      if (!pl.ok) flag_error(p.err, 4u);
+      // the pieces' down slices: codes (contiguous word rows), scale rows, zero-point rows
+      mbar_arrive_tx(kd_bar, (unsigned)pl.kd_total);
+      for (int q = 0; q < pl.npiece && pl.ok; ++q) {
+        const int sl = rows[pl.piece_row[q]].slot;
+        const uint32_t base = smem_u32(kd);
+        bulk_g2s(base + pl.piece_code[q],
+                 p.map2.wbase + (int64_t)sl * p.map2.wstride + (int64_t)pl.piece_w0[q] * g.H * 4,
+                 (unsigned)(2 * pl.piece_nb[q] * g.H * 4), kd_bar);
+        bulk_g2s(base + pl.piece_scale[q],
+                 p.map2.sbase + (int64_t)sl * p.map2.sstride + (int64_t)pl.piece_g0[q] * g.H * 2,
+                 (unsigned)(pl.piece_ng[q] * g.H * 2), kd_bar);
+        if (hz)
+          bulk_g2s(base + pl.piece_zero[q],
+                   p.map2.zbase + (int64_t)sl * p.map2.zstride + (int64_t)pl.piece_g0[q] * (g.H / 4),
+                   (unsigned)(pl.piece_ng[q] * (g.H / 4)), kd_bar);
+      }
       __threadfence_block();
-      st_volatile_shared(&ks.plan.ready, 1);
+      st_volatile_shared(&pl.ready, 1);
     }
     __syncwarp();
   }
@@ -1256,11 +1196,7 @@ __device__ void ks_layer(const FusedParams& p, const LiveRows& lv, const WarpLis
       mbar_wait(bars + st * 8, (unsigned)(seq / ns) & 1u, p.err);
     }
     __syncwarp();
-    return static_cast<const unsigned char*>(stages + (size_t)st * kKsStageBytes);
-  };
-  auto release = [&](int seq) {
-    __syncwarp();
-    if (lane == 0) mbar_arrive(bars + (ns + seq % ns) * 8);
+    return static_cast<const unsigned char*>(stages + (size_t)st * kStageBytes);
   };
   int nunits = -1;
   while (true) {
@@ -1279,14 +1215,15 @@ __device__ void ks_layer(const FusedParams& p, const LiveRows& lv, const WarpLis
       w.slot = t;
       const ItemRegs none{};
       process_work<true, 1>(p, w, lane, none, take(t), smem, mail1, nullptr, rows);
-      release(t);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bars + (ns + t % ns) * 8);
       if (t < head_k) head_item_done(p, lv, L, cta, lane, mail1, head_k, epoch, misc + 2);
       const int gb = fdiv(i, g.d_kp1);
       if (gb >= bs) {
         const int j = gb - bs;
         const int need = min(L.b, (gb + 1) * g.kp1) - gb * g.kp1;
         unsigned last = 0u;
-        if (lane == 0) {
+        if (lane == 0 && j < kKsMaxOwned) {
           __threadfence_block();
           last = atomicAdd(&ks.blk_cnt[j], 1) == need - 1;
           __threadfence_block();
@@ -1295,7 +1232,7 @@ __device__ void ks_layer(const FusedParams& p, const LiveRows& lv, const WarpLis
       }
       continue;
     }
-    if (nunits < 0) {                                         // the plan (written right after the prologue)
+    if (nunits < 0) {                                         // the plan, and the down buffer's copies
       if (lane == 0) {
         unsigned it = 0;
         while (ld_volatile_shared(&ks.plan.ready) == 0)
@@ -1304,6 +1241,7 @@ __device__ void ks_layer(const FusedParams& p, const LiveRows& lv, const WarpLis
             break;
           }
         __threadfence_block();
+        if (ld_volatile_shared(&ks.plan.ready)) mbar_wait(kd_bar, 0u, p.err);
       }
       __syncwarp();
       nunits = ld_volatile_shared(&ks.plan.ready) ? ks.plan.nunits : 0;
@@ -1312,34 +1250,32 @@ __device__ void ks_layer(const FusedParams& p, const LiveRows& lv, const WarpLis
     if (u >= nunits) break;
     const KsPlan& pl = ks.plan;
     const int seg = u / nob, cb = u - seg * nob;
-    const int nsub = pl.seg_nsub[seg];
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int tl = 0; tl < nsub; ++tl) {
-      const int sub = pl.seg_sub0[seg] + tl;
-      const int seq = range + pl.seg_base[seg] + cb * nsub + tl;
-      const int lb0 = pl.sub_lb0[sub], nb = pl.sub_nb[sub];
-      if (lane == 0) {                                        // the run's h-blocks are finished (bounded waits)
-        for (int jj = lb0; jj < lb0 + nb; ++jj) {
-          unsigned it = 0;
-          while (ld_volatile_shared(&ks.ready[jj]) == 0)
-            if (++it > kSpinLimit) {
-              flag_error(p.err, 2u);
-              break;
-            }
-        }
-        __threadfence_block();
+    const int q0 = pl.seg_p0[seg], q1 = q0 + pl.seg_np[seg];
+    if (lane == 0) {                                          // the segment's h-blocks are finished (bounded)
+      for (int jj = pl.piece_lb0[q0]; jj < pl.piece_lb0[q1 - 1] + pl.piece_nb[q1 - 1]; ++jj) {
+        unsigned it = 0;
+        while (ld_volatile_shared(&ks.ready[jj]) == 0)
+          if (++it > kSpinLimit) {
+            flag_error(p.err, 2u);
+            break;
+          }
       }
-      const unsigned char* st = take(seq);
+      __threadfence_block();
+    }
+    __syncwarp();
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int q = q0; q < q1; ++q) {
       float v[4] = {0.f, 0.f, 0.f, 0.f};
-      ks_dot(st, ks, lb0, nb, pl.sub_w0[sub], sbf, hz, lane, v);
-      release(seq);
-      const float wr = rows[pl.sub_row[sub]].wt;
+      ks_piece_dot(kd, ks, pl, q, cb, g.H, sbf, hz, lane, v);
+      const float wr = rows[pl.piece_row[q]].wt;
 #pragma unroll
       for (int c = 0; c < 4; ++c) acc[c] += v[c] * wr;
     }
     *reinterpret_cast<float4*>(p.part + ((size_t)cta * p.ks_segs + seg) * g.H + cb * kKsCols + lane * 4) =
         make_float4(acc[0], acc[1], acc[2], acc[3]);
   }
+  if (warp == 0 && lane == 0 && nunits <= 0 && ld_volatile_shared(&ks.plan.ready))
+    mbar_wait(kd_bar, 0u, p.err);                             // no bulk copy outlives the CTA
   csync();
   if (threadIdx.x == 0) grid_barrier(p.bar_count, p.bar_gen, epoch - 1u, gridDim.x, p.err);
   csync();
@@ -1357,7 +1293,7 @@ __device__ void ks_layer(const FusedParams& p, const LiveRows& lv, const WarpLis
 template <bool kTma, bool kKs = false>
 __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_kernel(const __grid_constant__ FusedParams p) {
   static_assert(!kKs || kTma, "K-split mode streams through the copy engine");
-  constexpr size_t kStage = kKs ? kKsStageBytes : kStageBytes;
+  constexpr size_t kStage = kStageBytes;
   extern __shared__ __align__(128) unsigned char smem[];
   const Geo& g = p.geo;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1389,13 +1325,12 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
       if (pt == 32) {
         ks.next = 0;
         ks.plan.ready = 0;
+        mbar_init(smem_u32(&ks.kd_bar), 1);
       }
     }
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     if (pt < 6 && (p.map13.has_zeros || (pt != 2 && pt != 5)))
       asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&p.tm[pt])) : "memory");
-    if (kKs && pt >= 64 && pt < 72 && (p.map13.has_zeros || pt < 70))
-      asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&p.tmk[pt - 64])) : "memory");
   }
   // Launched with programmatic stream serialisation, this CTA may start while the previous kernel of the
   // stream is finishing: everything above touches only shared memory and the kernel's own parameters;
@@ -1571,19 +1506,12 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
       __syncwarp();
       const int nblk = __popc(bal) * g.nb1;
       const LiveRows plv{prow, ptokrow, ptokcnt, nullptr, nblk * g.kp1, max(1, min((int)gridDim.x, nblk))};
-      if constexpr (kKs)
-        produce_ks(p, plv, [&](int r, int) { return pslot[r]; }, cta, stages, bars, tags, pw, lane,
-                   reinterpret_cast<const KsShared*>(smem + p.off_ks));
-      else
-        produce(p, plv, [&](int r, int) { return pslot[r]; }, cta, stages, bars, tags, pw, lane);
+      produce<kKs>(p, plv, [&](int r, int) { return pslot[r]; }, cta, stages, bars, tags, pw, lane);
     } else {
       bar_wait(2, 32 * (kProducers + 1));                     // routing compacted by warp 0
       const LiveRows lv{rowmap, tokrow, tokcnt, slotrow, (int)misc[4], (int)misc[5]};
       auto slot_of = [&](int r, int kind) { const RowPtr& rp = rows[r]; return rp.ok[kind - 1] ? rp.slot : -1; };
-      if constexpr (kKs)
-        produce_ks(p, lv, slot_of, cta, stages, bars, tags, pw, lane, reinterpret_cast<const KsShared*>(smem + p.off_ks));
-      else
-        produce(p, lv, slot_of, cta, stages, bars, tags, pw, lane);
+      produce<kKs>(p, lv, slot_of, cta, stages, bars, tags, pw, lane);
     }
     return;
    }
@@ -1717,11 +1645,22 @@ SmemPlan smem_plan_mode(const Geo& g, bool ks) {
   }
   return s;
 }
-TmaPlan tma_plan(const Geo& g, bool ks = false) {
+// K-split mode's down buffer: the largest set of pieces one CTA can own -- codes of every owned block, and the
+// scale and zero-point rows of at most owned / 4 + 3 (piece, group) pairs (each piece adds one group, and every
+// fourth block another).
+size_t ks_down_bytes(const Geo& g, bool hz) {
+  const int owned = (g.max_range + g.kp1 - 1) / g.kp1;
+  const int pairs = owned + 1 < owned / 4 + 3 ? owned + 1 : owned / 4 + 3;
+  size_t b = ((size_t)2 * owned * g.H * 4 + 127) & ~size_t(127);
+  b += ((size_t)pairs * g.H * 2 + 127) & ~size_t(127);
+  if (hz) b += ((size_t)pairs * (g.H / 4) + 127) & ~size_t(127);
+  return b;
+}
+TmaPlan tma_plan(const Geo& g, bool ks = false, size_t kd = 0) {
   TmaPlan t{};
   const size_t cap = 227 * 1024;
-  const size_t sb = ks ? kKsStageBytes : kStageBytes;
-  t.rest = smem_plan_mode(g, ks).total;
+  const size_t sb = kStageBytes;
+  t.rest = smem_plan_mode(g, ks).total + kd;
   const size_t fixed = t.rest + 2 * kMaxStages * 8 + kMaxStages * 4;
   int ns = fixed < cap ? (int)((cap - fixed) / sb) : 0;
   if (ns > kMaxStages) ns = kMaxStages;
@@ -1813,52 +1752,6 @@ bool arena_maps(const LayerArgs& a, CUtensorMap (&tm)[6]) {
   return true;
 }
 
-// K-split mode's down maps over the same arena: codes with boxes of 128 columns x 2, 4, 6, 8 word rows (runs of
-// 1..4 h-blocks), scales and zero points with boxes of 128 columns x 1 or 2 group rows. Cached like the six.
-bool ks_arena_maps(const LayerArgs& a, CUtensorMap (&tmk)[8]) {
-  struct Key {
-    const void* b[3];
-    int64_t st[3];
-    int H, I, S;
-    bool operator==(const Key& o) const {
-      for (int k = 0; k < 3; ++k)
-        if (b[k] != o.b[k] || st[k] != o.st[k]) return false;
-      return H == o.H && I == o.I && S == o.S;
-    }
-  };
-  static thread_local Key last{};
-  static thread_local bool have = false;
-  static thread_local CUtensorMap cache[8];
-  const Key k{{a.map2.wbase, a.map2.sbase, a.map2.zbase}, {a.map2.wstride, a.map2.sstride, a.map2.zstride},
-              a.H, a.I, a.map2.S};
-  if (!(have && last == k)) {
-    have = false;
-    if (!tensor_map_encoder()) return false;
-    const cuuint64_t I = (cuuint64_t)a.I, H = (cuuint64_t)a.H, S = (cuuint64_t)a.map2.S;
-    const cuuint64_t dc[3] = {H, I / 16, S}, sc[2] = {H * 4, (cuuint64_t)a.map2.wstride};
-    for (int nb = 1; nb <= 4; ++nb) {
-      const cuuint32_t bc[3] = {(cuuint32_t)kKsCols, (cuuint32_t)(2 * nb), 1};
-      if (!encode_map(&cache[nb - 1], CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, a.map2.wbase, dc, sc, bc)) return false;
-    }
-    const cuuint64_t ds[3] = {H, I / kGroup, S}, ss[2] = {H * 2, (cuuint64_t)a.map2.sstride};
-    for (int ng = 1; ng <= 2; ++ng) {
-      const cuuint32_t bs[3] = {(cuuint32_t)kKsCols, (cuuint32_t)ng, 1};
-      if (!encode_map(&cache[4 + ng - 1], CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, a.map2.sbase, ds, ss, bs)) return false;
-    }
-    if (a.map2.has_zeros) {
-      const cuuint64_t dz[3] = {H / 4, I / kGroup, S}, sz[2] = {H / 4, (cuuint64_t)a.map2.zstride};
-      for (int ng = 1; ng <= 2; ++ng) {
-        const cuuint32_t bz[3] = {(cuuint32_t)(kKsCols / 4), (cuuint32_t)ng, 1};
-        if (!encode_map(&cache[6 + ng - 1], CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, a.map2.zbase, dz, sz, bz)) return false;
-      }
-    }
-    last = k;
-    have = true;
-  }
-  for (int k2 = 0; k2 < 8; ++k2) tmk[k2] = cache[k2];
-  return true;
-}
-
 // Copy-engine mode needs a slot arena, 16-byte strides in every map (H and I multiples of 64) and the
 // driver's tensor-map encoder.
 bool tma_eligible(const LayerArgs& a) {
@@ -1886,12 +1779,14 @@ int launch_fused(const LayerArgs& a, int M, const void* x, const int32_t* ids, c
   p.y = static_cast<__nv_bfloat16*>(y); p.geo = g; p.err = a.err;
   size_t base = 0, total = sp.total;
   if (tma) {
-    const TmaPlan tp = tma_plan(g, ks);
+    const size_t kd = ks ? ks_down_bytes(g, a.map2.has_zeros != 0) : 0;
+    const TmaPlan tp = tma_plan(g, ks, kd);
     if (tp.nstage == 0 || !arena_maps(a, p.tm)) return kErrShape;
-    if (ks && !ks_arena_maps(a, p.tmk)) return kErrShape;
     p.nstage = tp.nstage;
     p.off_stages = 0;
-    base = tp.stages;
+    p.off_kd = tp.stages;                                        // (128-byte aligned: the stages are)
+    p.kd_bytes = (int)kd;
+    base = tp.stages + kd;
     p.off_bars = tp.stages + tp.rest;
     total = tp.total;
   }
@@ -1944,7 +1839,7 @@ bool ks_eligible(const LayerArgs& a, int M, int grid_cap) {
   if (g.grid > kKsMaxGrid) return false;
   const int owned = (g.max_range + g.kp1 - 1) / g.kp1;        // block starts inside the longest range
   if (owned > kKsMaxOwned || owned > g.nb1 + 1) return false;
-  return tma_plan(g, true).nstage > 0;
+  return tma_plan(g, true, ks_down_bytes(g, a.map2.has_zeros != 0)).nstage > 0;
 }
 
 int decode_layer_fused(const LayerArgs& a) {
