@@ -98,14 +98,8 @@ int w2a16_moe_gemv_slots(const void* a, int64_t stride_am,
                          int top_k, int mul_routed_weight, int scale_bf16,
                          unsigned int* err, void* stream);
 
-/* Workspace bytes with which the decode-layer entry points take their fastest per-token mode for M tokens
- * (control words, and the h tables or -- at decode sizes, at most 32 routed rows -- the per-CTA partial
- * outputs of the K-split mode). */
+/* Workspace bytes the decode-layer entry points need for M tokens (h buffer + control words). */
 size_t w2a16_moe_layer_workspace_bytes(int M, int H, int I, int top_k);
-
-/* The least workspace the decode-layer entry points accept for M tokens (control words and h tables);
- * between this and w2a16_moe_layer_workspace_bytes they run without the K-split mode. */
-size_t w2a16_moe_layer_workspace_min_bytes(int M, int H, int I, int top_k);
 
 /*
  * No counterpart in the reference (its batched path is the same Triton GEMV per routed row).
@@ -189,7 +183,7 @@ int w2a16_moe_decode_layer_slots_ex(const void* x, int M, int H, int I, int top_
  * global-mode capture), or a serving process whose device memory is fully reserved by its own pool at
  * start-up. It calls no cudaMalloc, cudaFree or allocating library routine. Its workspace is a fixed
  * array of W2A16_NOALLOC_SCRATCH_BYTES (4 MiB) inside the library that every GPU loading the library
- * holds until the process exits; layers needing more (w2a16_moe_layer_workspace_min_bytes(M, H, I, top_k)
+ * holds until the process exits; layers needing more (w2a16_moe_layer_workspace_bytes(M, H, I, top_k)
  * > W2A16_NOALLOC_SCRATCH_BYTES; at I=1536, top-8 that is M > 146) return W2A16_ERR_WORKSPACE.
  * The first call in each CUDA context (once per device, and again after a device reset, which makes a
  * new context) looks up that array's device address for the calling thread's current device (which must

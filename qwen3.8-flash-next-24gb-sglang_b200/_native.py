@@ -31,7 +31,6 @@ SIGNATURES = {
     "w2a16_moe_gemv_slots": (c_i32, [c_vp, c_i64, c_vp, c_i32, c_i32, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64,
                                      c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp]),
     "w2a16_moe_layer_workspace_bytes": (c_sz, [c_i32, c_i32, c_i32, c_i32]),
-    "w2a16_moe_layer_workspace_min_bytes": (c_sz, [c_i32, c_i32, c_i32, c_i32]),
     "w2a16_moe_layer_workspace_bytes_batched": (c_sz, [c_i32, c_i32, c_i32, c_i32]),
     "w2a16_moe_decode_layer_tab": (c_i32, [c_vp, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp, c_i32,
                                            c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i32, c_f32,

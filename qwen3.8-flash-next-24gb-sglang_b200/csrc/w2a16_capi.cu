@@ -85,10 +85,6 @@ size_t w2a16_moe_layer_workspace_bytes(int M, int H, int I, int top_k) {
   return layer_workspace_bytes(M, H, I, top_k);
 }
 
-size_t w2a16_moe_layer_workspace_min_bytes(int M, int H, int I, int top_k) {
-  return layer_workspace_min_bytes(M, H, I, top_k);
-}
-
 size_t w2a16_moe_layer_workspace_bytes_batched(int M, int H, int I, int top_k) {
   const size_t a = layer_workspace_bytes(M, H, I, top_k);
   if (M < kGroupedMinTokens) return a;

@@ -41,10 +41,7 @@ struct LayerArgs {
   unsigned* err;
   cudaStream_t stream;
 };
-// Workspace of the fused layer: layer_workspace_bytes lets it take its fastest mode (the K-split mode's
-// partial outputs at decode sizes), layer_workspace_min_bytes is the least it accepts.
 size_t layer_workspace_bytes(int M, int H, int I, int top_k);
-size_t layer_workspace_min_bytes(int M, int H, int I, int top_k);
 int decode_layer_fused(const LayerArgs& a);
 // The six arena tensor maps of the fused layer's copy-engine mode (gate_up codes / scales / zeros, then
 // down); false when the arena does not qualify (no slot table, H or I not a multiple of 64, no encoder).

@@ -50,19 +50,6 @@ constexpr int kScaleOff = 4096;
 constexpr int kZeroOff = 4352;
 constexpr int kMinStages = 16, kMaxStages = 48;             // multiples of kIssuers
 
-// K-split mode (decode sizes: at most kKsMaxRows routed rows). A CTA multiplies the h-blocks it finishes by
-// the matching K-slice of its rows' down projections, so no h crosses CTAs and the down products need no
-// barrier of their own; per-CTA partial outputs are summed after one grid barrier. The down slice of a run
-// of consecutive owned blocks of one routed row ("piece") is contiguous in the arena (2 word rows per block,
-// plus the scale and zero-point rows of the groups it touches), so each piece arrives in the CTA's down
-// buffer by 2-3 bulk copies issued right after the routing, streaming alongside the gate_up ring.
-constexpr int kKsCols = 128;                                 // output columns of a down unit
-constexpr int kKsMaxOwned = 12;                              // h-blocks one CTA finishes
-constexpr int kKsMaxPiece = 2;                               // routed rows one CTA's owned blocks belong to
-constexpr int kKsMaxRows = 32;                               // routed rows of a K-split launch
-constexpr int kKsMaxGrid = 160;                              // CTAs whose partials the workspace holds
-constexpr int kKsMaxSeg = 2;                                 // tokens one CTA's owned blocks belong to
-
 constexpr unsigned kSpinLimit = 1u << 22;                    // polls before a wait gives up
 constexpr unsigned kWaitLimit = 1u << 17;                    // suspending mbarrier tries before a wait gives up
 
@@ -129,7 +116,7 @@ __host__ __device__ __forceinline__ size_t htab_bytes(int I) {
 }
 
 struct SmemPlan {
-  size_t tabs, mail1, mail2, rows, misc, live, slots, preg, ks, total;
+  size_t tabs, mail1, mail2, rows, misc, live, slots, preg, total;
 };
 constexpr int kMaxStagedSlots = 2048;                        // slot tables up to 8 KB are staged
 constexpr int kMaxPrivSlots = 512;                           // producers keep private copies up to 2 KB
@@ -152,14 +139,13 @@ struct RowPtr {
   float wt;      // routing weight
 };
 
-// ks: K-split mode (no down-unit h tables or partials; its own block s.ks, sized where KsShared is defined).
-SmemPlan smem_plan(const Geo& g, bool ks = false) {
+SmemPlan smem_plan(const Geo& g) {
   SmemPlan s{};
   const size_t t1 = (size_t)g.M * token_table_bytes(g.H);
-  const size_t t2 = ks ? 0 : (size_t)g.top_k * htab_bytes(g.I);   // one down unit's h tables at a time
+  const size_t t2 = (size_t)g.top_k * htab_bytes(g.I);         // one down unit's h tables at a time
   s.tabs = t1 > t2 ? t1 : t2;
   s.mail1 = (size_t)g.max_range * 64 * 4;
-  s.mail2 = ks ? 0 : (size_t)g.s2 * 32 * 4;
+  s.mail2 = (size_t)g.s2 * 32 * 4;
   s.rows = ((size_t)g.R * sizeof(RowPtr) + 15) & ~size_t(15);
   s.misc = 64;                                                  // mbarrier, head counter, generation
   // LiveRows arrays and the live-row bit words
@@ -174,11 +160,6 @@ struct FusedParams {
   // copy-engine mode: tensor maps over the slot arena -- gate_up codes / scales / zero points (4-D:
   // column within half, half, row, slot) and down codes / scales / zero points (3-D: column, row, slot)
   CUtensorMap tm[6];
-  size_t off_kd;         // K-split: the down buffer (kd_bytes) in shared memory
-  int kd_bytes;
-  float* part;           // K-split: [grid][ks_segs][H] fp32 partial outputs
-  int ks_segs;           // K-split: segments per CTA the partial buffer holds (min(M, kKsMaxSeg))
-  size_t off_ks;
   int nstage;
   size_t off_stages, off_bars;
   const __nv_bfloat16* x;
@@ -603,13 +584,12 @@ __device__ __forceinline__ int4 item_desc(const Geo& g, const LiveRows& lv, cons
 // issuer. Each item is one tensor copy of codes (4 KB), one of scales and one of zero-point windows,
 // completing on the stage's `full` barrier; a stage is refilled once the warp that reduced it arrived on
 // its `empty` barrier. Items of a non-resident expert complete their phase on the arrival alone.
-// kGateOnly (K-split mode): the ring carries the gate_up range only.
-template <bool kGateOnly, class SlotOf>
+template <class SlotOf>
 __device__ void produce(const FusedParams& p, const LiveRows& lv, SlotOf slot_of, int cta, unsigned char* stages,
                         uint32_t bars, int* tags, int pr, int lane) {
   const Geo& g = p.geo;
   const WarpList L0 = warp_list(g, lv, cta, 0);
-  const int n = kGateOnly ? L0.range : L0.range + L0.nu * g.s2;
+  const int n = L0.range + L0.nu * g.s2;
   const int nw = n > pr ? (n - pr + kProducers - 1) / kProducers : 0;   // items of this warp: pr + kProducers*j
   const int ns = p.nstage;
   const bool hz = p.map13.has_zeros != 0;
@@ -664,168 +644,6 @@ __device__ void produce(const FusedParams& p, const LiveRows& lv, SlotOf slot_of
       const int last = s0 + ((n - 1 - s0) / ns) * ns;
       mbar_wait(bars + s0 * 8, (unsigned)(last / ns) & 1u, p.err);
     }
-}
-
-// ----------------------------------------------------------------------------- K-split mode
-// The CTA's plan: the h-blocks it finishes ("owned": those whose first gate_up item lies in its range), cut
-// into pieces (runs of one routed row), the tokens ("segments") those rows belong to, and where each piece's
-// down slice lies in the down buffer: codes of all pieces first, then their scale rows, then their zero rows.
-// Down units are (segment, 128 output columns), segment-major.
-struct KsPlan {
-  int ready;                         // set once the plan is in place
-  int bs, nown;                      // first owned block (over the live rows), owned blocks
-  int nseg, npiece, nunits, ok;      // ok = 0: the plan did not fit its limits (error bit 2, no down work)
-  int seg_tok[kKsMaxSeg], seg_p0[kKsMaxSeg], seg_np[kKsMaxSeg];
-  int piece_row[kKsMaxPiece], piece_lb0[kKsMaxPiece], piece_nb[kKsMaxPiece], piece_w0[kKsMaxPiece];
-  int piece_g0[kKsMaxPiece], piece_ng[kKsMaxPiece];
-  int piece_code[kKsMaxPiece], piece_scale[kKsMaxPiece], piece_zero[kKsMaxPiece];   // byte offsets
-  int kd_total;                      // bytes of the down buffer this CTA fills
-};
-struct KsShared {
-  unsigned long long kd_bar;         // mbarrier: the down buffer's bulk copies landed
-  KsPlan plan;
-  int blk_cnt[kKsMaxOwned];          // reduced gate_up items per owned block
-  int ready[kKsMaxOwned];            // owned block's h table written
-  int next;                          // next work index of the CTA (dynamic assignment to warps)
-  alignas(16) uint32_t hpairs[kKsMaxOwned][2 * kXRegs];   // h of each owned block: fixed-point pairs, 2 word rows
-  int hm64x[kKsMaxOwned];
-  float hscl[kKsMaxOwned];
-  float red[kWarps][32];             // final reduction: one partial sum per warp and column
-};
-
-// Lane 0 of one warp: the plan of this CTA (derived from the live rows and the ranges only).
-__device__ void ks_build_plan(const Geo& g, const LiveRows& lv, int cta, int nob, bool hz, int kd_cap, KsPlan& pl) {
-  const WarpList L = warp_list(g, lv, cta, 0);
-  const int bs = L.range > 0 ? (L.a + g.kp1 - 1) / g.kp1 : 0;
-  const int be = L.range > 0 ? (L.b + g.kp1 - 1) / g.kp1 : 0;
-  pl.bs = bs;
-  pl.nown = be - bs;
-  pl.ok = pl.nown <= kKsMaxOwned;
-  pl.nseg = 0;
-  pl.npiece = 0;
-  int last_rc = -1;
-  for (int j = 0; pl.ok && j < pl.nown; ++j) {
-    const int gb = bs + j;
-    const int rc = fdiv(gb, g.d_nb1), hb = gb - rc * g.nb1;
-    if (rc != last_rc) {
-      const int r = lv.rowmap[rc], m = fdiv(r, g.d_topk);
-      if (pl.npiece == kKsMaxPiece) {
-        pl.ok = 0;
-        break;
-      }
-      if (pl.nseg == 0 || pl.seg_tok[pl.nseg - 1] != m) {
-        if (pl.nseg == kKsMaxSeg) {
-          pl.ok = 0;
-          break;
-        }
-        pl.seg_tok[pl.nseg] = m;
-        pl.seg_p0[pl.nseg] = pl.npiece;
-        pl.seg_np[pl.nseg] = 0;
-        ++pl.nseg;
-      }
-      pl.piece_row[pl.npiece] = r;
-      pl.piece_lb0[pl.npiece] = j;
-      pl.piece_nb[pl.npiece] = 1;
-      pl.piece_w0[pl.npiece] = 2 * hb;
-      ++pl.seg_np[pl.nseg - 1];
-      ++pl.npiece;
-    } else {
-      ++pl.piece_nb[pl.npiece - 1];
-    }
-    last_rc = rc;
-  }
-  int off = 0;
-  for (int q = 0; q < pl.npiece; ++q) {
-    const int w0 = pl.piece_w0[q], nb = pl.piece_nb[q];
-    pl.piece_g0[q] = w0 >> 3;
-    pl.piece_ng[q] = ((w0 + 2 * nb - 1) >> 3) - (w0 >> 3) + 1;
-    pl.piece_code[q] = off;
-    off += 2 * nb * g.H * 4;
-  }
-  for (int q = 0; q < pl.npiece; ++q) {
-    pl.piece_scale[q] = off;
-    off += pl.piece_ng[q] * g.H * 2;
-  }
-  for (int q = 0; q < pl.npiece; ++q) {
-    pl.piece_zero[q] = off;
-    if (hz) off += pl.piece_ng[q] * (g.H / 4);
-  }
-  if (off > kd_cap) pl.ok = 0;
-  pl.kd_total = pl.ok ? off : 0;
-  pl.nunits = pl.ok ? pl.nseg * nob : 0;
-}
-
-// h of an owned block (lane l holds element l) -> the CTA's fixed-point table of that block: one exponent
-// for the 32 values, pairs packed as in the activation tables (word row l / 16).
-__device__ __forceinline__ void htab_local(KsShared& ks, int j, float h, int lane) {
-  const float mx = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(h))));
-  const int e = (mx > 0.f ? frexp_exponent(mx) : 0) - 15;
-  const int q = max(-32767, min(32767, __float2int_rn(h * pow2f(-e))));
-  const int s = __reduce_add_sync(0xffffffffu, q);
-  const int hi = __shfl_xor_sync(0xffffffffu, q, 4);
-  if ((lane & 4) == 0) {
-    const int c = lane & 15, kw = lane >> 4;
-    ks.hpairs[j][kw * kXRegs + (c & 3) * 2 + (c >> 3)] = (uint32_t)(q & 0xFFFF) | ((uint32_t)hi << 16);
-  }
-  if (lane == 0) {
-    ks.hm64x[j] = -64 * s;
-    ks.hscl[j] = pow2f(e - 6);
-  }
-}
-
-// Piece q's contribution to output columns cb * 128 + 4 lane .. +3 from the down buffer: its word rows (two per
-// owned block) against the blocks' h tables, each quantization group's scales applied once its blocks are
-// summed; returns the 4 sums before the routing weight.
-__device__ __forceinline__ void ks_piece_dot(const unsigned char* kd, const KsShared& ks, const KsPlan& pl, int q,
-                                             int cb, int H, bool sbf, bool has_z, int lane, float (&v)[4]) {
-  const int nb = pl.piece_nb[q], w0 = pl.piece_w0[q], g0 = pl.piece_g0[q], lb0 = pl.piece_lb0[q];
-  const size_t rowb = (size_t)H * 4;
-  const unsigned char* code = kd + pl.piece_code[q] + (size_t)cb * (kKsCols * 4) + lane * 16;
-  const unsigned char* scl = kd + pl.piece_scale[q] + (size_t)cb * (kKsCols * 2) + lane * 8;
-  const unsigned char* zr = kd + pl.piece_zero[q] + (size_t)cb * (kKsCols / 4) + lane;
-  float f[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int j = 0; j < nb; ++j) {
-    const int wr = w0 + 2 * j, gi = (wr >> 3) - g0;
-    int acc[4][4];
-#pragma unroll
-    for (int c = 0; c < 4; ++c)
-#pragma unroll
-      for (int k = 0; k < 4; ++k) acc[c][k] = 0;
-#pragma unroll
-    for (int kk = 0; kk < 2; ++kk) {
-      const uint4 w = *reinterpret_cast<const uint4*>(code + (size_t)(2 * j + kk) * rowb);
-      const uint4* xp = reinterpret_cast<const uint4*>(&ks.hpairs[lb0 + j][kk * kXRegs]);
-      const uint4 xa = xp[0], xb = xp[1];
-      const uint32_t xr[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-      word_dot(w.x, xr, acc[0]);
-      word_dot(w.y, xr, acc[1]);
-      word_dot(w.z, xr, acc[2]);
-      word_dot(w.w, xr, acc[3]);
-    }
-    const int m64x = ks.hm64x[lb0 + j];
-    const float sx = ks.hscl[lb0 + j];
-    const uint32_t zb = has_z ? (uint32_t)zr[(size_t)gi * (H / 4)] : 0u;
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const int zp = has_z ? (int)((zb >> (2 * c)) & 3u) : 2;
-      f[c] += (float)(combine_classes(acc[c]) + zp * m64x) * sx;
-    }
-    if (j == nb - 1 || ((wr + 2) >> 3) != (wr >> 3)) {       // the group's blocks are summed: its scales
-      float sc[4];
-      scales4(*reinterpret_cast<const uint2*>(scl + (size_t)gi * (H * 2)), sbf, sc);
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        v[c] += f[c] * sc[c];
-        f[c] = 0.f;
-      }
-    }
-  }
-}
-
-// Item i of a range of n1 items cut into grid1 ranges (the first n1 % grid1 one item longer) -> its CTA.
-__device__ __forceinline__ int range_owner(int n1, int grid1, int i) {
-  const int q = n1 / grid1, rem = n1 - q * grid1;
-  return i < rem * (q + 1) ? i / (q + 1) : rem + (i - rem * (q + 1)) / q;
 }
 
 // 4 columns x 1 group of this lane from a ring stage. Gate_up stages hold 256-byte word rows (32 gate |
@@ -1057,243 +875,10 @@ __device__ __forceinline__ void unit_tables(const FusedParams& p, const LiveRows
   csync();
 }
 
-// ----------------------------------------------------------------------------- K-split mode, reducing warps
-// Owned block gb (local index j) after its last local gate_up item: (gate, up) sums of its items in item order,
-// plus the tail sums the next CTA published when the block runs into it (bounded wait on the epoch tag), h =
-// silu(gate) * up into the CTA's h tables, then the block's ready flag.
-__device__ void ks_finish_block(const FusedParams& p, const WarpList& L, int cta, int lane, const float* mail1,
-                                KsShared& ks, int gb, int j, int need, unsigned epoch) {
-  const Geo& g = p.geo;
-  const int t0 = gb * g.kp1 - L.a;
-  float gs = 0.f, us = 0.f;
-  for (int i = 0; i < need; ++i) {
-    gs += mail1[(size_t)(t0 + i) * 64 + lane];
-    us += mail1[(size_t)(t0 + i) * 64 + 32 + lane];
-  }
-  if ((gb + 1) * g.kp1 > L.b) {
-    const unsigned long long* slot = p.hand + (size_t)(cta + 1) * 64;
-    unsigned long long vg = 0, vu = 0;
-    unsigned it = 0;
-    while (true) {
-      vg = ld_relaxed_u64(slot + lane);
-      vu = ld_relaxed_u64(slot + 32 + lane);
-      if ((unsigned)(vg >> 32) == epoch && (unsigned)(vu >> 32) == epoch) break;
-      if (++it > kSpinLimit) {
-        flag_error(p.err, 2u);
-        break;
-      }
-      __nanosleep(32);
-    }
-    __syncwarp();
-    gs += __uint_as_float((unsigned)vg);
-    us += __uint_as_float((unsigned)vu);
-  }
-  htab_local(ks, j, silu(gs) * us, lane);
-  __syncwarp();
-  if (lane == 0) {
-    __threadfence_block();
-    st_volatile_shared(&ks.ready[j], 1);
-  }
-}
-
-// After the grid barrier: y[m, 32 columns] of unit (token m, column chunk) = routed_scaling * the sum of the
-// partials of the CTAs owning token m's blocks (warp w takes CTAs c0 + w, c0 + w + 16, ...; the warps' sums
-// are added in warp order: a fixed order, so results are reproducible).
-__device__ void ks_reduce(const FusedParams& p, const LiveRows& lv, int cta, int warp, int lane, KsShared& ks) {
-  const Geo& g = p.geo;
-  const int nch = g.H / 32;
-  const int units = g.M * nch;
-  const int q = lv.grid1 > 0 ? lv.n1 / lv.grid1 : 0, rem = lv.n1 - q * lv.grid1;
-  for (int uu = cta; uu < units; uu += gridDim.x) {
-    const int m = uu / nch, ch = uu - m * nch;
-    int r0 = 0;
-    for (int mm = 0; mm < m; ++mm) r0 += lv.tokcnt[mm];
-    const int cnt = lv.tokcnt[m];
-    float acc = 0.f;
-    if (cnt > 0) {
-      const int b0 = r0 * g.nb1, b1 = (r0 + cnt) * g.nb1;
-      const int c0 = range_owner(lv.n1, lv.grid1, b0 * g.kp1);
-      const int c1 = range_owner(lv.n1, lv.grid1, (b1 - 1) * g.kp1);
-      constexpr int kPer = (kKsMaxGrid + kWarps - 1) / kWarps;   // partials one warp adds per column
-      float v[kPer];
-#pragma unroll
-      for (int i = 0; i < kPer; ++i) {                        // every load issued before the first add
-        const int c = c0 + warp + i * kWarps;
-        v[i] = 0.f;
-        if (c <= c1) {
-          int seg = 0;                                          // token m is segment 0 of CTA c unless c's
-          if (p.ks_segs > 1) {                                  // first owned block belongs to an earlier token
-            const int ac = c * q + min(c, rem);
-            const int bsc = (ac + g.kp1 - 1) / g.kp1;
-            seg = fdiv(lv.rowmap[fdiv(bsc, g.d_nb1)], g.d_topk) == m ? 0 : 1;
-          }
-          v[i] = __ldcg(p.part + ((size_t)c * p.ks_segs + seg) * g.H + ch * 32 + lane);
-        }
-      }
-#pragma unroll
-      for (int i = 0; i < kPer; ++i) acc += v[i];
-    }
-    ks.red[warp][lane] = acc;
-    csync();
-    if (warp == 0) {
-      float sum = 0.f;
-      for (int w = 0; w < kWarps; ++w) sum += ks.red[w][lane];
-      p.y[(int64_t)m * g.H + ch * 32 + lane] = __float2bfloat16(sum * p.rsf);
-    }
-    csync();
-  }
-}
-
-// The reducing warps of K-split mode after the prologue: warp 0 writes the plan and starts the down buffer's
-// bulk copies; every warp takes work indices from the CTA's counter -- gate_up items of the range first (in
-// ring order), then down units (segment, 128 output columns), which wait for their blocks' h and the down
-// buffer and accumulate the pieces' products with the rows' routing weights in registers; then the grid
-// barrier and the final sums.
-__device__ void ks_layer(const FusedParams& p, const LiveRows& lv, const WarpList& L, int cta, int warp, int lane,
-                         unsigned char* smem, unsigned char* stages, uint32_t bars, int* tags, float* mail1,
-                         const RowPtr* rows, unsigned* misc) {
-  const Geo& g = p.geo;
-  KsShared& ks = *reinterpret_cast<KsShared*>(smem + p.off_ks);
-  const unsigned char* kd = smem + p.off_kd;
-  const uint32_t kd_bar = smem_u32(&ks.kd_bar);
-  const int nob = g.H / kKsCols;
-  const unsigned epoch = misc[3] + 1u;
-  const int range = L.range;
-  const int head_k = L.a % g.kp1 ? min(g.kp1 - L.a % g.kp1, range) : 0;   // items finishing the previous CTA's block
-  const int bs = range > 0 ? (L.a + g.kp1 - 1) / g.kp1 : 0;
-  const int ns = p.nstage;
-  const bool sbf = p.scale_bf16 != 0, hz = p.map2.has_zeros != 0;
-  if (warp == 0) {
-    if (lane == 0) {
-      KsPlan& pl = ks.plan;
-      ks_build_plan(g, lv, cta, nob, hz, p.kd_bytes, pl);
-      if (!pl.ok) flag_error(p.err, 4u);
-      // the pieces' down slices: codes (contiguous word rows), scale rows, zero-point rows
-      mbar_arrive_tx(kd_bar, (unsigned)pl.kd_total);
-      for (int q = 0; q < pl.npiece && pl.ok; ++q) {
-        const int sl = rows[pl.piece_row[q]].slot;
-        const uint32_t base = smem_u32(kd);
-        bulk_g2s(base + pl.piece_code[q],
-                 p.map2.wbase + (int64_t)sl * p.map2.wstride + (int64_t)pl.piece_w0[q] * g.H * 4,
-                 (unsigned)(2 * pl.piece_nb[q] * g.H * 4), kd_bar);
-        bulk_g2s(base + pl.piece_scale[q],
-                 p.map2.sbase + (int64_t)sl * p.map2.sstride + (int64_t)pl.piece_g0[q] * g.H * 2,
-                 (unsigned)(pl.piece_ng[q] * g.H * 2), kd_bar);
-        if (hz)
-          bulk_g2s(base + pl.piece_zero[q],
-                   p.map2.zbase + (int64_t)sl * p.map2.zstride + (int64_t)pl.piece_g0[q] * (g.H / 4),
-                   (unsigned)(pl.piece_ng[q] * (g.H / 4)), kd_bar);
-      }
-      __threadfence_block();
-      st_volatile_shared(&pl.ready, 1);
-    }
-    __syncwarp();
-  }
-  auto take = [&](int seq) {                                  // the item's stage, once its copies landed
-    const int st = seq % ns;
-    if (lane == 0) {
-      wait_tag(tags, st, seq, p.err);
-      mbar_wait(bars + st * 8, (unsigned)(seq / ns) & 1u, p.err);
-    }
-    __syncwarp();
-    return static_cast<const unsigned char*>(stages + (size_t)st * kStageBytes);
-  };
-  int nunits = -1;
-  while (true) {
-    int t = 0;
-    if (lane == 0) t = atomicAdd(&ks.next, 1);
-    t = __shfl_sync(0xffffffffu, t, 0);
-    if (t < range) {
-      const int i = L.a + t;
-      Work w{};
-      w.kind = 1;
-      const int rc = fdiv(i, g.d_row1);
-      w.r = lv.rowmap[rc];
-      const int rem = i - rc * (g.nb1 * g.kp1);
-      w.b = fdiv(rem, g.d_kp1);
-      w.kp = rem - w.b * g.kp1;
-      w.slot = t;
-      const ItemRegs none{};
-      process_work<true, 1>(p, w, lane, none, take(t), smem, mail1, nullptr, rows);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bars + (ns + t % ns) * 8);
-      if (t < head_k) head_item_done(p, lv, L, cta, lane, mail1, head_k, epoch, misc + 2);
-      const int gb = fdiv(i, g.d_kp1);
-      if (gb >= bs) {
-        const int j = gb - bs;
-        const int need = min(L.b, (gb + 1) * g.kp1) - gb * g.kp1;
-        unsigned last = 0u;
-        if (lane == 0 && j < kKsMaxOwned) {
-          __threadfence_block();
-          last = atomicAdd(&ks.blk_cnt[j], 1) == need - 1;
-          __threadfence_block();
-        }
-        if (__shfl_sync(0xffffffffu, last, 0)) ks_finish_block(p, L, cta, lane, mail1, ks, gb, j, need, epoch);
-      }
-      continue;
-    }
-    if (nunits < 0) {                                         // the plan, and the down buffer's copies
-      if (lane == 0) {
-        unsigned it = 0;
-        while (ld_volatile_shared(&ks.plan.ready) == 0)
-          if (++it > kSpinLimit) {
-            flag_error(p.err, 2u);
-            break;
-          }
-        __threadfence_block();
-        if (ld_volatile_shared(&ks.plan.ready)) mbar_wait(kd_bar, 0u, p.err);
-      }
-      __syncwarp();
-      nunits = ld_volatile_shared(&ks.plan.ready) ? ks.plan.nunits : 0;
-    }
-    const int u = t - range;
-    if (u >= nunits) break;
-    const KsPlan& pl = ks.plan;
-    const int seg = u / nob, cb = u - seg * nob;
-    const int q0 = pl.seg_p0[seg], q1 = q0 + pl.seg_np[seg];
-    if (lane == 0) {                                          // the segment's h-blocks are finished (bounded)
-      for (int jj = pl.piece_lb0[q0]; jj < pl.piece_lb0[q1 - 1] + pl.piece_nb[q1 - 1]; ++jj) {
-        unsigned it = 0;
-        while (ld_volatile_shared(&ks.ready[jj]) == 0)
-          if (++it > kSpinLimit) {
-            flag_error(p.err, 2u);
-            break;
-          }
-      }
-      __threadfence_block();
-    }
-    __syncwarp();
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int q = q0; q < q1; ++q) {
-      float v[4] = {0.f, 0.f, 0.f, 0.f};
-      ks_piece_dot(kd, ks, pl, q, cb, g.H, sbf, hz, lane, v);
-      const float wr = rows[pl.piece_row[q]].wt;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) acc[c] += v[c] * wr;
-    }
-    *reinterpret_cast<float4*>(p.part + ((size_t)cta * p.ks_segs + seg) * g.H + cb * kKsCols + lane * 4) =
-        make_float4(acc[0], acc[1], acc[2], acc[3]);
-  }
-  if (warp == 0 && lane == 0 && nunits <= 0 && ld_volatile_shared(&ks.plan.ready))
-    mbar_wait(kd_bar, 0u, p.err);                             // no bulk copy outlives the CTA
-  csync();
-  if (threadIdx.x == 0) grid_barrier(p.bar_count, p.bar_gen, epoch - 1u, gridDim.x, p.err);
-  csync();
-  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
-  ks_reduce(p, lv, cta, warp, lane, ks);
-}
-
 // kTma = false: register mode (any expert map), 512 threads; every lane loads its item data itself.
-// kTma = true: copy-engine mode (slot arenas), 512 reducing threads + 4 producer warps.
-// kKs = true (copy-engine mode only): K-split down projection -- the reducing warps take the CTA's work
-// (gate_up items, then (token, 128 output columns) down units) from a shared counter; the warp that reduces
-// the last item of an owned h-block finishes it into the CTA's h tables; down units accumulate the owned
-// blocks' products in registers and store the CTA's partial outputs; after the grid barrier the CTAs sum the
-// partials of each token in CTA order (deterministic) into y.
-template <bool kTma, bool kKs = false>
+// kTma = true: copy-engine mode (slot arenas), 512 reducing threads + one producer warp.
+template <bool kTma>
 __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_kernel(const __grid_constant__ FusedParams p) {
-  static_assert(!kKs || kTma, "K-split mode streams through the copy engine");
-  constexpr size_t kStage = kStageBytes;
   extern __shared__ __align__(128) unsigned char smem[];
   const Geo& g = p.geo;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1316,18 +901,6 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
       if (b < p.nstage) tags[b] = -1;
     }
     if (pt == 0) mbar_init(hbar, 1);                          // the h-table copies' barrier
-    if constexpr (kKs) {                                      // work counter, block counts and flags, plan flag
-      KsShared& ks = *reinterpret_cast<KsShared*>(smem + p.off_ks);
-      if (pt < kKsMaxOwned) {
-        ks.blk_cnt[pt] = 0;
-        ks.ready[pt] = 0;
-      }
-      if (pt == 32) {
-        ks.next = 0;
-        ks.plan.ready = 0;
-        mbar_init(smem_u32(&ks.kd_bar), 1);
-      }
-    }
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     if (pt < 6 && (p.map13.has_zeros || (pt != 2 && pt != 5)))
       asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&p.tm[pt])) : "memory");
@@ -1506,12 +1079,12 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
       __syncwarp();
       const int nblk = __popc(bal) * g.nb1;
       const LiveRows plv{prow, ptokrow, ptokcnt, nullptr, nblk * g.kp1, max(1, min((int)gridDim.x, nblk))};
-      produce<kKs>(p, plv, [&](int r, int) { return pslot[r]; }, cta, stages, bars, tags, pw, lane);
+      produce(p, plv, [&](int r, int) { return pslot[r]; }, cta, stages, bars, tags, pw, lane);
     } else {
       bar_wait(2, 32 * (kProducers + 1));                     // routing compacted by warp 0
       const LiveRows lv{rowmap, tokrow, tokcnt, slotrow, (int)misc[4], (int)misc[5]};
-      auto slot_of = [&](int r, int kind) { const RowPtr& rp = rows[r]; return rp.ok[kind - 1] ? rp.slot : -1; };
-      produce<kKs>(p, lv, slot_of, cta, stages, bars, tags, pw, lane);
+      produce(p, lv, [&](int r, int kind) { const RowPtr& rp = rows[r]; return rp.ok[kind - 1] ? rp.slot : -1; }, cta,
+              stages, bars, tags, pw, lane);
     }
     return;
    }
@@ -1520,9 +1093,6 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
   else csync();
   const LiveRows lv{rowmap, tokrow, tokcnt, slotrow, (int)misc[4], (int)misc[5]};
   const WarpList L = warp_list(g, lv, cta, warp);
-  if constexpr (kKs) {
-    ks_layer(p, lv, L, cta, warp, lane, smem, stages, bars, tags, mail1, rows, misc);
-  } else {
   for (int idx = threadIdx.x; idx < g.max_units * g.top_k; idx += kThreads) {   // rows of the CTA's down units
     const int q = fdiv(idx, g.d_topk), jr = idx - q * g.top_k, u = cta + g.grid * q;
     int row = -1;
@@ -1563,7 +1133,7 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
         mbar_wait(bars + st * 8, (unsigned)(w.seq / p.nstage) & 1u, p.err);
       }
       __syncwarp();
-      process_work<true, K>(p, w, lane, cur, stages + (size_t)st * kStage, smem, mail1, mail2, rows);
+      process_work<true, K>(p, w, lane, cur, stages + (size_t)st * kStageBytes, smem, mail1, mail2, rows);
       __syncwarp();
       if (lane == 0) mbar_arrive(bars + (p.nstage + st) * 8);
       if constexpr (K == 1)
@@ -1594,7 +1164,6 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
       p.y[(int64_t)m * g.H + b * 32 + lane] = __float2bfloat16(acc * p.rsf);
     }
   }
-  }  // (kKs == false)
 }
 
 }  // namespace
@@ -1603,28 +1172,13 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
 // only grow and are equal between calls, so zero-filling before the first call is all they need),
 // kMaxGrid x 512 bytes of hand-off words (tagged with past epochs, never reset; zero qualifies), then the
 // down tables of the routed rows [R][htab_bytes(I)] (2.25 I bytes each).
-// K-split mode puts its partial outputs after the hand-off words instead: [kKsMaxGrid][min(M, kKsMaxSeg)][H]
-// fp32. layer_workspace_bytes covers both modes (what a caller should pass); layer_workspace_min_bytes is
-// what the layer accepts (the K-split mode is then taken only when its partials fit).
 constexpr int kMaxGrid = 256;
 constexpr size_t kHandBytes = (size_t)kMaxGrid * 64 * 8;
-constexpr size_t kHeadBytes = 256 + kHandBytes;
-size_t layer_workspace_min_bytes(int M, int H, int I, int top_k) {
-  (void)H;
-  if (M <= 0 || I <= 0 || top_k <= 0) return kHeadBytes;
-  return kHeadBytes + (size_t)M * top_k * htab_bytes(I);
-}
-bool ks_shape_ok(int M, int H, int I, int top_k) {
-  return M > 0 && top_k > 0 && M * top_k <= kKsMaxRows && H % kKsCols == 0 && I % kGroup == 0;
-}
-size_t ks_workspace_bytes(int M, int H) {
-  return kHeadBytes + (size_t)kKsMaxGrid * (M < kKsMaxSeg ? M : kKsMaxSeg) * H * 4;
-}
 size_t layer_workspace_bytes(int M, int H, int I, int top_k) {
-  const size_t a = layer_workspace_min_bytes(M, H, I, top_k);
-  if (!ks_shape_ok(M, H, I, top_k)) return a;
-  const size_t b = ks_workspace_bytes(M, H);
-  return a > b ? a : b;
+  (void)H;
+  const size_t head = 256 + kHandBytes;
+  if (M <= 0 || I <= 0 || top_k <= 0) return head;
+  return head + (size_t)M * top_k * htab_bytes(I);
 }
 
 namespace {
@@ -1637,36 +1191,16 @@ struct TmaPlan {
   int nstage;
   size_t stages, rest, total;
 };
-SmemPlan smem_plan_mode(const Geo& g, bool ks) {
-  SmemPlan s = smem_plan(g, ks);
-  if (ks) {
-    s.ks = (sizeof(KsShared) + 15) & ~size_t(15);
-    s.total += s.ks;
-  }
-  return s;
-}
-// K-split mode's down buffer: the largest set of pieces one CTA can own -- codes of every owned block, and the
-// scale and zero-point rows of at most owned / 4 + 3 (piece, group) pairs (each piece adds one group, and every
-// fourth block another).
-size_t ks_down_bytes(const Geo& g, bool hz) {
-  const int owned = (g.max_range + g.kp1 - 1) / g.kp1;
-  const int pairs = owned + 1 < owned / 4 + 3 ? owned + 1 : owned / 4 + 3;
-  size_t b = ((size_t)2 * owned * g.H * 4 + 127) & ~size_t(127);
-  b += ((size_t)pairs * g.H * 2 + 127) & ~size_t(127);
-  if (hz) b += ((size_t)pairs * (g.H / 4) + 127) & ~size_t(127);
-  return b;
-}
-TmaPlan tma_plan(const Geo& g, bool ks = false, size_t kd = 0) {
+TmaPlan tma_plan(const Geo& g) {
   TmaPlan t{};
   const size_t cap = 227 * 1024;
-  const size_t sb = kStageBytes;
-  t.rest = smem_plan_mode(g, ks).total + kd;
+  t.rest = smem_plan(g).total;
   const size_t fixed = t.rest + 2 * kMaxStages * 8 + kMaxStages * 4;
-  int ns = fixed < cap ? (int)((cap - fixed) / sb) : 0;
+  int ns = fixed < cap ? (int)((cap - fixed) / kStageBytes) : 0;
   if (ns > kMaxStages) ns = kMaxStages;
   ns -= ns % kIssuers;
   t.nstage = ns >= kMinStages ? ns : 0;
-  t.stages = (size_t)t.nstage * sb;
+  t.stages = (size_t)t.nstage * kStageBytes;
   t.total = t.stages + t.rest + 2 * (size_t)t.nstage * 8 + (size_t)t.nstage * 4;
   return t;
 }
@@ -1770,23 +1304,20 @@ Geo layer_geo(const LayerArgs& a, int M, int grid_cap) {
 }
 
 int launch_fused(const LayerArgs& a, int M, const void* x, const int32_t* ids, const float* w, void* y,
-                        int grid_cap, bool tma, bool ks) {
+                        int grid_cap, bool tma) {
   const Geo g = layer_geo(a, M, grid_cap);
-  const SmemPlan sp = smem_plan_mode(g, ks);
+  const SmemPlan sp = smem_plan(g);
   FusedParams p{};
   p.x = static_cast<const __nv_bfloat16*>(x); p.ids = ids; p.topk_w = w;
   p.map13 = a.map13; p.map2 = a.map2; p.scale_bf16 = a.scale_bf16; p.rsf = a.routed_scaling;
   p.y = static_cast<__nv_bfloat16*>(y); p.geo = g; p.err = a.err;
   size_t base = 0, total = sp.total;
   if (tma) {
-    const size_t kd = ks ? ks_down_bytes(g, a.map2.has_zeros != 0) : 0;
-    const TmaPlan tp = tma_plan(g, ks, kd);
+    const TmaPlan tp = tma_plan(g);
     if (tp.nstage == 0 || !arena_maps(a, p.tm)) return kErrShape;
     p.nstage = tp.nstage;
     p.off_stages = 0;
-    p.off_kd = tp.stages;                                        // (128-byte aligned: the stages are)
-    p.kd_bytes = (int)kd;
-    base = tp.stages + kd;
+    base = tp.stages;
     p.off_bars = tp.stages + tp.rest;
     total = tp.total;
   }
@@ -1798,16 +1329,13 @@ int launch_fused(const LayerArgs& a, int M, const void* x, const int32_t* ids, c
   p.off_live = p.off_misc + sp.misc;
   p.off_slots = p.off_live + sp.live;
   p.off_preg = p.off_slots + sp.slots;
-  p.off_ks = p.off_preg + sp.preg;
   unsigned* ctl = static_cast<unsigned*>(a.workspace);
   p.bar_count = ctl;
   p.bar_gen = ctl + 32;
   p.hand = reinterpret_cast<unsigned long long*>(static_cast<unsigned char*>(a.workspace) + 256);
-  p.htab = static_cast<unsigned char*>(a.workspace) + kHeadBytes;
-  p.part = reinterpret_cast<float*>(static_cast<unsigned char*>(a.workspace) + kHeadBytes);
-  p.ks_segs = M < kKsMaxSeg ? M : kKsMaxSeg;
+  p.htab = static_cast<unsigned char*>(a.workspace) + 256 + kHandBytes;
 
-  auto kern = ks ? fused_layer_kernel<true, true> : (tma ? fused_layer_kernel<true> : fused_layer_kernel<false>);
+  auto kern = tma ? fused_layer_kernel<true> : fused_layer_kernel<false>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)total) != cudaSuccess)
     return kErrLaunch;
   cudaLaunchConfig_t cfg{};
@@ -1829,24 +1357,11 @@ int launch_fused(const LayerArgs& a, int M, const void* x, const int32_t* ids, c
 
 bool layer_arena_maps(const LayerArgs& a, CUtensorMap (&tm)[6]) { return tma_eligible(a) && arena_maps(a, tm); }
 
-// K-split mode for this launch: slot arena in copy-engine mode, at most kKsMaxRows routed rows, a CTA finishing
-// at most kKsMaxOwned h-blocks of at most two routed rows (so of at most kKsMaxSeg tokens), a grid whose partials
-// the workspace holds, and a ring of at least kMinStages stages.
-bool ks_eligible(const LayerArgs& a, int M, int grid_cap) {
-  if (!ks_shape_ok(M, a.H, a.I, a.top_k)) return false;
-  if (a.workspace_bytes < ks_workspace_bytes(M, a.H)) return false;
-  const Geo g = layer_geo(a, M, grid_cap);
-  if (g.grid > kKsMaxGrid) return false;
-  const int owned = (g.max_range + g.kp1 - 1) / g.kp1;        // block starts inside the longest range
-  if (owned > kKsMaxOwned || owned > g.nb1 + 1) return false;
-  return tma_plan(g, true, ks_down_bytes(g, a.map2.has_zeros != 0)).nstage > 0;
-}
-
 int decode_layer_fused(const LayerArgs& a) {
   if (a.M <= 0) return kOk;
   if (a.H % kGroup != 0 || a.I % kGroup != 0 || a.top_k <= 0) return kErrShape;
   if (!a.x || !a.ids || !a.topk_w || !a.y) return kErrArg;
-  if (!a.workspace || a.workspace_bytes < layer_workspace_min_bytes(a.M, a.H, a.I, a.top_k)) return kErrWorkspace;
+  if (!a.workspace || a.workspace_bytes < layer_workspace_bytes(a.M, a.H, a.I, a.top_k)) return kErrWorkspace;
   if (reinterpret_cast<uintptr_t>(a.workspace) & 255u) return kErrAlign;
 
   static thread_local int cached_dev = -1, cached_cap = 0;
@@ -1870,10 +1385,9 @@ int decode_layer_fused(const LayerArgs& a) {
   if (!fits(mmax)) return kErrShape;
   for (int m0 = 0; m0 < a.M; m0 += mmax) {
     const int mc = a.M - m0 < mmax ? a.M - m0 : mmax;
-    const bool ks = tma && ks_eligible(a, mc, cached_cap);
     const int st = launch_fused(a, mc, static_cast<const __nv_bfloat16*>(a.x) + (size_t)m0 * a.H,
                                 a.ids + (size_t)m0 * a.top_k, a.topk_w + (size_t)m0 * a.top_k,
-                                static_cast<__nv_bfloat16*>(a.y) + (size_t)m0 * a.H, cached_cap, tma, ks);
+                                static_cast<__nv_bfloat16*>(a.y) + (size_t)m0 * a.H, cached_cap, tma);
     if (st != kOk) return st;
   }
   return kOk;

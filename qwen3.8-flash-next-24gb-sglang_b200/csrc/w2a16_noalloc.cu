@@ -74,14 +74,13 @@ extern "C" int w2a16_moe_decode_layer_slots_noalloc(
     const void* zeros2, int64_t zeros2_slot_bytes, int scale_bf16, float routed_scaling_factor, void* y,
     unsigned int* err, void* stream) {
   if (M < 0 || H <= 0 || I <= 0 || top_k <= 0) return W2A16_ERR_ARG;
-  if (w2a16::layer_workspace_min_bytes(M, H, I, top_k) > (size_t)W2A16_NOALLOC_SCRATCH_BYTES)
+  if (w2a16::layer_workspace_bytes(M, H, I, top_k) > (size_t)W2A16_NOALLOC_SCRATCH_BYTES)
     return W2A16_ERR_WORKSPACE;  // M * top_k * I too large for the fixed scratch array
   void* ws = nullptr;
   const int st = scratch_address(&ws);
   if (st != W2A16_OK) return st;
   // The same path choice as w2a16_moe_decode_layer_slots given this much workspace: per-token below
-  // W2A16_BATCHED_AUTO_TOKENS tokens (in its K-split mode when the partial outputs fit the array), batched from
-  // there on when its buffers fit the array.
+  // W2A16_BATCHED_AUTO_TOKENS tokens, batched from there on when its buffers fit the array.
   return w2a16_moe_decode_layer_slots_ex(x, M, H, I, top_k, topk_ids, topk_w, slots, num_experts, num_slots, codes13,
                                          codes13_slot_bytes, scales13, scales13_slot_bytes, zeros13,
                                          zeros13_slot_bytes, codes2, codes2_slot_bytes, scales2, scales2_slot_bytes,

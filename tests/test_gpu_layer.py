@@ -138,9 +138,7 @@ def test_config2_resident_slots_full_size(pkg, dev):
 
 
 def test_table_form_equals_slot_form(pkg, dev):
-    """apply_gemv on the reference's cached int64 tables agrees with moe_decode_layer on the arena (the slot
-    form's K-split mode adds the down products in another order, so within rounding, 2e-3 of the largest
-    output), and both agree with the oracle."""
+    """apply_gemv on the reference's cached int64 tables == moe_decode_layer on the arena, bit-exact."""
     arena, x, ids, w, y = run_case(pkg, dev, 32, 2048, 768, 2, 8, seed=6)
     wt13, st13, sw13, ss13 = pkg.make_tables(arena.codes13, arena.scales13)
     wt2, st2, sw2, ss2 = pkg.make_tables(arena.codes2, arena.scales2)
@@ -148,8 +146,7 @@ def test_table_form_equals_slot_form(pkg, dev):
     zt2, _ = pkg.make_zero_table(arena.zeros2)
     tabs = ((wt13, st13, sw13, ss13), (wt2, st2, sw2, ss2), 2 * 768, 2048, 2048, 768, False)
     y_tab = pkg.apply_gemv(x, ids, w, tabs, None, zero_tabs=(zt13, zt2))
-    assert O.max_rel_err(y_tab.float().cpu(), y.float().cpu()) < 2e-3
-    assert O.max_rel_err(y_tab.float().cpu(), oracle_layer(arena, x, ids, w)) < TOL
+    assert torch.equal(y_tab, y)
 
 
 def test_deterministic_and_graph_capturable(pkg, dev):
@@ -181,50 +178,3 @@ def test_empty_and_all_masked(pkg, dev):
     arena.slots.fill_(-1)
     y0 = pkg.moe_decode_layer(x, ids, w, arena)
     assert torch.equal(y0.cpu(), torch.zeros(1, 256, dtype=torch.bfloat16))
-
-
-def _slots_call(pkg, arena, x, ids, w, path, ws_bytes):
-    """The slot-form layer through the C ABI with an explicit path and workspace size."""
-    lib = pkg._native.lib()
-    M, H = x.shape
-    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=x.device)
-    y = torch.full_like(x, float("nan"))
-    esz = arena.scales13.element_size()
-    st = lib.w2a16_moe_decode_layer_slots_ex(
-        x.data_ptr(), M, H, arena.I, ids.shape[1], ids.data_ptr(), w.data_ptr(), arena.slots.data_ptr(), arena.E,
-        arena.S, arena.codes13.data_ptr(), arena.codes13.stride(0) * 4, arena.scales13.data_ptr(),
-        arena.scales13.stride(0) * esz, arena.zeros13.data_ptr(), arena.zeros13.stride(0), arena.codes2.data_ptr(),
-        arena.codes2.stride(0) * 4, arena.scales2.data_ptr(), arena.scales2.stride(0) * esz, arena.zeros2.data_ptr(),
-        arena.zeros2.stride(0), int(arena.scale_bf16), 1.0, y.data_ptr(), ws.data_ptr(), ws_bytes, path, None,
-        torch.cuda.current_stream().cuda_stream)
-    assert st == 0, st
-    torch.cuda.synchronize()
-    return y
-
-
-@pytest.mark.parametrize("M,E,H,I,k", [(1, 256, 4096, 1536, 8), (2, 64, 2048, 768, 8), (4, 256, 4096, 1536, 8),
-                                       (1, 8, 256, 256, 4), (3, 32, 1024, 512, 4)])
-def test_ksplit_mode_vs_unit_mode(pkg, dev, M, E, H, I, k):
-    """Decode sizes (at most 32 routed rows) run the K-split mode when the workspace holds its partial outputs
-    (w2a16_moe_layer_workspace_bytes) and the unit mode with the least workspace
-    (w2a16_moe_layer_workspace_min_bytes): both agree with the oracle and with each other, every token; no
-    bounded wait gives up; the K-split result repeats bit for bit."""
-    lib = pkg._native.lib()
-    arena = pkg.synth.make_arena(E, H, I, seed=40 + M, zeros=True, device=dev, gen_device=dev)
-    x = pkg.synth.make_activation(M, H, seed=40 + M, device=dev, gen_device=dev)
-    ids, w = pkg.synth.route_softmax(M, E, k, seed=40 + M, device=dev, gen_device=dev)
-    if M == 3:
-        arena.slots[ids[1, 0].long()] = -1                    # one masked row
-    pkg.last_device_error(dev)
-    full = int(lib.w2a16_moe_layer_workspace_bytes(M, H, I, k))
-    least = int(lib.w2a16_moe_layer_workspace_min_bytes(M, H, I, k))
-    assert full > least
-    y_ks = _slots_call(pkg, arena, x, ids, w, pkg._native.PATH_PER_TOKEN, full)
-    y_un = _slots_call(pkg, arena, x, ids, w, pkg._native.PATH_PER_TOKEN, least)
-    assert pkg.last_device_error(dev) == 0
-    ref = O.moe_layer_by_expert(arena, x, ids, w)
-    for m in range(M):
-        assert O.max_rel_err(y_ks[m:m + 1].float().cpu(), ref[m:m + 1]) < TOL, m
-        assert O.max_rel_err(y_un[m:m + 1].float().cpu(), ref[m:m + 1]) < TOL, m
-    assert O.max_rel_err(y_ks.float().cpu(), y_un.float().cpu()) < 2e-3
-    assert torch.equal(_slots_call(pkg, arena, x, ids, w, pkg._native.PATH_PER_TOKEN, full), y_ks)

@@ -76,6 +76,6 @@ def test_noalloc_entry_rejects_oversized_layers(pkg, dev):
     # memory access
     lib = pkg._native.lib()
     M = 1
-    while lib.w2a16_moe_layer_workspace_min_bytes(M, 4096, 1536, 8) <= 4 << 20:
+    while lib.w2a16_moe_layer_workspace_bytes(M, 4096, 1536, 8) <= 4 << 20:
         M += 1
     assert _call_noalloc(pkg, x, ids, w, arena, y, M=M, H=4096, I=1536) == 5
