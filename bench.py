@@ -1,29 +1,37 @@
-"""Benchmark: W2A16 g128 MoE decode layer on B200 (device-timed), with e2e, roofline, CPU baseline.
+"""Benchmark: W2A16 g128 MoE decode layers on B200 (device-timed), with e2e, roofline and a CPU baseline.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--case stack|layer|batched|int8]
 
-N=1: BASELINE config 1 — one decode MoE layer (M=1, H=4096, I=1536, E=256 resident, top-8, W2A16 g128
-with per-group zero points, f16 scales), a fresh routing and activation every step; a "step" is one
-layer. The expert set (1.29 GB) is far larger than L2 and consecutive steps share no expert within a
-window of 4 steps (more than L2 holds), so no step reads weights out of L2.
-N>1: BASELINE config 4 — expert-parallel decode step over N GPUs (see expert_parallel.py).
+Default case ("stack"), the same workload at every N: the decode step of BASELINE config 4 -- a stack of L=48
+distinct MoE layers (M=1, H=4096, I=1536, E=256 experts per layer, top-8, W2A16 g128 with per-group zero points,
+f16 scales), each layer's input the previous layer's output, a fresh routing for every layer of every step. At
+N=1 all 256 experts of every layer sit on the one GPU, so each layer is BASELINE config 1; at N>1 (one process per
+GPU under torchrun) the experts are split 1/N per rank and every layer ends with the library's peer all-reduce of
+the partial outputs over NVLink. A "step" is one pass through the L layers. `value` is the whole job's GB/s of
+algorithmic layer bytes (every routed expert's codes, scales and zero points, plus x and y) over the device time
+of the step (max over ranks). The step with config 4's INT8 dense [4096 -> 4096] projection after every layer is
+timed as well and reported under "with_dense". No expert is reused within a window of 4 layers, and all layers
+together (62 GB at N=1) are far larger than L2, so no layer reads its weights out of L2.
 
-The JSON line reports effective GB/s (algorithmic bytes streamed per second, whole job) as `value`,
-plus µs per layer, the fraction of the measured HBM peak, the dominant kernel's roofline, the CPU
-baseline (the oracle port of the reference's torch dequantise-then-matmul path, timed on the host),
-e2e through the public API with host buffers, and SM clocks sampled during the timed region.
-``--impl reference`` times the reference's CPU path alone and prints its own line.
+The JSON line also carries the dominant kernel's roofline, e2e through the public API with pinned host buffers
+(each step copies its input activation and routing in and its output back), SM clocks sampled during the timed
+region, and, on rank 0 at N=1, the CPU baseline (the oracle port of the reference's torch path). ``--impl
+reference`` times the reference's CPU path alone and prints its own line.
+
+Other cases (profiling drivers; one GPU): ``layer`` runs `--calls` config-1 layers over an arena of
+`--experts` experts (a small arena keeps an ncu capture small); ``batched`` times config 3's token counts on the
+per-token and batched paths; ``int8`` times the INT8 dense GEMV cycling 16 distinct weight matrices.
 """
 from __future__ import annotations
 
 import argparse
 import json
-import math
 import os
 import statistics
 import subprocess
 import sys
 import time
+from datetime import timedelta
 
 import torch
 
@@ -31,7 +39,10 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "W2A16 MoE layer µs & HBM GB/s (% of ~8 TB/s) at 1/2/4/8 B200 vs host-CPU torch"
-CFG1 = dict(E=256, H=4096, I=1536, top_k=8, M=1)
+SHAPE = dict(E=256, H=4096, I=1536, top_k=8, M=1)
+LAYERS = 48
+DTYPE = ("2-bit codes x 16-bit block fixed-point activations (one power-of-two exponent per 128 x values, "
+         "per 32 h values) -> exact int32 group sums -> fp32 accumulation -> bf16 output")
 
 
 def peaks():
@@ -45,7 +56,7 @@ def peaks():
 def measured_traffic(name: str):
     """DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of the named kernel, from the
     committed ncu summary profiles/<name>.json (written from one ncu capture); None when absent."""
-    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "profiles", name + ".json")
+    path = os.path.join(ROOT, "profiles", name + ".json")
     if not os.path.exists(path):
         return None
     try:
@@ -54,10 +65,19 @@ def measured_traffic(name: str):
         return None
 
 
+def layer_bytes(H: int, I: int, k: int, M: int, zeros: bool = True) -> int:
+    """Algorithmic bytes of one layer: every routed expert's gate_up and down codes, f16 scales and (with zeros)
+    zero points, plus x and y (bf16)."""
+    per = (H // 16) * 2 * I * 4 + (H // 128) * 2 * I * 2 + (I // 16) * H * 4 + (I // 128) * H * 2
+    if zeros:
+        per += (H // 128) * (2 * I // 4) + (I // 128) * (H // 4)
+    return per * k * M + 2 * M * H * 2
+
+
 # ----------------------------------------------------------------------------- routing pool
 def routing_pool(P: int, E: int, k: int, window: int, seed: int):
     """P routings (top-k of softmax(N(0,1)) renormalised), redrawn until no expert repeats within
-    `window` consecutive steps."""
+    `window` consecutive draws."""
     g = torch.Generator().manual_seed(seed)
     ids = torch.empty(P, k, dtype=torch.int32)
     ws = torch.empty(P, k, dtype=torch.float32)
@@ -90,6 +110,7 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.idx = gpu_index
         self.proc = None
+        self.lines = []
 
     def __enter__(self):
         try:
@@ -102,7 +123,6 @@ class ClockSampler:
         return self
 
     def __exit__(self, *a):
-        self.lines = []
         if self.proc is not None:
             time.sleep(0.15)
             self.proc.terminate()
@@ -132,185 +152,331 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+# ----------------------------------------------------------------------------- timing helpers
+def capture(fn, P: int):
+    """A CUDA graph of fn(0) .. fn(P-1) (warmed once on the capture stream)."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        fn(0)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g, stream=s):
+            for i in range(P):
+                fn(i)
+    torch.cuda.current_stream().wait_stream(s)
+    g.replay()
+    torch.cuda.synchronize()
+    return g
+
+
+def time_replays(g, reps: int, barrier=None):
+    """Device time (ms) of `reps` back-to-back replays, and of each replay (CUDA events on the current stream)."""
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(reps + 1)]
+    if barrier:
+        barrier()
+    torch.cuda.synchronize()
+    evs[0].record()
+    for r in range(reps):
+        g.replay()
+        evs[r + 1].record()
+    torch.cuda.synchronize()
+    each = [evs[r].elapsed_time(evs[r + 1]) for r in range(reps)]
+    return evs[0].elapsed_time(evs[reps]), each
+
+
+def pct(xs, q):
+    xs = sorted(xs)
+    return xs[min(len(xs) - 1, int(round(q * (len(xs) - 1))))]
+
+
 # ----------------------------------------------------------------------------- CPU baseline
 def cpu_baseline(arena, x, ids, w, budget_s: float):
     import oracle as O
     experts = O.routed_experts_from_arena(arena, ids)
     sec, n = O.time_cpu_layer(x.cpu(), experts, ids.cpu().reshape(1, -1), w.cpu().reshape(1, -1), budget_s)
-    info = O.cpu_info()
-    return sec, n, info
+    return sec, n, O.cpu_info()
 
 
-def layer_bytes(arena, n_experts: int, M: int, H: int) -> int:
-    return n_experts * arena.bytes_per_expert() + 2 * M * H * 2
+# ----------------------------------------------------------------------------- the layer stack, any N
+def run_stack(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    import torch.distributed as dist
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    try:
+        _run_stack(args, world, rank, dev)
+    finally:
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
 
 
-# ----------------------------------------------------------------------------- our arm, N = 1
-def run_single(args):
+def _run_stack(args, world: int, rank: int, dev: torch.device):
+    import torch.distributed as dist
     import __graft_entry__ as graft
+    import oracle as O
     pkg = graft.load_package()
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
-    E, H, I, k, M = (CFG1[n] for n in ("E", "H", "I", "top_k", "M"))
-    arena = pkg.synth.make_arena(E, H, I, seed=0, zeros=True, scale_dtype=torch.float16, device=dev)
-    P = min(args.steps, 1000)
-    ids_pool, w_pool = routing_pool(P, E, k, window=4, seed=0)
-    ids_d = ids_pool.to(dev).reshape(P, M, k)
-    w_d = w_pool.to(dev).reshape(P, M, k)
-    x_d = pkg.synth.make_activation(P, H, seed=0, device=dev).reshape(P, M, H)
-    y_d = torch.empty(P, M, H, dtype=torch.bfloat16, device=dev)
-    bps = layer_bytes(arena, k, M, H)
+    ep = pkg.expert_parallel
+    E, H, I, k, M = (SHAPE[n] for n in ("E", "H", "I", "top_k", "M"))
+    L = LAYERS
+    lo, hi = ep.expert_range(E, world, rank)
+    slots = ep.local_slot_table(E, world, rank, dev)
+    t0 = time.time()
+    arenas = []
+    for l in range(L):
+        a = pkg.synth.make_arena(hi - lo, H, I, seed=7919 * l + lo, zeros=True, scale_dtype=torch.float16,
+                                 device=dev)
+        arenas.append(pkg.ExpertArena(a.codes13, a.scales13, a.codes2, a.scales2, a.zeros13, a.zeros2, slots))
+    dense = [pkg.synth.make_int8_dense(H, H, seed=104729 + l, device=dev) for l in range(L)]
+    ar = ep.PeerAllReduce(M * H, dev) if world > 1 else None
+    P = 8                                              # steps (routings) cycled by the timed graph
+    ids_all, w_all = routing_pool(P * L, E, k, window=4, seed=0)
+    ids_d = ids_all.reshape(P, L, M, k).to(dev)
+    w_d = w_all.reshape(P, L, M, k).to(dev)
+    x_d = pkg.synth.make_activation(P * M, H, seed=0, device=dev).reshape(P, M, H)
+    bufs = [torch.empty(M, H, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    setup_s = time.time() - t0
+    barrier = (lambda: dist.barrier()) if world > 1 else None
 
-    def step(i):
-        pkg.moe_decode_layer(x_d[i], ids_d[i], w_d[i], arena, out=y_d[i])
+    def moe(x, l, i, out):
+        y = pkg.moe_decode_layer(x, ids_d[i, l], w_d[i, l], arenas[l], out=out if ar is None else None)
+        return ar(y) if ar is not None else y
+
+    def step(i, with_dense=False, x0=None):
+        x = x_d[i] if x0 is None else x0
+        for l in range(L):
+            y = moe(x, l, i, bufs[l & 1])
+            x = pkg.int8_gemv(y, dense[l][0], dense[l][1]) if with_dense else y
+        return x
+
+    # correctness of one layer of the stack: GPU output vs the fp32 oracle (partials all-reduced over ranks)
+    y0 = moe(x_d[0], 0, 0, bufs[0])
+    ref = O.moe_layer_from_arena(arenas[0], x_d[0], ids_d[0, 0], w_d[0, 0]).to(dev)
+    if world > 1:
+        dist.all_reduce(ref)
+    err = O.max_rel_err(y0.float().cpu(), ref.cpu())
 
     for i in range(max(args.warmup, 3)):
         step(i % P)
     torch.cuda.synchronize()
-
-    # capture P steps in one graph (launch overhead out of the timed region, as a serving graph does)
-    s = torch.cuda.Stream()
-    s.wait_stream(torch.cuda.current_stream())
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.stream(s):
-        step(0)
-        torch.cuda.synchronize()
-        with torch.cuda.graph(g, stream=s):
-            for i in range(P):
-                step(i)
-    torch.cuda.current_stream().wait_stream(s)
-    reps, rem = divmod(args.steps, P)
-    g_rem = None
-    if rem:
-        g_rem = torch.cuda.CUDAGraph()
-        with torch.cuda.stream(s):
-            with torch.cuda.graph(g_rem, stream=s):
-                for i in range(rem):
-                    step(i)
-        torch.cuda.current_stream().wait_stream(s)
-    g.replay()
-    torch.cuda.synchronize()
-
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    steps = max(1, args.steps)
+    reps, rem = divmod(steps, P)
+    g = capture(lambda i: step(i), P) if reps else None
+    g_rem = capture(lambda i: step(i), rem) if rem else None
     with ClockSampler(dev.index or 0) as clk:
-        torch.cuda.synchronize()
-        ev0.record()
-        for _ in range(reps):
-            g.replay()
-        if g_rem is not None:
-            g_rem.replay()
-        ev1.record()
-        torch.cuda.synchronize()
-    ms = ev0.elapsed_time(ev1)
-    us_step = ms * 1e3 / args.steps
-    gbs = bps / (us_step * 1e-6) / 1e9
-    peak, peak_kind = peaks()
+        ms, each = time_replays(g, reps, barrier) if reps else (0.0, [])
+        if g_rem is not None:                          # the last steps % P steps (exactly `steps` steps in all)
+            ms_rem, _ = time_replays(g_rem, 1, barrier)
+            ms += ms_rem
+    del g, g_rem
+    tm = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+    us_step = float(tm.item()) * 1e3 / steps
+    us_layer = us_step / L
+    per_layer = [e * 1e3 / (P * L) for e in each] or [us_layer]
 
-    # e2e: host (pinned) buffers through the public API, copies inside the timed region, eager calls
-    K_e = min(args.steps, 2000)
-    # one pinned host record per step: x (bf16) | topk ids (int32) | topk weights (fp32), moved by one copy
-    nx, ni = M * H * 2, M * k * 4
-    rec = nx + 2 * ni
-    rec_h = torch.empty(P, rec, dtype=torch.uint8).pin_memory()
-    rec_h[:, :nx] = x_d.cpu().reshape(P, -1).view(torch.uint8)
-    rec_h[:, nx:nx + ni] = ids_d.cpu().reshape(P, -1).view(torch.uint8)
-    rec_h[:, nx + ni:] = w_d.cpu().reshape(P, -1).view(torch.uint8)
-    y_h = torch.empty(P, M, H, dtype=torch.bfloat16).pin_memory()
-    rec_d = torch.empty(rec, dtype=torch.uint8, device=dev)
-    xb = rec_d[:nx].view(torch.bfloat16).view(M, H)
-    ib = rec_d[nx:nx + ni].view(torch.int32).view(M, k)
-    wb = rec_d[nx + ni:].view(torch.float32).view(M, k)
+    gd = capture(lambda i: step(i, with_dense=True), P)
+    reps_d = max(1, reps // 2)
+    msd, _ = time_replays(gd, reps_d, barrier)
+    del gd
+    tmd = torch.tensor([msd], device=dev)
+    if world > 1:
+        dist.all_reduce(tmd, op=dist.ReduceOp.MAX)
+    us_step_dense = float(tmd.item()) * 1e3 / (reps_d * P)
 
-    y_e = torch.empty(M, H, dtype=torch.bfloat16, device=dev)
+    # e2e: every step copies its input activation and its L layers' routing in from pinned host memory and its
+    # output back, around the public-API calls (a CUDA graph of P steps, as a decode loop replays graphs)
+    xh = x_d.cpu().pin_memory()
+    rh = torch.cat([ids_d.view(P, -1).view(torch.uint8).cpu(), w_d.view(P, -1).view(torch.uint8).cpu()], 1).pin_memory()
+    out_h = torch.empty(P, M, H, dtype=torch.bfloat16).pin_memory()
+    x_in = torch.empty(M, H, dtype=torch.bfloat16, device=dev)
+    r_in = torch.empty(rh.shape[1], dtype=torch.uint8, device=dev)
+    nid = ids_d[0].numel() * 4
+    ids_in = r_in[:nid].view(torch.int32).view(L, M, k)
+    w_in = r_in[nid:].view(torch.float32).view(L, M, k)
 
     def e2e_step(i):
-        rec_d.copy_(rec_h[i], non_blocking=True)
-        pkg.moe_decode_layer(xb, ib, wb, arena, out=y_e)
-        y_h[i].copy_(y_e, non_blocking=True)
+        x_in.copy_(xh[i], non_blocking=True)
+        r_in.copy_(rh[i], non_blocking=True)
+        x = x_in
+        for l in range(L):
+            y = pkg.moe_decode_layer(x, ids_in[l], w_in[l], arenas[l], out=bufs[l & 1] if ar is None else None)
+            x = ar(y) if ar is not None else y
+        out_h[i].copy_(x, non_blocking=True)
 
-    for i in range(3):
-        e2e_step(i)
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    ev0.record()
-    for i in range(K_e):
-        e2e_step(i % P)
-    ev1.record()
-    torch.cuda.synchronize()
-    e2e_ms = max(ev0.elapsed_time(ev1), (time.perf_counter() - t0) * 1e3)
-    e2e_eager_us = e2e_ms * 1e3 / K_e
-
-    # the same steps captured in a CUDA graph, as a decode loop that replays graphs runs them: every step
-    # still copies its inputs from pinned host memory, calls the public API and copies y back to the host
-    G_e = min(P, 250)
-    s_e = torch.cuda.Stream()
-    s_e.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(s_e):
-        e2e_step(0)
-        g_e = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g_e, stream=s_e):
-            for i in range(G_e):
-                e2e_step(i)
-    torch.cuda.current_stream().wait_stream(s_e)
-    g_e.replay()
-    torch.cuda.synchronize()
-    reps = max(1, K_e // G_e)
-    t0 = time.perf_counter()
-    ev0.record()
-    for _ in range(reps):
-        g_e.replay()
-    ev1.record()
-    torch.cuda.synchronize()
-    e2e_ms = max(ev0.elapsed_time(ev1), (time.perf_counter() - t0) * 1e3)
-    e2e_graph_us = e2e_ms * 1e3 / (reps * G_e)
-    del g_e
-    e2e_us = min(e2e_eager_us, e2e_graph_us)
-    e2e_how = ("CUDA graph of" if e2e_graph_us <= e2e_eager_us else "eager Python calls:") + \
-        " per step one pinned-host H2D copy of the step's x | topk ids | topk weights record, a moe_decode_layer " \
-        "call on device views of it and the D2H copy of y into pinned host memory (max of device events and host " \
-        "wall clock)"
-    h2d = rec
+    ge = capture(e2e_step, P)
+    reps_e = max(1, reps)
+    t_host = time.perf_counter()
+    mse, _ = time_replays(ge, reps_e, barrier)
+    host_ms = (time.perf_counter() - t_host) * 1e3
+    del ge
+    tme = torch.tensor([max(mse, host_ms)], device=dev)
+    if world > 1:
+        dist.all_reduce(tme, op=dist.ReduceOp.MAX)
+    e2e_us_step = float(tme.item()) * 1e3 / (reps_e * P)
+    h2d = x_in.numel() * 2 + r_in.numel()
     d2h = M * H * 2
+    ar_flag = 0
+    if ar is not None:
+        try:
+            ar.check()
+        except RuntimeError:
+            ar_flag = 1
 
-    # check the result of the timed graph once against the oracle (cheap: one layer)
-    import oracle as O
-    ref = O.moe_layer_from_arena(arena, x_d[0], ids_d[0], w_d[0])
-    err = O.max_rel_err(y_d[0].float().cpu(), ref)
-
-    sec, n_cpu, info = cpu_baseline(arena, x_d[0], ids_d[0], w_d[0], args.cpu_budget)
-    cpu_gbs = bps / sec / 1e9
-
-    launches_per_step = 1        # one cooperative fused-layer kernel per layer
-    traffic = measured_traffic("fused_layer_config1")
+    bpl = layer_bytes(H, I, k, M)
+    gbs = bpl * L / (us_step * 1e-6) / 1e9
+    peak, peak_kind = peaks()
+    if rank != 0:
+        return
+    cpu = None
+    if world == 1:
+        sec, n_cpu, info = cpu_baseline(arenas[0], x_d[0], ids_d[0, 0], w_d[0, 0], args.cpu_budget)
+        cpu = {"value": round(bpl / sec / 1e9, 3), "unit": "GB/s", "cores": info["torch_threads"], "kind": "port",
+               "us_per_layer": round(sec * 1e6, 1),
+               "sample": f"{n_cpu} layers of config 1 (8 routed experts dequantised in fp32 + matmuls, torch CPU)",
+               "cpu_model": info["cpu_model"], "cpu_count": info["cpu_count"]}
+    per_gpu = gbs / world
     line = {
-        "metric": METRIC, "value": round(gbs, 1), "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
+        "metric": METRIC, "value": round(gbs, 1), "unit": "GB/s", "n_gpus": world, "steps": steps,
         "warmup": max(args.warmup, 3), "ms_per_step": round(us_step / 1e3, 6), "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "u2xbf16->fp32 (int32 exact group sums)",
-        "data": "synthetic (seeded; BASELINE config 1 distributions)",
-        "config": {"workload": "config1: decode MoE layer M=1 H=4096 I=1536 E=256 top-8 W2A16 g128 zp",
-                   "global_batch": M, "seq_len": 1, "parallelism": "single GPU",
-                   "l2": "inputs larger than L2 (1.29 GB of experts; no expert reused within 4 steps)",
-                   "graph_steps": P},
-        "us_per_layer": round(us_step, 3), "bytes_per_layer": bps,
-        "hbm_frac": round(gbs / peak, 4), "hbm_peak_gbs": peak, "hbm_peak_kind": peak_kind,
-        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(gbs / peak, 4), "traffic": traffic,
-                     "kernel": "fused_layer_kernel (gate_up+SiLU*mul, grid barrier, down+weighted top-k sum): "
-                               "one cooperative launch per layer; achieved = algorithmic bytes / device time per layer",
+        "scaling": "strong", "vs_baseline": None, "dtype": DTYPE,
+        "data": "synthetic (seeded; BASELINE config 1 / config 4 distributions)",
+        "config": {"workload": f"config4 stack of {L} MoE layers, each config 1 (M=1 H=4096 I=1536 E=256 top-8 "
+                               f"W2A16 g128 zp f16 scales), experts {E // world} per GPU",
+                   "global_batch": M, "seq_len": 1,
+                   "parallelism": "single GPU" if world == 1 else f"ep{world} (peer-memory all-reduce per layer)",
+                   "l2": f"inputs larger than L2 ({(hi - lo) * L} local experts, {bpl * L * world // 2**20} MB of "
+                         "routed weights per step; no expert reused within 4 layers)",
+                   "layers": L, "graph_steps": P},
+        "us_per_layer": round(us_layer, 3), "us_per_layer_p50": round(pct(per_layer, 0.5), 3),
+        "us_per_layer_p99": round(pct(per_layer, 0.99), 3),
+        "percentiles_over": f"{len(per_layer)} graph replays of {P} steps x {L} layers (mean layer time per replay)",
+        "bytes_per_layer": bpl, "hbm_frac": round(per_gpu / peak, 4), "hbm_peak_gbs": peak,
+        "roofline": {"bound": "hbm", "achieved": round(per_gpu, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(per_gpu / peak, 4), "traffic": measured_traffic("fused_layer_config1"),
+                     "kernel": "fused_layer_kernel (gate_up+SiLU*mul, grid barrier, down+weighted top-k sum): one "
+                               "cooperative launch per layer; achieved = algorithmic layer bytes / device time per "
+                               "layer" + ("" if world == 1 else " / N GPUs (includes the all-reduce)"),
                      "peak_kind": peak_kind},
-        "cpu_baseline": {"value": round(cpu_gbs, 3), "unit": "GB/s", "cores": info["torch_threads"],
-                         "kind": "port", "us_per_layer": round(sec * 1e6, 1),
-                         "sample": f"{n_cpu} layers of config 1 (8 routed experts dequantised in fp32 + matmuls)",
-                         "cpu_model": info["cpu_model"], "cpu_count": info["cpu_count"]},
-        "e2e": {"value": round(bps / (e2e_us * 1e-6) / 1e9, 1), "unit": "GB/s", "us_per_layer": round(e2e_us, 2),
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "how": e2e_how, "us_per_layer_eager": round(e2e_eager_us, 2),
-                "us_per_layer_graph": round(e2e_graph_us, 2)},
-        "gpu_launches": launches_per_step * args.steps,
+        "e2e": {"value": round(bpl * L / (e2e_us_step * 1e-6) / 1e9, 1), "unit": "GB/s",
+                "us_per_layer": round(e2e_us_step / L, 3), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "how": "CUDA graph of steps, each: pinned-host H2D of x and the L layers' routing, L moe_decode_layer "
+                       "calls" + ("" if world == 1 else " + peer all-reduces") + ", D2H of the output (max of device "
+                       "events and host wall clock)"},
+        "with_dense": {"us_per_step": round(us_step_dense, 2), "us_per_layer": round(us_step_dense / L, 3),
+                       "gbs": round((bpl + (H // 4) * H * 4 + H * 2) * L / (us_step_dense * 1e-6) / 1e9, 1),
+                       "what": "config 4 step: every MoE layer followed by the INT8 dense [4096 -> 4096] GEMV "
+                               "(replicated on every rank)"},
+        "gpu_launches": steps * L * (1 if world == 1 else 2),
         "clocks": clk.summary(),
         "check_max_rel_err": err,
+        "setup_s": round(setup_s, 1),
     }
-    print(json.dumps(line))
+    if cpu:
+        line["cpu_baseline"] = cpu
+    if ar is not None:
+        line["allreduce"] = {"impl": "w2a16_allreduce_peers_bf16 (one-shot over NVLink peer memory)",
+                             "device_error": ar_flag}
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- profiling cases (one GPU)
+def run_case_layer(args):
+    """`--calls` config-1 layers over an arena of `--experts` experts (no expert reused within 4 calls), the
+    last one checked against the oracle. The command that ncu captures use."""
+    import __graft_entry__ as graft
+    import oracle as O
+    pkg = graft.load_package()
+    dev = torch.device("cuda", 0)
+    E, H, I, k, M = args.experts, SHAPE["H"], SHAPE["I"], SHAPE["top_k"], args.M
+    arena = pkg.synth.make_arena(E, H, I, seed=0, zeros=True, scale_dtype=torch.float16, device=dev)
+    ids_pool, w_pool = routing_pool(args.calls * M, E, k, window=min(4, max(1, E // (2 * k))), seed=0)
+    x = pkg.synth.make_activation(args.calls * M, H, seed=0, device=dev)
+    ids, ws = ids_pool.to(dev), w_pool.to(dev)
+    y = torch.empty(M, H, dtype=torch.bfloat16, device=dev)
+    for c in range(args.calls):
+        sl = slice(c * M, (c + 1) * M)
+        pkg.moe_decode_layer(x[sl], ids[sl], ws[sl], arena, out=y)
+    torch.cuda.synchronize()
+    sl = slice((args.calls - 1) * M, args.calls * M)
+    err = O.max_rel_err(y.float().cpu(), O.moe_layer_from_arena(arena, x[sl], ids[sl], ws[sl]))
+    print(json.dumps({"case": "layer", "experts": E, "M": M, "calls": args.calls, "max_rel_err": err}))
+    return 0 if err < 1e-2 else 1
+
+
+def run_case_batched(args):
+    """Config 3's token counts: the layer per call (CUDA-graph replay of `--calls` calls, fresh uniform routing per
+    call) on the per-token path and on the batched tensor-core path; bytes per layer count each distinct routed
+    expert once. The last call of each path is checked against the oracle."""
+    import __graft_entry__ as graft
+    import oracle as O
+    pkg = graft.load_package()
+    dev = torch.device("cuda", 0)
+    E, H, I, k = SHAPE["E"], SHAPE["H"], SHAPE["I"], SHAPE["top_k"]
+    arena = pkg.synth.make_arena(E, H, I, seed=0, zeros=True, scale_dtype=torch.float16, device=dev, gen_device=dev)
+    per_expert = arena.bytes_per_expert()
+    rc = 0
+    for M in args.tokens:
+        P = args.calls
+        x = pkg.synth.make_activation(P * M, H, seed=M, device=dev, gen_device=dev).reshape(P, M, H)
+        ids, w = pkg.synth.route_softmax(P * M, E, k, seed=M, device=dev, gen_device=dev, uniform_logits=True)
+        ids = ids.reshape(P, M, k).contiguous()
+        w = w.reshape(P, M, k).contiguous()
+        distinct = sum(int(torch.unique(ids[c]).numel()) for c in range(P)) / P
+        res = {}
+        for name, batched in (("batched", True), ("per-token", False)):
+            if batched and M < 16:
+                continue
+            y = torch.empty(P, M, H, dtype=torch.bfloat16, device=dev)
+            g = capture(lambda c: pkg.moe_decode_layer(x[c], ids[c], w[c], arena, batched=batched, out=y[c]), P)
+            times = [time_replays(g, 1)[0] * 1e3 / P for _ in range(3)]
+            us = sorted(times)[1]
+            del g
+            rel = O.max_rel_err(y[P - 1].float().cpu(), O.moe_layer_by_expert(arena, x[P - 1], ids[P - 1], w[P - 1]))
+            res[name] = us
+            rc |= 0 if rel < 1e-2 else 1
+            print(json.dumps({"case": "batched", "M": M, "path": name, "us_per_layer": round(us, 1),
+                              "distinct_experts": round(distinct, 1),
+                              "gbs_distinct": round(distinct * per_expert / us / 1e3, 1), "max_rel_err": rel}))
+    return rc
+
+
+def run_case_int8(args):
+    """The INT8 dense [4096 -> 4096] GEMV (config 2/4) over 16 distinct weight matrices cycled (269 MB > L2):
+    µs per call and GB/s of algorithmic bytes (weights + scales + x + y), CUDA-graph replay; checked once."""
+    import __graft_entry__ as graft
+    import oracle as O
+    pkg = graft.load_package()
+    dev = torch.device("cuda", 0)
+    K = N = SHAPE["H"]
+    mats = [pkg.synth.make_int8_dense(K, N, seed=3 + i, device=dev) for i in range(16)]
+    x = pkg.synth.make_activation(16, K, seed=5, device=dev)
+    ys = torch.empty(16, N, dtype=torch.bfloat16, device=dev)
+
+    def call(i):
+        q, s = mats[i % 16]
+        pkg.int8_gemv(x[i % 16:i % 16 + 1], q, s, out=ys[i % 16:i % 16 + 1])
+
+    P = 64
+    g = capture(call, P)
+    times = [time_replays(g, 1)[0] * 1e3 / P for _ in range(5)]
+    us = sorted(times)[2]
+    del g
+    q, s = mats[15]
+    ref = O.int8_gemv(x[15:16].float().cpu(), q.cpu(), s.float().cpu())
+    err = O.max_rel_err(ys[15:16].float().cpu(), ref)
+    nbytes = K * N + N * 2 + K * 2 + N * 2
+    peak, kind = peaks()
+    print(json.dumps({"case": "int8", "K": K, "N": N, "us_per_call": round(us, 3), "gbs": round(nbytes / us / 1e3, 1),
+                      "hbm_frac": round(nbytes / us / 1e3 / peak, 4), "peak_kind": kind, "max_rel_err": err,
+                      "l2": "16 distinct weight matrices cycled (269 MB > L2)"}))
+    return 0 if err < 1e-2 else 1
 
 
 # ----------------------------------------------------------------------------- reference arm
@@ -318,12 +484,9 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    import __graft_entry__ as graft
-    pkg = graft.load_package()
     import oracle as O
-    E, H, I, k, M = (CFG1[n] for n in ("E", "H", "I", "top_k", "M"))
+    E, H, I, k, M = (SHAPE[n] for n in ("E", "H", "I", "top_k", "M"))
     # only the routed experts are materialised on the host (the reference dequantises those)
-    torch.manual_seed(0)
     ids_pool, w_pool = routing_pool(max(args.steps, 1), E, k, window=4, seed=0)
     g = torch.Generator().manual_seed(0)
     experts = {}
@@ -337,8 +500,7 @@ def run_reference(args):
         z2 = torch.randint(0, 256, (I // 128, H // 4), dtype=torch.uint8, generator=gg)
         experts[e] = (c13, s13, z13, c2, s2, z2)
     x = torch.randn(1, H, generator=g).to(torch.bfloat16)
-    bps = k * (H // 16 * 2 * I * 4 + H // 128 * 2 * I * 2 + H // 128 * 2 * I // 4
-               + I // 16 * H * 4 + I // 128 * H * 2 + I // 128 * H // 4) + 2 * H * 2
+    bps = layer_bytes(H, I, k, M)
     torch.set_num_threads(os.cpu_count() or 1)
     for _ in range(max(args.warmup, 1)):
         O.moe_layer_routed_only(x, experts, ids_pool[:1], w_pool[:1])
@@ -354,7 +516,8 @@ def run_reference(args):
         "steps": n, "warmup": max(args.warmup, 1), "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
         "data": "synthetic (seeded; BASELINE config 1 distributions)",
-        "config": {"workload": "config1: decode MoE layer M=1 H=4096 I=1536 E=256 top-8 W2A16 g128 zp",
+        "config": {"workload": f"config4 stack of {LAYERS} MoE layers, each config 1 (M=1 H=4096 I=1536 E=256 "
+                               "top-8 W2A16 g128 zp f16 scales); timed per layer on the host",
                    "global_batch": 1, "seq_len": 1, "parallelism": "host CPU"},
         "us_per_layer": round(sec * 1e6, 1),
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": info["torch_threads"], "kind": "port",
@@ -368,24 +531,30 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--steps", type=int, default=40)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--case", choices=["stack", "layer", "batched", "int8"], default="stack")
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU baseline sampling")
+    ap.add_argument("--experts", type=int, default=256, help="case layer: experts in the arena")
+    ap.add_argument("--calls", type=int, default=6, help="case layer / batched: calls")
+    ap.add_argument("--M", type=int, default=1, help="case layer: tokens per call")
+    ap.add_argument("--tokens", type=int, nargs="+", default=[4, 16, 64], help="case batched: token counts")
     args = ap.parse_args()
     if args.impl == "reference":
         # bounded CPU work: each step is one layer of the reference formulation (~0.1-1 s)
         args.steps = max(1, min(args.steps, 20))
         run_reference(args)
-        return
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    if world > 1 or args.gpus > 1:
-        import __graft_entry__ as graft
-        ep = graft.load_package().expert_parallel
-        ep.bench_main(args)
-        return
-    run_single(args)
+        return 0
+    if args.case == "layer":
+        return run_case_layer(args)
+    if args.case == "batched":
+        return run_case_batched(args)
+    if args.case == "int8":
+        return run_case_int8(args)
+    run_stack(args)
+    return 0
 
 
 if __name__ == "__main__":
-    main()
+    raise SystemExit(main())

@@ -243,10 +243,12 @@ size_t w2a16_int8_workspace_bytes(int M, int K, int N);
  * mapped into this process), each holding 2 x world x n_max bf16 and, at flag_offset bytes (>= 4 world n_max,
  * 16-byte multiple), `world` uint32 flags that are zero before the first call. epoch: this rank's device call
  * counter (zero initially). Every rank must make the same sequence of calls; n <= n_max, both multiples of 8,
- * `in` 16-byte aligned. A wait that gives up sets bit 1 of `err`. */
+ * `in` 16-byte aligned. A rank waits for every other rank's flag for at most spin_limit polls (0: the
+ * library's default of 2^22, well above any healthy delay); a wait that gives up sets bit 1 of `err`, and the
+ * call then completes with whatever rows are in place, so a lost rank is reported instead of hanging the GPU. */
 int w2a16_allreduce_peers_bf16(const void* in, void* out, int n, int n_max, const uint64_t* peer_bufs,
                                size_t flag_offset, int rank, int world, unsigned int* epoch, unsigned int* err,
-                               void* stream);
+                               unsigned int spin_limit, void* stream);
 
 #ifdef __cplusplus
 }

@@ -49,7 +49,8 @@ SIGNATURES = {
                                                      c_i32, c_f32, c_vp, c_vp, c_vp]),
     "w2a16_to_word_ncontig": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_i32, c_vp]),
     "w2a16_gather_rows_tab": (c_i32, [c_vp, c_vp, c_i32, c_vp, c_i64, c_vp]),
-    "w2a16_allreduce_peers_bf16": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_vp, c_sz, c_i32, c_i32, c_vp, c_vp, c_vp]),
+    "w2a16_allreduce_peers_bf16": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_vp, c_sz, c_i32, c_i32, c_vp, c_vp, ctypes.c_uint,
+                                           c_vp]),
     "w2a16_int8_gemv": (c_i32, [c_vp, c_i64, c_vp, c_vp, c_i32, c_i32, c_i32, c_i32, c_i32, c_vp, c_i64,
                                 c_vp, c_sz, c_vp]),
     "w2a16_int8_workspace_bytes": (c_sz, [c_i32, c_i32, c_i32]),

@@ -22,7 +22,7 @@
 namespace w2a16 {
 namespace {
 
-constexpr unsigned kArSpinLimit = 1u << 22;
+constexpr unsigned kArSpinLimit = 1u << 22;                  // default polls before a flag wait gives up
 constexpr int kArThreads = 512;
 
 __device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
@@ -42,6 +42,7 @@ struct ArParams {
   size_t flag_off;
   unsigned* epoch;        // this rank's call counter
   unsigned* err;
+  unsigned spin_limit;    // polls before a flag wait gives up
 };
 
 __global__ void __launch_bounds__(kArThreads, 1) allreduce_kernel(ArParams p) {
@@ -71,7 +72,7 @@ __global__ void __launch_bounds__(kArThreads, 1) allreduce_kernel(ArParams p) {
     // rank threadIdx.x's call-e row is in place once its flag reached e: a flag already at e + 1 means that
     // rank finished call e too (it cannot reach e + 2 before this rank has read call e's slot)
     while ((int)(ld_acquire_sys(own_flags + threadIdx.x) - e) < 0) {
-      if (++it > kArSpinLimit) {
+      if (++it > p.spin_limit) {
         flag_error(p.err, 2u);
         break;
       }
@@ -90,7 +91,7 @@ __global__ void __launch_bounds__(kArThreads, 1) allreduce_kernel(ArParams p) {
 }  // namespace
 
 int allreduce_peers_bf16(const void* in, void* out, int n, int n_max, const uint64_t* bufs, size_t flag_off, int rank,
-                         int world, unsigned* epoch, unsigned* err, cudaStream_t stream) {
+                         int world, unsigned* epoch, unsigned* err, unsigned spin_limit, cudaStream_t stream) {
   if (n <= 0) return kOk;
   if (!in || !out || !bufs || !epoch || world <= 0 || world > kArThreads || rank < 0 || rank >= world)
     return kErrArg;
@@ -101,6 +102,7 @@ int allreduce_peers_bf16(const void* in, void* out, int n, int n_max, const uint
   p.out = static_cast<__nv_bfloat16*>(out);
   p.n = n; p.n_max = n_max; p.rank = rank; p.world = world;
   p.bufs = bufs; p.flag_off = flag_off; p.epoch = epoch; p.err = err;
+  p.spin_limit = spin_limit ? spin_limit : kArSpinLimit;
   allreduce_kernel<<<1, kArThreads, 0, stream>>>(p);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
 }

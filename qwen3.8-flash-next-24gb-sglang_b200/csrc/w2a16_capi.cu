@@ -174,8 +174,9 @@ size_t w2a16_int8_workspace_bytes(int M, int K, int N) { return int8_workspace_b
 
 int w2a16_allreduce_peers_bf16(const void* in, void* out, int n, int n_max, const uint64_t* peer_bufs,
                                size_t flag_offset, int rank, int world, unsigned int* epoch, unsigned int* err,
-                               void* stream) {
-  return allreduce_peers_bf16(in, out, n, n_max, peer_bufs, flag_offset, rank, world, epoch, err, as_stream(stream));
+                               unsigned int spin_limit, void* stream) {
+  return allreduce_peers_bf16(in, out, n, n_max, peer_bufs, flag_offset, rank, world, epoch, err, spin_limit,
+                              as_stream(stream));
 }
 
 int w2a16_int8_gemv(const void* x, int64_t stride_xm, const int32_t* qweight, const void* scales, int group,

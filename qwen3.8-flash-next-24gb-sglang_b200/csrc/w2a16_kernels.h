@@ -56,7 +56,7 @@ size_t grouped_workspace_bytes(int M, int H, int I, int top_k);
 int grouped_check(const LayerArgs& a);
 int decode_layer_grouped(const LayerArgs& a);
 int allreduce_peers_bf16(const void* in, void* out, int n, int n_max, const uint64_t* bufs, size_t flag_off, int rank,
-                         int world, unsigned* epoch, unsigned* err, cudaStream_t stream);
+                         int world, unsigned* epoch, unsigned* err, unsigned spin_limit, cudaStream_t stream);
 
 // INT8 dense GEMV (w2a16_int8.cu).
 struct Int8Args {

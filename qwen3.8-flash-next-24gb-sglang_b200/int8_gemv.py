@@ -12,7 +12,6 @@ import torch
 
 from . import _native
 from .expert_gemv import _stream
-from .moe_layer import layer_workspace
 
 __all__ = ["int8_gemv"]
 
@@ -28,11 +27,11 @@ def _ws(device, nbytes):
     return t
 
 
-@torch.library.custom_op("w2a16_moe::int8_gemv", mutates_args=())
-def _int8_gemv(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor, zero: int) -> torch.Tensor:
+def _int8_gemv_impl(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor, zero: int,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
     M, K = x.shape
     N = qweight.shape[1]
-    y = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    y = torch.empty((M, N), dtype=torch.bfloat16, device=x.device) if out is None else out
     if M == 0:
         return y
     group = K // scales.shape[0]
@@ -43,13 +42,20 @@ def _int8_gemv(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor, zer
     return y
 
 
+@torch.library.custom_op("w2a16_moe::int8_gemv", mutates_args=())
+def _int8_gemv(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor, zero: int) -> torch.Tensor:
+    return _int8_gemv_impl(x, qweight, scales, zero)
+
+
 @_int8_gemv.register_fake
 def _int8_gemv_fake(x, qweight, scales, zero):
     return x.new_empty((x.shape[0], qweight.shape[1]), dtype=torch.bfloat16)
 
 
-def int8_gemv(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor, zero: int = 128) -> torch.Tensor:
-    """x bf16 [M, K] (or [K]), qweight int32 [K/4, N], scales f16 [K/group, N] -> bf16 [M, N]."""
+def int8_gemv(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor, zero: int = 128,
+              out: torch.Tensor | None = None) -> torch.Tensor:
+    """x bf16 [M, K] (or [K]), qweight int32 [K/4, N], scales f16 [K/group, N] -> bf16 [M, N]. ``out`` (bf16
+    [M, N], rows contiguous, on x's device) receives the result instead of a new tensor."""
     squeeze = x.dim() == 1
     x2 = x[None] if squeeze else x
     if not (x2.is_cuda and qweight.is_cuda and scales.is_cuda):
@@ -58,5 +64,13 @@ def int8_gemv(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor, zero
         raise ValueError("int8_gemv expects x bf16, qweight int32, scales f16")
     if qweight.shape[0] * 4 != x2.shape[1]:
         raise ValueError(f"K mismatch: x {tuple(x2.shape)} vs qweight {tuple(qweight.shape)}")
-    y = _int8_gemv(x2.contiguous(), qweight.contiguous(), scales.contiguous(), int(zero))
+    if out is not None:
+        o2 = out[None] if out.dim() == 1 else out
+        if o2.shape != (x2.shape[0], qweight.shape[1]) or o2.dtype != torch.bfloat16 or o2.stride(-1) != 1 \
+                or o2.device != x2.device:
+            raise ValueError("out must be a bf16 tensor [M, N] with contiguous rows on x's device")
+        _int8_gemv_impl(x2.contiguous(), qweight.contiguous(), scales.contiguous(), int(zero), out=o2)
+        return out
+    op = _int8_gemv if torch.compiler.is_compiling() else _int8_gemv_impl
+    y = op(x2.contiguous(), qweight.contiguous(), scales.contiguous(), int(zero))
     return y[0] if squeeze else y

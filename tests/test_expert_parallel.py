@@ -87,3 +87,79 @@ def test_sum_of_rank_partials_is_the_full_layer(world):
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     rel = q.get(timeout=5)
     assert rel < 1e-5, rel
+
+
+# ----------------------------------------------------------------------------- peer all-reduce protocol model
+class _ArModel:
+    """The one-shot peer all-reduce's protocol (csrc/w2a16_allreduce.cu) as a step-by-step model: call e of a
+    rank writes its row into parity slot e & 1 of every rank's buffer, raises its flag to e on every rank, waits
+    until each of its own flags reached e, sums the rows of its own slot, and stores e as its epoch. `signed`
+    selects the kernel's wait (flag - e >= 0 as a signed distance) or an equality wait (flag == e)."""
+
+    def __init__(self, world, signed):
+        self.world, self.signed = world, signed
+        self.rows = [[[None] * world for _ in range(2)] for _ in range(world)]   # [rank][slot][row]
+        self.flags = [[0] * world for _ in range(world)]
+        self.epoch = [0] * world
+        self.results = [[] for _ in range(world)]
+        self.max_polls = [0] * world
+
+    def rank(self, r, calls, poll_limit):
+        for e in range(1, calls + 1):
+            for q in range(self.world):                     # push this call's row into every rank's slot e & 1
+                self.rows[q][e & 1][r] = (e, r)
+                yield
+            for q in range(self.world):                     # raise the flag on every rank
+                self.flags[q][r] = e
+                yield
+            for q in range(self.world):                     # wait for every rank's row (bounded)
+                polls = 0
+                while not ((self.flags[r][q] - e >= 0) if self.signed else (self.flags[r][q] == e)):
+                    polls += 1
+                    if polls > poll_limit:
+                        raise TimeoutError(f"rank {r} call {e}: flag of rank {q} is {self.flags[r][q]}")
+                    yield
+                self.max_polls[r] = max(self.max_polls[r], polls)
+            self.results[r].append(tuple(self.rows[r][e & 1]))   # the rows this rank sums
+            self.epoch[r] = e
+            yield
+
+
+def _run_model(world, calls, seed, signed, order=None, poll_limit=10_000):
+    import random
+    m = _ArModel(world, signed)
+    gens = {r: m.rank(r, calls, poll_limit) for r in range(world)}
+    rnd = random.Random(seed)
+    sched = iter(order) if order is not None else None
+    while gens:
+        r = next(sched) if sched is not None else rnd.choice(sorted(gens))
+        if r not in gens:
+            continue
+        try:
+            next(gens[r])
+        except StopIteration:
+            del gens[r]
+    return m
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_allreduce_protocol_sums_the_right_rows(world):
+    """Under random interleavings every rank sums, for every call e, exactly the rows all ranks wrote for call e
+    (a slot is never overwritten while a rank still reads it), and no wait gives up."""
+    for seed in range(20):
+        m = _run_model(world, 12, seed, signed=True)
+        for r in range(world):
+            assert m.results[r] == [tuple((e, q) for q in range(world)) for e in range(1, 13)]
+            assert m.epoch[r] == 12
+
+
+def test_allreduce_equality_wait_misses_a_flag_that_moved_on():
+    """A fast rank can finish call e and raise its flag to e + 1 before a slow rank polls it. An equality wait
+    then never sees e and gives up although the row is in place; the signed-distance wait the kernel uses
+    accepts e + 1 and sums the right rows."""
+    # rank 1 runs call 1 to its end and pushes call 2's rows and flags; only then does rank 0 start polling
+    order = [1] * 2 + [0] * 2 + [0] * 2 + [1] * 30 + [0] * 60
+    with pytest.raises(TimeoutError):
+        _run_model(2, 2, 0, signed=False, order=order + [0] * 100, poll_limit=50)
+    m = _run_model(2, 2, 0, signed=True, order=order + [0, 1] * 200, poll_limit=50)
+    assert m.results[0] == [((1, 0), (1, 1)), ((2, 0), (2, 1))]
