@@ -10,9 +10,20 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
+def _flag_off(n, world):
+    return ((n * 4 * world + 255) // 256) * 256
+
+
+def _buffer(n, world, dev):
+    """A peer buffer of the documented layout: 2 parity slots x world rows x n bf16, then `world` uint32 flags at
+    flag_off (zero)."""
+    return torch.zeros(_flag_off(n, world) + 4 * 64, dtype=torch.uint8, device=dev)
+
+
 def _call(pkg, dev, world, rank, n, buf, peers, epoch, err, spin_limit, x):
     out = torch.empty_like(x)
-    flag_off = ((n * 4 * world + 255) // 256) * 256
+    flag_off = _flag_off(n, world)
+    assert buf.numel() >= flag_off + 4 * world
     st = pkg._native.lib().w2a16_allreduce_peers_bf16(
         x.data_ptr(), out.data_ptr(), n, n, peers.data_ptr(), flag_off, rank, world, epoch.data_ptr(), err.data_ptr(),
         spin_limit, torch.cuda.current_stream(dev).cuda_stream)
@@ -22,7 +33,7 @@ def _call(pkg, dev, world, rank, n, buf, peers, epoch, err, spin_limit, x):
 
 def test_allreduce_world_one_is_identity(pkg, dev):
     n = 4096
-    buf = torch.zeros(16 << 10, dtype=torch.uint8, device=dev)
+    buf = _buffer(n, 1, dev)
     peers = torch.tensor([buf.data_ptr()], dtype=torch.int64, device=dev)
     epoch = torch.zeros(1, dtype=torch.int32, device=dev)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -36,7 +47,7 @@ def test_allreduce_world_one_is_identity(pkg, dev):
 
 def test_allreduce_wait_gives_up_when_a_rank_never_arrives(pkg, dev):
     n = 4096
-    buf = torch.zeros(64 << 10, dtype=torch.uint8, device=dev)
+    buf = _buffer(n, 2, dev)
     peers = torch.tensor([buf.data_ptr(), buf.data_ptr()], dtype=torch.int64, device=dev)   # both "ranks" here
     epoch = torch.zeros(1, dtype=torch.int32, device=dev)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -49,7 +60,7 @@ def test_allreduce_wait_gives_up_when_a_rank_never_arrives(pkg, dev):
     assert int(epoch.item()) == 1                                        # and the call completed
     # the context is usable: a world-1 call on the same stream runs and returns the identity
     err.zero_()
-    buf1 = torch.zeros(16 << 10, dtype=torch.uint8, device=dev)
+    buf1 = _buffer(n, 1, dev)
     peers1 = torch.tensor([buf1.data_ptr()], dtype=torch.int64, device=dev)
     ep1 = torch.zeros(1, dtype=torch.int32, device=dev)
     out = _call(pkg, dev, 1, 0, n, buf1, peers1, ep1, err, 0, x)
