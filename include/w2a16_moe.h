@@ -13,6 +13,7 @@
  *   4 W2A16_ERR_ARG       a required pointer is NULL or an argument is out of range
  *   5 W2A16_ERR_WORKSPACE the workspace is missing or too small
  *   6 W2A16_ERR_DEVICE    no usable sm_100 device
+ *   7 W2A16_ERR_MEMORY    no physical memory (or host memory) for another arena chunk
  *
  * Layouts (the reference's N-contiguous int32-word layout, gemv/moe_gemv_int2_tab.py:3-5):
  *   codes   int32 [K/16, N] per expert; value k of column n at bits 2*(k%16) of word k/16
@@ -45,6 +46,7 @@ extern "C" {
 #define W2A16_ERR_ARG 4
 #define W2A16_ERR_WORKSPACE 5
 #define W2A16_ERR_DEVICE 6
+#define W2A16_ERR_MEMORY 7
 
 /* Library version string, e.g. "w2a16_moe 0.1 sm_100a". */
 const char* w2a16_version(void);
@@ -249,6 +251,46 @@ size_t w2a16_int8_workspace_bytes(int M, int K, int N);
 int w2a16_allreduce_peers_bf16(const void* in, void* out, int n, int n_max, const uint64_t* peer_bufs,
                                size_t flag_offset, int rank, int world, unsigned int* epoch, unsigned int* err,
                                unsigned int spin_limit, void* stream);
+
+/*
+ * Native row arena for expert residency. Replaces RowArena (gemv/row_arena.py:34-123) and the virtual-memory
+ * plumbing it borrows from SGLang: virtual addresses for max_rows rows of row_bytes are reserved once, and a
+ * prefix of them is backed by physical memory in chunks (the device granularity rounds chunk_bytes up; 0 picks
+ * 4 MiB). Growing maps chunks after the backed prefix; shrinking unmaps every chunk that lies entirely beyond the
+ * rows kept and returns it to the driver. Row addresses (base + i * row_bytes) never change, so slot or address
+ * tables into the arena -- and CUDA graphs captured over kernels that read them -- stay valid across resizes; a
+ * table entry must only name backed rows. Not thread-safe per arena; resizes happen on the host between steps
+ * (synchronise before a shrink if kernels may still read the rows being released).
+ */
+typedef struct w2a16_arena w2a16_arena;
+int w2a16_arena_create(int device, int64_t row_bytes, int64_t max_rows, int64_t chunk_bytes, w2a16_arena** out);
+/* Back rows [0, n) (n clamped to max_rows); adds the bytes newly mapped to *mapped_bytes (may be NULL).
+ * W2A16_ERR_MEMORY when the device has no memory for another chunk (the chunks mapped so far stay). */
+int w2a16_arena_ensure_rows(w2a16_arena* arena, int64_t n, int64_t* mapped_bytes);
+/* Keep rows [0, n) backed and release every chunk entirely beyond row n; the bytes freed in *freed_bytes. */
+int w2a16_arena_shrink_rows(w2a16_arena* arena, int64_t n, int64_t* freed_bytes);
+uint64_t w2a16_arena_base(const w2a16_arena* arena);
+int64_t w2a16_arena_backed_rows(const w2a16_arena* arena);
+int64_t w2a16_arena_chunk_bytes(const w2a16_arena* arena);
+/* Unmap and release every chunk and free the reserved addresses. */
+int w2a16_arena_destroy(w2a16_arena* arena);
+
+/* The driver calls an arena makes (each returns 0 on success), so the arena's bookkeeping can be exercised
+ * against a fake: granularity of device allocations, reserve / free a virtual range, create / release a physical
+ * chunk, map a chunk at an address with read-write access for the device / unmap it. ctx is passed back. */
+typedef struct w2a16_vmm_driver {
+  void* ctx;
+  int (*granularity)(void* ctx, int device, uint64_t* bytes);
+  int (*reserve)(void* ctx, uint64_t bytes, uint64_t* base);
+  int (*free_va)(void* ctx, uint64_t base, uint64_t bytes);
+  int (*create)(void* ctx, int device, uint64_t bytes, uint64_t* handle);
+  int (*release)(void* ctx, uint64_t handle);
+  int (*map)(void* ctx, int device, uint64_t va, uint64_t bytes, uint64_t handle);
+  int (*unmap)(void* ctx, uint64_t va, uint64_t bytes);
+} w2a16_vmm_driver;
+/* w2a16_arena_create over the given driver table (w2a16_arena_create uses the CUDA driver's). */
+int w2a16_arena_create_with_driver(const w2a16_vmm_driver* driver, int device, int64_t row_bytes, int64_t max_rows,
+                                   int64_t chunk_bytes, w2a16_arena** out);
 
 #ifdef __cplusplus
 }

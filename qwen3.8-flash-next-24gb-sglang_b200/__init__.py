@@ -10,6 +10,8 @@ Public API (mirrors the reference's ``expert_gemv`` module and ``MoeWNA16Method.
 * :class:`MoeWNA16Method` / :func:`use_gemv` / :func:`fused_experts_w2a16` — the caller's 2-bit
   dispatch (patches/ncontig_gemv.py:169-255): load-time relayout, the M <= 16 / ``SGLANG_MOE_GEMV`` gate,
   and the tiled branch for larger batches;
+* :mod:`arena` — native expert arenas (reserved virtual addresses, chunks mapped on growth and released on
+  shrink; an elastic layer arena with an in-place slot table), the reference's ``RowArena`` / elastic resize;
 * :func:`int8_gemv` — the INT8 dense projection GEMV;
 * :mod:`expert_parallel` — experts split across GPUs (one process per GPU, NCCL all-reduce).
 
@@ -24,3 +26,4 @@ from .moe_method import MoeWNA16Method, use_gemv, fused_experts_w2a16  # noqa: F
 from .int8_gemv import int8_gemv  # noqa: F401
 from . import synth  # noqa: F401
 from . import expert_parallel  # noqa: F401
+from . import arena  # noqa: F401

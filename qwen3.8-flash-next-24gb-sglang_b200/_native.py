@@ -19,6 +19,7 @@ BATCHED_AUTO_TOKENS = 64
 STATUS = {
     0: "ok", 1: "unsupported shape", 2: "misaligned stride or base address", 3: "CUDA launch failed",
     4: "invalid argument", 5: "workspace missing or too small", 6: "no usable sm_100 device",
+    7: "no memory for another arena chunk",
 }
 
 # name -> (restype, argtypes); mirrors include/w2a16_moe.h one for one
@@ -54,7 +55,30 @@ SIGNATURES = {
     "w2a16_int8_gemv": (c_i32, [c_vp, c_i64, c_vp, c_vp, c_i32, c_i32, c_i32, c_i32, c_i32, c_vp, c_i64,
                                 c_vp, c_sz, c_vp]),
     "w2a16_int8_workspace_bytes": (c_sz, [c_i32, c_i32, c_i32]),
+    "w2a16_arena_create": (c_i32, [c_i32, c_i64, c_i64, c_i64, c_vp]),
+    "w2a16_arena_create_with_driver": (c_i32, [c_vp, c_i32, c_i64, c_i64, c_i64, c_vp]),
+    "w2a16_arena_ensure_rows": (c_i32, [c_vp, c_i64, c_vp]),
+    "w2a16_arena_shrink_rows": (c_i32, [c_vp, c_i64, c_vp]),
+    "w2a16_arena_base": (ctypes.c_uint64, [c_vp]),
+    "w2a16_arena_backed_rows": (c_i64, [c_vp]),
+    "w2a16_arena_chunk_bytes": (c_i64, [c_vp]),
+    "w2a16_arena_destroy": (c_i32, [c_vp]),
 }
+
+
+class VmmDriver(ctypes.Structure):
+    """w2a16_vmm_driver of include/w2a16_moe.h (a table of driver calls an arena makes)."""
+    _u64p = ctypes.POINTER(ctypes.c_uint64)
+    _fields_ = [
+        ("ctx", c_vp),
+        ("granularity", ctypes.CFUNCTYPE(c_i32, c_vp, c_i32, _u64p)),
+        ("reserve", ctypes.CFUNCTYPE(c_i32, c_vp, ctypes.c_uint64, _u64p)),
+        ("free_va", ctypes.CFUNCTYPE(c_i32, c_vp, ctypes.c_uint64, ctypes.c_uint64)),
+        ("create", ctypes.CFUNCTYPE(c_i32, c_vp, c_i32, ctypes.c_uint64, _u64p)),
+        ("release", ctypes.CFUNCTYPE(c_i32, c_vp, ctypes.c_uint64)),
+        ("map", ctypes.CFUNCTYPE(c_i32, c_vp, c_i32, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64)),
+        ("unmap", ctypes.CFUNCTYPE(c_i32, c_vp, ctypes.c_uint64, ctypes.c_uint64)),
+    ]
 
 _lib = None
 _lock = threading.Lock()

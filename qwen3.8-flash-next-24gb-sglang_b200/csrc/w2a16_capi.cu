@@ -43,6 +43,7 @@ const char* w2a16_status_string(int s) {
     case W2A16_ERR_ARG: return "invalid argument";
     case W2A16_ERR_WORKSPACE: return "workspace missing or too small";
     case W2A16_ERR_DEVICE: return "no usable sm_100 device";
+    case W2A16_ERR_MEMORY: return "no memory for another arena chunk";
     default: return "unknown status";
   }
 }

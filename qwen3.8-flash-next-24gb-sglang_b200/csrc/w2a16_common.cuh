@@ -38,6 +38,7 @@ enum Status : int {
   kErrArg = 4,
   kErrWorkspace = 5,
   kErrDevice = 6,
+  kErrMemory = 7,
 };
 
 // Device-side error word: bit 0 = an expert id outside [0, E) or an arena slot id outside [-1, S) (the row
