@@ -10,23 +10,26 @@
 // proj_kernel<kGateUp> (persistent, one CTA per SM): work items (group, tile of 128 weight columns -- gate_up:
 // 64 gate columns and the matching 64 up columns; down: 128 output columns), dealt round-robin. A producer warp
 // streams each item's codes, scales and zero points through a ring of shared-memory stages with tensor copies
-// (the fused layer's arena maps). Per 128-value quantization group along K:
-//   * warps 8-15 expand the codes to bf16(128 + q) -- exact -- straight into tensor memory as the MMA's A
-//     operand (the tile's column r is TMEM lane r; one 16-value word is 8 columns, one tcgen05.st);
-//   * warps 4-7 stage the group's rows of the activation (x for gate_up, h for down) in shared memory as the
-//     B operand, with the rows' sums and the tile's scales and zero points;
-//   * two MMA warps, taking alternate groups, issue 8 tcgen05.mma (A from tensor memory, M = 128 columns,
-//     N = 16 rows, K = 16, fp32 accumulation in tensor memory) and commit them to an mbarrier;
-//   * warps 0-3 read the accumulators (tcgen05.ld) and fold them into registers:
-//     acc += s * (D - (128 + zp) * sum x), the reference's zero-point fold (gemv/moe_gemv_int2_tab.py:61-66)
-//     applied per group with its scale.
-// Four operand and accumulator buffers rotate between groups, handed over with mbarriers (operands ready,
-// MMA done, accumulator read), so every role works on a different group at a time. Within each 16-value word
-// the MMA's K order is permuted (position 2j = value j, 2j + 1 = value j + 8, which is what one LOP3 per pair
-// yields); the B operand is staged in the same order. At decode sizes an expert has only a few rows per call,
-// so N = 16 MMAs leave the tensor pipe mostly idle (about 5 % active); the path pays where the per-token
-// path re-reads each expert many times, from about 64 tokens.
-// Epilogues: gate_up -> h = silu(gate) * up in bf16 per routed row; down -> routed weight * y row in fp32.
+// (the fused layer's arena maps). Per 128-value quantization group along K the group's exact integer sums
+// come from the tensor cores (kind::i8, int32 accumulation), with the arithmetic of the per-token kernels:
+//   * the expansion warps write the codes themselves as the A operand (s8, 0..3) into tensor memory -- one
+//     shift and one mask per four codes (the tile's column r is TMEM lane r) -- and the group's scales and
+//     zero points into shared memory;
+//   * the staging warps copy each routed row's group of the activation table into the B operand (s8,
+//     K-major, no swizzle): row n holds token n's high bytes, row 16 + n its low bytes; plus the row's scale
+//     and sum. xtab_kernel builds the tables once per call (x) and once between the projections (h): every
+//     row's 128 values of a group in 15-bit fixed point with one power-of-two scale, split into a signed high
+//     and a signed low byte (x16 = 256 hi + lo), in the K order of the A operand;
+//   * one MMA thread issues 4 tcgen05.mma (A from tensor memory, M = 128 columns, N = 32, K = 32) per group
+//     into the group's own accumulator in tensor memory;
+//   * two fold sets (taking alternate groups) read the accumulator (tcgen05.ld) and fold it exactly as the
+//     reference folds its zero point (gemv/moe_gemv_int2_tab.py:61-66): T = 256 D_hi + D_lo - zp sum x16
+//     (exact int32), acc += T * s * 2^e in fp32; at the end of an item the sets add their partial sums and
+//     write gate_up -> h = silu(gate) * up in bf16 per routed row, or down -> routed weight * y row in fp32.
+// Expansion and staging also come in two sets taking alternate groups. kNB operand/accumulator buffers
+// rotate between groups, handed over with mbarriers (operands ready, MMA done, buffer read). Within each
+// 16-value word the MMA's K order is the 4 x 4 transpose of the code order (K position p holds code
+// 4 * (p % 4) + p / 4); the B operand is staged in the same order.
 //
 // sum_kernel: y[m] = routed_scaling * (sum of the token's live y rows in routing order), deterministic.
 #include <climits>
@@ -38,15 +41,18 @@
 namespace w2a16 {
 namespace {
 
-constexpr int kGN = 16;                          // MMA N: rows of one group
+constexpr int kGN = 16;                          // routed rows of one group (tokens of one expert)
+constexpr int kBN = 2 * kGN;                     // MMA N: a high-byte and a low-byte row per routed row
 constexpr int kTileCols = 128;                   // MMA M: weight columns of a tile
-constexpr int kCompute = 512;                    // warps 0-3 fold, 4-7 stage B and the scales, 8-15 expand codes
-constexpr int kWriters = kCompute - 128;          // threads that write a group's operands (warps 4-15)
-constexpr int kMmaWarps = 2;                     // MMA issuers, taking alternate groups
-constexpr int kGThreads = kCompute + 32 + 32 * kMmaWarps;   // + the producer warp and the MMA warps
-constexpr int kAcols = kGroup / 2;               // TMEM columns of one group of the A operand (bf16 pairs)
-constexpr int kWordRows = kGroup / 16;           // 16-value word rows of a group
-constexpr int kBBytes = kGN * kGroup * 2;        // one group of the B operand (bf16)
+constexpr int kSets = 2;                         // warp sets per role (4 warps each, one per TMEM lane quarter)
+// warps: 0-7 fold sets, 8-15 expansion sets, 16-23 staging sets, the MMA warp, the producer warp; set k of a role
+// takes the groups gc with gc % kSets == k, so the sets work on different groups at the same time
+constexpr int kExpWarp0 = 4 * kSets, kStgWarp0 = 8 * kSets, kMmaWarp = 12 * kSets,
+              kProducerWarp = kMmaWarp + 1;
+constexpr int kGThreads = 32 * (kProducerWarp + 1);
+constexpr int kAcols = kGroup / 4;               // TMEM columns of one group of the A operand (4 codes each)
+constexpr int kDcols = kBN;                      // TMEM columns of one group's accumulator
+constexpr int kBBytes = kBN * kGroup;            // one group of the B operand (s8)
 constexpr int kGURing = 16, kDNRing = 8;
 // Ring stages (offsets multiples of 128 bytes, as tensor copies require):
 //   gate_up, 2 groups x (64 gate + 64 up columns): codes 2 x 4 KB [copy][word row][half][32 columns],
@@ -58,19 +64,25 @@ constexpr int kDNStage = 17664, kDNScale = 16384, kDNZero = 17408;
 constexpr int kMaxGroupedRows = 1024;            // routed rows per launch
 constexpr int kGroupedChunk = 128;               // tokens per launch
 constexpr unsigned kGWait = 1u << 17;            // suspending mbarrier tries before a wait gives up
-constexpr int kNB = 4;                           // operand / accumulator buffers in flight
-constexpr int kTmemCols = 512;                   // A: kNB buffers of kAcols columns; then kNB accumulators of kGN
-// kind::f16 instruction descriptor: fp32 accumulator, bf16 A and B, both K-major, N = 16, M = 128
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kGN >> 3) << 17) |
+constexpr int kNB = 6;                           // operand / accumulator buffers in flight
+constexpr int kTmemCols = 512;                   // A: kNB x kAcols columns, then kNB accumulators of kDcols
+static_assert(kNB * (kAcols + kDcols) <= kTmemCols, "tensor memory");
+// kind::i8 instruction descriptor: s32 accumulator, A and B s8 (the codes 0..3 are non-negative s8), both
+// K-major, N = 32, M = 128
+constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kBN >> 3) << 17) |
                             ((uint32_t)(kTileCols >> 4) << 24);
 
 __host__ __device__ constexpr int ring_bytes(bool gu) { return gu ? kGURing * kGUStage : kDNRing * kDNStage; }
-// mbarriers (full, empty per stage; ready, mma, tfree per buffer), tensor-memory address, row sums [kNB][kGN],
-// scales and zero points [kNB][128], gate_up's up-half exchange [64][kGN]
+// per buffer: scales sc[128] f32, zero points zc[128] i32, row scales xe[16] f32, row sums xs[16] i32
+constexpr int kSideBytes = kTileCols * 8 + kGN * 8;
+// mbarriers (full, empty per stage; ready, mma, free per buffer), tensor-memory address, the fold sets' item
+// exchange [128][kGN] and gate_up's up-half exchange [64][kGN]
 __host__ __device__ constexpr int small_bytes(bool gu) {
-  return (2 * (gu ? kGURing : kDNRing) + 3 * kNB) * 8 + 16 + kNB * kGN * 4 + kNB * kTileCols * 8 + 64 * kGN * 4;
+  return (2 * (gu ? kGURing : kDNRing) + 3 * kNB) * 8 + 16 + kTileCols * kGN * 4 + 64 * kGN * 4;
 }
-__host__ __device__ constexpr int proj_smem(bool gu) { return kNB * kBBytes + ring_bytes(gu) + small_bytes(gu); }
+__host__ __device__ constexpr int proj_smem(bool gu) {
+  return kNB * kBBytes + ring_bytes(gu) + kNB * kSideBytes + small_bytes(gu);
+}
 
 // Route tables in the workspace: [0] groups, then gslot, gstart, gcnt, order (R entries each) from int 16.
 struct RouteView {
@@ -86,9 +98,10 @@ struct ProjParams {
   CUtensorMap tm[3];          // codes, scales, zero windows of this projection (arena maps)
   int* route;                 // route tables (RouteView layout)
   int R;
-  const __nv_bfloat16* act;   // gate_up: x [M, H]; down: h [R, I]
-  int64_t act_stride;         // elements per activation row
-  int act_row_div;            // routed row r reads activation row r / act_row_div
+  const unsigned char* tab;   // activation tables (xtab_kernel): gate_up x rows, down h rows
+  const float* xe;            // [rows][G] power-of-two scale of each row and group
+  const int* xs;              // [rows][G] sum of the row's 15-bit values over the group
+  int act_row_div;            // routed row r reads table row r / act_row_div
   int K, N;                   // reduction length (H or I), weight columns (2I or H)
   int I;                      // h columns (gate_up output)
   int has_zeros, scale_bf16;
@@ -141,7 +154,8 @@ __device__ __forceinline__ void g_tma_4d(uint32_t dst, const CUtensorMap* map, i
 }
 __device__ __forceinline__ void tc_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
 __device__ __forceinline__ void tc_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
-__device__ __forceinline__ void fold_sync() { asm volatile("bar.sync 2, 128;\n" ::: "memory"); }
+__device__ __forceinline__ void fold_sync() { asm volatile("bar.sync 2, 128;\n" ::: "memory"); }     // fold set 0
+__device__ __forceinline__ void fold_sync2() { asm volatile("bar.sync 4, 256;\n" ::: "memory"); }    // both fold sets
 
 // Shared-memory matrix descriptor, K-major, no swizzle: core matrices of 8 rows x 16 bytes, the two 16-byte
 // halves of a K = 16 slice 128 bytes apart (leading byte offset), 8-row groups 256 bytes apart (stride byte
@@ -225,18 +239,21 @@ __global__ void __launch_bounds__(kGThreads, 1) proj_kernel(const __grid_constan
   constexpr int kGPS = kGU ? 2 : 4;                   // groups per stage
   unsigned char* bbuf = smem;                         // B operand, kNB buffers
   unsigned char* ring = smem + kNB * kBBytes;
-  unsigned char* small = ring + ring_bytes(kGU);
-  const uint32_t bars = s_u32(small);                 // full[kNS], empty[kNS], ready[kNB], mma[kNB], tfree[kNB]
+  unsigned char* side = ring + ring_bytes(kGU);       // per buffer: sc, zc, xe, xs
+  unsigned char* small = side + kNB * kSideBytes;
+  const uint32_t bars = s_u32(small);                 // full[kNS], empty[kNS], ready[kNB], mma[kNB], free[kNB]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(small + (2 * kNS + 3 * kNB) * 8);
-  float* bsum = reinterpret_cast<float*>(small + (2 * kNS + 3 * kNB) * 8 + 16);   // [kNB][kGN]
-  float* sc = bsum + kNB * kGN;                        // [kNB][128]
-  int* zc = reinterpret_cast<int*>(sc + kNB * kTileCols);   // [kNB][128]
-  float* upx = reinterpret_cast<float*>(zc + kNB * kTileCols);   // [64][kGN]
+  float* part = reinterpret_cast<float*>(small + (2 * kNS + 3 * kNB) * 8 + 16);   // [128][kGN]
+  float* upx = part + kTileCols * kGN;                                           // [64][kGN]
+  auto sc_of = [&](int b) { return reinterpret_cast<float*>(side + b * kSideBytes); };
+  auto zc_of = [&](int b) { return reinterpret_cast<int*>(side + b * kSideBytes + kTileCols * 4); };
+  auto xe_of = [&](int b) { return reinterpret_cast<float*>(side + b * kSideBytes + kTileCols * 8); };
+  auto xs_of = [&](int b) { return reinterpret_cast<int*>(side + b * kSideBytes + kTileCols * 8 + kGN * 4); };
   auto full = [&](int s) { return bars + 8u * s; };
   auto empty = [&](int s) { return bars + 8u * (kNS + s); };
   auto ready = [&](int b) { return bars + 8u * (2 * kNS + b); };
   auto mmab = [&](int b) { return bars + 8u * (2 * kNS + kNB + b); };
-  auto tfree = [&](int b) { return bars + 8u * (2 * kNS + 2 * kNB + b); };
+  auto freeb = [&](int b) { return bars + 8u * (2 * kNS + 2 * kNB + b); };
   // group gc uses buffer gc % kNB for the (gc / kNB)-th time: the phase parity of its barriers
   auto buf = [](unsigned gc) { return (int)(gc % kNB); };
   auto par = [](unsigned gc) { return (gc / kNB) & 1u; };
@@ -246,17 +263,16 @@ __global__ void __launch_bounds__(kGThreads, 1) proj_kernel(const __grid_constan
   const int nsteps = (G + kGPS - 1) / kGPS;
   const int ntiles = kGU ? p.I / 64 : p.N / kTileCols;
   const bool aligned = (s_u32(smem) & 1023u) == 0;
-  constexpr int kProducerWarp = kCompute / 32, kMmaWarp = kProducerWarp + 1;
 
   if (warp == kProducerWarp && lane == 0) {
     for (int s = 0; s < kNS; ++s) {
       g_mbar_init(full(s), 1);
-      g_mbar_init(empty(s), kWriters);
+      g_mbar_init(empty(s), 4 * kGPS);                // per group of the stage, its expansion set's 4 warps
     }
     for (int b = 0; b < kNB; ++b) {
-      g_mbar_init(ready(b), kWriters);
+      g_mbar_init(ready(b), 8);                       // the group's expansion set and staging set, 4 warps each
       g_mbar_init(mmab(b), 1);
-      g_mbar_init(tfree(b), 128);
+      g_mbar_init(freeb(b), 4);                       // the group's fold set
     }
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     for (int k = 0; k < 3; ++k)
@@ -273,6 +289,7 @@ __global__ void __launch_bounds__(kGThreads, 1) proj_kernel(const __grid_constan
   __syncthreads();
   tc_after();
   const uint32_t tmem = *tmem_slot;
+  const uint32_t tacc = tmem + (uint32_t)(kNB * kAcols);   // accumulator of buffer b at column tacc + b * kDcols
   const int ngroups = p.route[0];
   const int nitems = ngroups * ntiles;
 
@@ -319,110 +336,171 @@ __global__ void __launch_bounds__(kGThreads, 1) proj_kernel(const __grid_constan
     return;
   }
 
-  if (warp >= kMmaWarp) {
-    // MMA issuers (one thread per warp takes every kMmaWarps-th group: one thread issues an MMA only every
-    // few tens of cycles): per group, once its operands are in place and its accumulator buffer has been read
+  if (warp == kMmaWarp) {
+    // MMA issuer: per group, once its operands are in place, 4 MMAs of K = 32 into the group's accumulator,
+    // committed to the buffer's MMA barrier (the fold set waits on it)
     if (lane == 0) {
-      const unsigned q = (unsigned)(warp - kMmaWarp);
       unsigned gc = 0;
       for (int w = blockIdx.x; w < nitems; w += gridDim.x)
         for (int g = 0; g < G; ++g, ++gc) {
-          if (gc % kMmaWarps != q) continue;
           const int b = buf(gc);
           g_mbar_wait(ready(b), par(gc), p.err);
-          if (gc >= kNB) g_mbar_wait(tfree(b), par(gc - kNB), p.err);
           tc_after();
           const uint32_t b0 = s_u32(bbuf + b * kBBytes);
-          const uint32_t dt = tmem + (uint32_t)(kNB * kAcols + b * kGN);
+          const uint32_t dt = tacc + (uint32_t)(b * kDcols);
 #pragma unroll
-          for (int k16 = 0; k16 < kGroup / 16; ++k16) {
-            const uint32_t at = tmem + (uint32_t)(b * kAcols + k16 * 8);
-            const uint64_t bd = kmajor_desc(b0 + k16 * 512);
-            asm volatile(
-                "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\ntcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(dt),
-                "r"(at), "l"(bd), "r"(kIdesc), "r"(k16)
-                : "memory");
+          for (int k32 = 0; k32 < kGroup / 32; ++k32) {
+            const uint32_t at = tmem + (uint32_t)(b * kAcols + k32 * 8);
+            const uint64_t bd = kmajor_desc(b0 + k32 * 1024);
+            if (k32 == 0)
+              asm volatile("tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, 0;\n" ::"r"(dt), "r"(at), "l"(bd),
+                           "r"(kIdesc)
+                           : "memory");
+            else
+              asm volatile("tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, 1;\n" ::"r"(dt), "r"(at), "l"(bd),
+                           "r"(kIdesc)
+                           : "memory");
           }
           asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(mmab(b))
                        : "memory");
         }
     }
     __syncwarp();
-  } else if (warp < 4) {
-    // ---------------------------------------------------------------- fold warps: thread r = tile column r
-    unsigned gc = 0;
-    float acc[kGN];
-    for (int w = blockIdx.x; w < nitems; w += gridDim.x) {
+  } else if (warp < kExpWarp0) {
+    // ---------------------------------------------------------------- fold sets: thread = tile column r
+    const int set = warp >> 2;
+    const int r = 32 * (warp & 3) + lane;
+    unsigned gc0 = 0;
+    for (int w = blockIdx.x; w < nitems; w += gridDim.x, gc0 += (unsigned)G) {
       const int gi = w / ntiles, t = w - gi * ntiles;
-      const int g0 = rv.gstart()[gi], cnt = rv.gcnt()[gi];
+      float acc[kGN];
 #pragma unroll
       for (int n = 0; n < kGN; ++n) acc[n] = 0.f;
-      for (int g = 0; g < G; ++g, ++gc) {
-        const int bx = buf(gc);
-        g_mbar_wait(ready(bx), par(gc), p.err);         // this group's scales, zero points, row sums
-        g_mbar_wait(mmab(bx), par(gc), p.err);          // and its accumulators
+      const int gfirst = (int)(((unsigned)set + kSets - gc0 % kSets) % kSets);
+      for (int g = gfirst; g < G; g += kSets) {
+        const unsigned gc = gc0 + (unsigned)g;
+        const int b = buf(gc);
+        g_mbar_wait(ready(b), par(gc), p.err);          // the group's scales, zero points, row scales and sums
+        g_mbar_wait(mmab(b), par(gc), p.err);           // and its MMAs are done
         tc_after();
-        uint32_t d[kGN];
+        uint32_t d[kBN];
         asm volatile(
-            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-            "%15}, [%16];\n"
+            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+            "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n"
             : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3]), "=r"(d[4]), "=r"(d[5]), "=r"(d[6]), "=r"(d[7]),
-              "=r"(d[8]), "=r"(d[9]), "=r"(d[10]), "=r"(d[11]), "=r"(d[12]), "=r"(d[13]), "=r"(d[14]), "=r"(d[15])
-            : "r"(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)(kNB * kAcols + bx * kGN)));
+              "=r"(d[8]), "=r"(d[9]), "=r"(d[10]), "=r"(d[11]), "=r"(d[12]), "=r"(d[13]), "=r"(d[14]), "=r"(d[15]),
+              "=r"(d[16]), "=r"(d[17]), "=r"(d[18]), "=r"(d[19]), "=r"(d[20]), "=r"(d[21]), "=r"(d[22]), "=r"(d[23]),
+              "=r"(d[24]), "=r"(d[25]), "=r"(d[26]), "=r"(d[27]), "=r"(d[28]), "=r"(d[29]), "=r"(d[30]), "=r"(d[31])
+            : "r"(tacc + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(b * kDcols)));
         asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
-        const float s = sc[bx * kTileCols + tid];
-        const float zz = 128.f + (float)zc[bx * kTileCols + tid];
+        const float s = sc_of(b)[r];
+        const int zp = zc_of(b)[r];
+        const float* xe = xe_of(b);
+        const int* xs = xs_of(b);
 #pragma unroll
-        for (int n = 0; n < kGN; ++n) acc[n] += s * (__uint_as_float(d[n]) - zz * bsum[bx * kGN + n]);
+        for (int n = 0; n < kGN; ++n) {
+          const int T = (int)d[n] * 256 + (int)d[kGN + n] - zp * xs[n];   // exact: |T| < 2^24
+          acc[n] = fmaf((float)T, s * xe[n], acc[n]);
+        }
         tc_before();
-        g_mbar_arrive(tfree(bx));                       // accumulators and row data of buffer bx are read
+        __syncwarp();
+        if (lane == 0) g_mbar_arrive(freeb(b));          // the buffer's accumulator and side data are read
       }
-      if constexpr (kGU) {
-        // rows 0-63 gate, 64-127 up of the tile's 64 h-columns: h = silu(gate) * up
-        if (tid >= 64)
+      // the two sets' partial sums of the item, added in set order, then the epilogue by set 0
+      if (set == 1)
 #pragma unroll
-          for (int n = 0; n < kGN; ++n) upx[(tid - 64) * kGN + n] = acc[n];
-        fold_sync();
-        if (tid < 64)
+        for (int n = 0; n < kGN; ++n) part[r * kGN + n] = acc[n];
+      fold_sync2();
+      if (set == 0) {
+#pragma unroll
+        for (int n = 0; n < kGN; ++n) acc[n] += part[r * kGN + n];
+        const int g0 = rv.gstart()[gi], cnt = rv.gcnt()[gi];
+        if constexpr (kGU) {
+          // rows 0-63 gate, 64-127 up of the tile's 64 h-columns: h = silu(gate) * up
+          if (r >= 64)
+#pragma unroll
+            for (int n = 0; n < kGN; ++n) upx[(r - 64) * kGN + n] = acc[n];
+          fold_sync();
+          if (r < 64)
+#pragma unroll
+            for (int n = 0; n < kGN; ++n)
+              if (n < cnt) {
+                const int row = rv.order()[g0 + n];
+                p.hout[(int64_t)row * p.I + 64 * t + r] = __float2bfloat16(silu(acc[n]) * upx[r * kGN + n]);
+              }
+          fold_sync();
+        } else {
 #pragma unroll
           for (int n = 0; n < kGN; ++n)
             if (n < cnt) {
               const int row = rv.order()[g0 + n];
-              p.hout[(int64_t)row * p.I + 64 * t + tid] = __float2bfloat16(silu(acc[n]) * upx[tid * kGN + n]);
+              p.yrows[(int64_t)row * p.N + kTileCols * t + r] = p.topk_w[row] * acc[n];
             }
-        fold_sync();
-      } else {
-#pragma unroll
-        for (int n = 0; n < kGN; ++n)
-          if (n < cnt) {
-            const int row = rv.order()[g0 + n];
-            p.yrows[(int64_t)row * p.N + kTileCols * t + tid] = p.topk_w[row] * acc[n];
-          }
+        }
       }
+      fold_sync2();                                     // set 0 has read the exchange before set 1 writes again
     }
-  } else if (warp < 8) {
-    // ---------------------------------------------------------------- staging warps: B, row sums, scales
-    const bool sbf = p.scale_bf16 != 0, hz = p.has_zeros != 0;
-    const int r = tid - 128;                            // tile column whose scale / zero point this thread takes
-    const int bn = r >> 3, bs = r & 7;                  // B row r / 8, K = 16 slice r % 8 of every group
-    int i = 0;
-    unsigned gc = 0;
-    for (int w = blockIdx.x; w < nitems; w += gridDim.x) {
+  } else if (warp >= kStgWarp0) {
+    // ---------------------------------------------------------------- staging sets: the B operand
+    // thread: routed row bn of the group (B rows bn and kGN + bn), 16-value word bs of each group
+    const int set = (warp - kStgWarp0) >> 2;
+    const int r = tid - 32 * (kStgWarp0 + 4 * set);
+    const int bn = r >> 3, bs = r & 7;
+    unsigned gc0 = 0;
+    for (int w = blockIdx.x; w < nitems; w += gridDim.x, gc0 += (unsigned)G) {
       const int gi = w / ntiles;
       const int g0 = rv.gstart()[gi], cnt = rv.gcnt()[gi];
-      const __nv_bfloat16* brow = nullptr;
-      if (bn < cnt) brow = p.act + (int64_t)(rv.order()[g0 + bn] / p.act_row_div) * p.act_stride + bs * 16;
-      uint4 pa = make_uint4(0, 0, 0, 0), pb = pa;
-      if (brow) {
-        pa = *reinterpret_cast<const uint4*>(brow);
-        pb = *reinterpret_cast<const uint4*>(brow + 8);
+      const int trow = bn < cnt ? rv.order()[g0 + bn] / p.act_row_div : -1;   // table row, -1 = padding
+      const int gfirst = (int)(((unsigned)set + kSets - gc0 % kSets) % kSets);
+      uint4 ph = make_uint4(0, 0, 0, 0), pl = ph;
+      float e = 0.f;
+      int sx = 0;
+      auto fetch = [&](int g) {
+        const unsigned char* src = p.tab + ((size_t)trow * G + g) * 256 + bs * 16;
+        ph = *reinterpret_cast<const uint4*>(src);
+        pl = *reinterpret_cast<const uint4*>(src + 128);
+        if (bs == 0) {
+          e = p.xe[(size_t)trow * G + g];
+          sx = p.xs[(size_t)trow * G + g];
+        }
+      };
+      if (trow >= 0 && gfirst < G) fetch(gfirst);
+      for (int g = gfirst; g < G; g += kSets) {
+        const unsigned gc = gc0 + (unsigned)g;
+        const int b = buf(gc);
+        if (gc >= kNB) g_mbar_wait(freeb(b), par(gc - kNB), p.err);   // buffer b's previous group is folded
+        unsigned char* B = bbuf + b * kBBytes + (bs >> 1) * 1024;
+        *reinterpret_cast<uint4*>(B + canon_off(bn, bs & 1)) = ph;
+        *reinterpret_cast<uint4*>(B + canon_off(kGN + bn, bs & 1)) = pl;
+        if (bs == 0) {
+          xe_of(b)[bn] = e;
+          xs_of(b)[bn] = sx;
+        }
+        if (trow >= 0 && g + kSets < G) fetch(g + kSets);   // this set's next group of the item
+        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");   // generic writes -> the MMA's reads
+        __syncwarp();
+        if (lane == 0) g_mbar_arrive(ready(b));
       }
-      for (int g = 0; g < G; ++g, ++gc) {
+    }
+  } else {
+    // ---------------------------------------------------------------- expansion sets: codes -> A in TMEM
+    // warp kExpWarp0 + 4 set + q takes TMEM lanes (tile columns) 32 q .. + 31 of its set's groups
+    const bool sbf = p.scale_bf16 != 0, hz = p.has_zeros != 0;
+    const int set = (warp - kExpWarp0) >> 2;
+    const int r = 32 * (warp & 3) + lane;
+    const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+    int i = 0;                                          // the CTA's stage count at the item's start
+    unsigned gc0 = 0;
+    for (int w = blockIdx.x; w < nitems; w += gridDim.x, i += nsteps, gc0 += (unsigned)G) {
+      const int gfirst = (int)(((unsigned)set + kSets - gc0 % kSets) % kSets);
+      for (int g = gfirst; g < G; g += kSets) {
+        const unsigned gc = gc0 + (unsigned)g;
         const int s = g / kGPS, gs = g - s * kGPS;
         const int st = (i + s) % kNS;
         const int b = buf(gc);
-        if (gc >= kNB) g_mbar_wait(tfree(b), par(gc - kNB), p.err);   // group gc - kNB folded (its MMA done)
-        if (gs == 0) g_mbar_wait(full(st), (unsigned)((i + s) / kNS) & 1u, p.err);
+        if (gc >= kNB) g_mbar_wait(freeb(b), par(gc - kNB), p.err);   // buffer b's previous group is folded
+        tc_after();                                     // the stores below come after that group's MMAs
+        g_mbar_wait(full(st), (unsigned)((i + s) / kNS) & 1u, p.err);
         const unsigned char* stg = ring + (size_t)st * kStage;
         uint32_t raw;
         int zp = 2;
@@ -434,82 +512,117 @@ __global__ void __launch_bounds__(kGThreads, 1) proj_kernel(const __grid_constan
           raw = *reinterpret_cast<const uint16_t*>(stg + kDNScale + (r >> 5) * 256 + (gs * 32 + (r & 31)) * 2);
           if (hz) zp = (stg[kDNZero + (r >> 6) * 128 + gs * 16 + ((r & 63) >> 2)] >> (2 * (r & 3))) & 3;
         }
-        sc[b * kTileCols + r] = sbf ? __bfloat162float(__ushort_as_bfloat16((unsigned short)raw))
-                                    : __half2float(__ushort_as_half((unsigned short)raw));
-        zc[b * kTileCols + r] = zp;
-        // B: the prefetched slice in the permuted K order, and the row's sum over the group
-        unsigned char* B = bbuf + b * kBBytes + bs * 512 + canon_off(bn, 0);
-        *reinterpret_cast<uint4*>(B) = make_uint4(__byte_perm(pa.x, pb.x, 0x5410), __byte_perm(pa.x, pb.x, 0x7632),
-                                                  __byte_perm(pa.y, pb.y, 0x5410), __byte_perm(pa.y, pb.y, 0x7632));
-        *reinterpret_cast<uint4*>(B + 128) = make_uint4(__byte_perm(pa.z, pb.z, 0x5410), __byte_perm(pa.z, pb.z, 0x7632),
-                                                        __byte_perm(pa.w, pb.w, 0x5410), __byte_perm(pa.w, pb.w, 0x7632));
-        float sum = 0.f;
-        const uint32_t v[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
+        sc_of(b)[r] = sbf ? __bfloat162float(__ushort_as_bfloat16((unsigned short)raw))
+                          : __half2float(__ushort_as_half((unsigned short)raw));
+        zc_of(b)[r] = zp;
+        // word kw -> 4 TMEM columns: class c = codes c, 4 + c, 8 + c, 12 + c as bytes (bits 2c of each byte)
 #pragma unroll
-        for (int k = 0; k < 8; ++k) sum += __uint_as_float(v[k] << 16) + __uint_as_float(v[k] & 0xFFFF0000u);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 4);
-        if (bs == 0) bsum[b * kGN + bn] = sum;
-        if (brow && g + 1 < G) {                        // next group's slice
-          pa = *reinterpret_cast<const uint4*>(brow + (g + 1) * kGroup);
-          pb = *reinterpret_cast<const uint4*>(brow + (g + 1) * kGroup + 8);
-        }
-        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");   // generic writes -> the MMA's reads
-        g_mbar_arrive(ready(b));
-        if (gs == kGPS - 1 || g == G - 1) g_mbar_arrive(empty(st));     // this thread is done with the stage
-      }
-      i += nsteps;
-    }
-  } else {
-    // ---------------------------------------------------------------- expansion warps: codes -> A in TMEM
-    // warp 8 + q takes TMEM lanes (tile columns) 32 (q % 4) .. + 31 and word rows q / 4, q / 4 + 2, ...
-    const int r = 32 * (warp & 3) + lane, kw0 = (warp - 8) >> 2;
-    const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
-    int i = 0;
-    unsigned gc = 0;
-    for (int w = blockIdx.x; w < nitems; w += gridDim.x) {
-      for (int g = 0; g < G; ++g, ++gc) {
-        const int s = g / kGPS, gs = g - s * kGPS;
-        const int st = (i + s) % kNS;
-        const int b = buf(gc);
-        if (gc >= kNB) g_mbar_wait(mmab(b), par(gc - kNB), p.err);   // A buffer b is free
-        tc_after();                                     // the stores below come after that MMA's reads
-        if (gs == 0) g_mbar_wait(full(st), (unsigned)((i + s) / kNS) & 1u, p.err);
-        const unsigned char* stg = ring + (size_t)st * kStage;
-        // bf16(128 + q), value j and j + 8 of a word paired in one register: 8 TMEM columns per word
+        for (int h = 0; h < 2; ++h) {
+          uint32_t m[16];
 #pragma unroll
-        for (int j = 0; j < kWordRows / 2; ++j) {
-          const int kw = kw0 + 2 * j;
-          uint32_t wd;
-          if constexpr (kGU)
-            wd = *reinterpret_cast<const uint32_t*>(stg + ((r & 63) >> 5) * 4096 + (gs * 8 + kw) * 256 +
-                                                    (r >> 6) * 128 + (r & 31) * 4);
-          else
-            wd = *reinterpret_cast<const uint32_t*>(stg + (r >> 5) * 4096 + (gs * 8 + kw) * 128 + (r & 31) * 4);
-          uint32_t m[8];
+          for (int j = 0; j < 4; ++j) {
+            const int kw = 4 * h + j;
+            uint32_t wd;
+            if constexpr (kGU)
+              wd = *reinterpret_cast<const uint32_t*>(stg + ((r & 63) >> 5) * 4096 + (gs * 8 + kw) * 256 +
+                                                      (r >> 6) * 128 + (r & 31) * 4);
+            else
+              wd = *reinterpret_cast<const uint32_t*>(stg + (r >> 5) * 4096 + (gs * 8 + kw) * 128 + (r & 31) * 4);
 #pragma unroll
-          for (int jj = 0; jj < 8; ++jj) m[jj] = ((wd >> (2 * jj)) & 0x00030003u) | 0x43004300u;
-          asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};\n" ::"r"(
-                           tmem + lane_base + (uint32_t)(b * kAcols + kw * 8)),
-                       "r"(m[0]), "r"(m[1]), "r"(m[2]), "r"(m[3]), "r"(m[4]), "r"(m[5]), "r"(m[6]), "r"(m[7])
-                       : "memory");
+            for (int c = 0; c < 4; ++c) m[4 * j + c] = (wd >> (2 * c)) & 0x03030303u;
+          }
+          asm volatile(
+              "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+              "%14, %15, %16};\n" ::"r"(tmem + lane_base + (uint32_t)(b * kAcols + 16 * h)),
+              "r"(m[0]), "r"(m[1]), "r"(m[2]), "r"(m[3]), "r"(m[4]), "r"(m[5]), "r"(m[6]), "r"(m[7]), "r"(m[8]),
+              "r"(m[9]), "r"(m[10]), "r"(m[11]), "r"(m[12]), "r"(m[13]), "r"(m[14]), "r"(m[15])
+              : "memory");
         }
         asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
         tc_before();
-        g_mbar_arrive(ready(b));
-        if (gs == kGPS - 1 || g == G - 1) g_mbar_arrive(empty(st));     // this thread is done with the stage
+        __syncwarp();                                   // the warp's stores are complete and its stage reads done
+        if (lane == 0) {
+          g_mbar_arrive(ready(b));
+          // the stage's empty barrier counts 4 arrivals per group; the last group of an item also stands in for
+          // the groups a short last stage lacks
+          g_mbar_arrive(empty(st));
+          if (g == G - 1)
+            for (int k = gs + 1; k < kGPS; ++k) g_mbar_arrive(empty(st));
+        }
       }
-      i += nsteps;
     }
   }
-  // compute warps and the MMA warp: every accumulator was read after its MMA completed (the folds waited on
-  // them), so the tensor memory can go
+  // all but the producer: every group's MMAs completed before its fold set read the accumulator, so the tensor
+  // memory can go
   tc_before();
-  asm volatile("bar.sync 3, %0;\n" ::"n"(kCompute + 32 * kMmaWarps) : "memory");
+  asm volatile("bar.sync 3, %0;\n" ::"n"(kGThreads - 32) : "memory");
   if (warp == 0) {
     tc_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+// Activation tables for the B operand: rows x K bf16 -> per (row, 128-value group) 256 bytes (8 words x 16 high
+// bytes, then 8 words x 16 low bytes; K position 4c + j of a word holds value 4j + c), the power-of-two scale
+// 2^(e - 14) (mx = f 2^e, f in [0.5, 1), so |x16| <= 2^14) and the sum of the 128 values x16. Eight lanes per
+// (row, group), one 16-value word each.
+__global__ void __launch_bounds__(256) xtab_kernel(const __nv_bfloat16* act, int rows, int64_t stride, int G,
+                                                   unsigned char* tab, float* xe, int* xs) {
+  const int team = (int)((blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 3);
+  const int bs = threadIdx.x & 7;
+  const bool live = team < rows * G;
+  const int row = live ? team / G : 0, g = live ? team - row * G : 0;
+  float v[16];
+  {
+    uint4 pa = make_uint4(0, 0, 0, 0), pb = pa;
+    if (live) {
+      const __nv_bfloat16* src = act + (int64_t)row * stride + g * kGroup + bs * 16;
+      pa = *reinterpret_cast<const uint4*>(src);
+      pb = *reinterpret_cast<const uint4*>(src + 8);
+    }
+    const uint32_t u[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      v[2 * k] = __uint_as_float(u[k] << 16);
+      v[2 * k + 1] = __uint_as_float(u[k] & 0xFFFF0000u);
+    }
+  }
+  float mx = 0.f;
+#pragma unroll
+  for (int k = 0; k < 16; ++k) mx = fmaxf(mx, fabsf(v[k]));
+  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+  const int e = mx > 0.f ? frexp_exponent(mx) : 0;
+  const float inv = pow2f(14 - e);
+  // t = x16 + 128: its byte 1 is the signed high byte hi = (x16 + 128) >> 8, its byte 0 xor 0x80 the signed
+  // low byte lo = x16 - 256 hi
+  uint32_t t[16];
+  int sum = 0;
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    const int q = __float2int_rn(v[k] * inv);
+    sum += q;
+    t[k] = (uint32_t)(q + 128);
+  }
+  sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+  sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+  sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+  uint32_t H[4], L[4];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    // values c, 4 + c, 8 + c, 12 + c -> bytes 0..3
+    H[c] = __byte_perm(__byte_perm(t[c], t[4 + c], 0x0051), __byte_perm(t[8 + c], t[12 + c], 0x0051), 0x5410);
+    L[c] = __byte_perm(__byte_perm(t[c], t[4 + c], 0x0040), __byte_perm(t[8 + c], t[12 + c], 0x0040), 0x5410) ^
+           0x80808080u;
+  }
+  if (!live) return;
+  unsigned char* dst = tab + (size_t)team * 256 + bs * 16;
+  *reinterpret_cast<uint4*>(dst) = make_uint4(H[0], H[1], H[2], H[3]);
+  *reinterpret_cast<uint4*>(dst + 128) = make_uint4(L[0], L[1], L[2], L[3]);
+  if (bs == 0) {
+    xe[team] = pow2f(e - 14);
+    xs[team] = sum;
   }
 }
 
@@ -541,11 +654,17 @@ size_t align256(size_t b) { return (b + 255) & ~size_t(255); }
 // Workspace of the grouped path: the per-token layer's persistent head first (its barrier words and epoch-tagged
 // hand-off words must survive calls of either path, so this path never writes there), then for one launch of
 // up to chunk_tokens() tokens the route tables, h [R, I] bf16 and the y rows [R, H] fp32.
+// Bytes of the activation tables of `rows` rows of K values (xtab_kernel): 256 per (row, group), then the scales
+// and the sums.
+size_t tab_bytes(size_t rows, int K) {
+  const size_t n = rows * (size_t)(K / kGroup);
+  return align256(n * 256) + align256(n * 4) + align256(n * 4);
+}
 size_t grouped_workspace_bytes(int M, int H, int I, int top_k) {
   if (M <= 0 || top_k <= 0 || top_k > kMaxGroupedRows) return 0;
-  const size_t R = (size_t)chunk_tokens(M, top_k) * top_k;
+  const size_t mc = (size_t)chunk_tokens(M, top_k), R = mc * top_k;
   return align256(layer_workspace_bytes(0, H, I, top_k)) + align256((16 + 4 * R) * 4) + align256(R * I * 2) +
-         align256(R * H * 4);
+         align256(R * H * 4) + tab_bytes(mc, H) + tab_bytes(R, I);
 }
 
 int grouped_check(const LayerArgs& a) {
@@ -581,25 +700,40 @@ int decode_layer_grouped(const LayerArgs& a) {
   __nv_bfloat16* hbuf = reinterpret_cast<__nv_bfloat16*>(ws + align256((16 + 4 * (size_t)Rmax) * 4));
   float* yrows = reinterpret_cast<float*>(ws + align256((16 + 4 * (size_t)Rmax) * 4) +
                                           align256((size_t)Rmax * a.I * 2));
+  // activation tables: x (mc_max rows of H), then h (Rmax rows of I)
+  struct Tab { unsigned char* t; float* e; int* s; };
+  auto carve = [](unsigned char* base, size_t rows, int K) {
+    const size_t n = rows * (size_t)(K / kGroup);
+    return Tab{base, reinterpret_cast<float*>(base + align256(n * 256)),
+               reinterpret_cast<int*>(base + align256(n * 256) + align256(n * 4))};
+  };
+  unsigned char* tabs = reinterpret_cast<unsigned char*>(yrows) + align256((size_t)Rmax * a.H * 4);
+  const Tab xt = carve(tabs, (size_t)mc_max, a.H);
+  const Tab ht = carve(tabs + tab_bytes((size_t)mc_max, a.H), (size_t)Rmax, a.I);
+  const int G1 = a.H / kGroup, G2 = a.I / kGroup;
   const bool hz = a.map13.has_zeros != 0;
   for (int m0 = 0; m0 < a.M; m0 += mc_max) {
     const int mc = a.M - m0 < mc_max ? a.M - m0 : mc_max;
     const int R = mc * a.top_k;
     const int32_t* ids = a.ids + (size_t)m0 * a.top_k;
     route_kernel<<<1, 1024, 0, a.stream>>>(ids, a.map13.slots, a.map13.E, a.map13.S, R, route, a.err);
+    const int nx = mc * G1 * 8;                         // 8 lanes per (row, group)
+    xtab_kernel<<<(unsigned)((nx + 255) / 256), 256, 0, a.stream>>>(
+        static_cast<const __nv_bfloat16*>(a.x) + (size_t)m0 * a.H, mc, a.H, G1, xt.t, xt.e, xt.s);
     ProjParams gu{};
     gu.tm[0] = tm[0]; gu.tm[1] = tm[1]; gu.tm[2] = tm[2];
     gu.route = route; gu.R = R;
-    gu.act = static_cast<const __nv_bfloat16*>(a.x) + (size_t)m0 * a.H;
-    gu.act_stride = a.H; gu.act_row_div = a.top_k;
+    gu.tab = xt.t; gu.xe = xt.e; gu.xs = xt.s; gu.act_row_div = a.top_k;
     gu.K = a.H; gu.N = 2 * a.I; gu.I = a.I;
     gu.has_zeros = hz; gu.scale_bf16 = a.scale_bf16;
     gu.hout = hbuf; gu.err = a.err;
     proj_kernel<true><<<sms, kGThreads, proj_smem(true), a.stream>>>(gu);
+    const int nh = R * G2 * 8;
+    xtab_kernel<<<(unsigned)((nh + 255) / 256), 256, 0, a.stream>>>(hbuf, R, a.I, G2, ht.t, ht.e, ht.s);
     ProjParams dn{};
     dn.tm[0] = tm[3]; dn.tm[1] = tm[4]; dn.tm[2] = tm[5];
     dn.route = route; dn.R = R;
-    dn.act = hbuf; dn.act_stride = a.I; dn.act_row_div = 1;
+    dn.tab = ht.t; dn.xe = ht.e; dn.xs = ht.s; dn.act_row_div = 1;
     dn.K = a.I; dn.N = a.H; dn.I = a.I;
     dn.has_zeros = hz; dn.scale_bf16 = a.scale_bf16;
     dn.topk_w = a.topk_w + (size_t)m0 * a.top_k; dn.yrows = yrows; dn.err = a.err;
