@@ -44,11 +44,13 @@ namespace {
 constexpr int kGN = 16;                          // routed rows of one group (tokens of one expert)
 constexpr int kBN = 2 * kGN;                     // MMA N: a high-byte and a low-byte row per routed row
 constexpr int kTileCols = 128;                   // MMA M: weight columns of a tile
-constexpr int kSets = 2;                         // warp sets per role (4 warps each, one per TMEM lane quarter)
-// warps: 0-7 fold sets, 8-15 expansion sets, 16-23 staging sets, the MMA warp, the producer warp; set k of a role
-// takes the groups gc with gc % kSets == k, so the sets work on different groups at the same time
-constexpr int kExpWarp0 = 4 * kSets, kStgWarp0 = 8 * kSets, kMmaWarp = 12 * kSets,
-              kProducerWarp = kMmaWarp + 1;
+constexpr int kSets = 2;                         // fold and expansion sets (4 warps each, one per TMEM lane quarter)
+constexpr int kMmaWarps = 4;                     // MMA issuers, one per SM sub-partition
+// warps: 0-7 fold sets, 8-15 expansion sets, 16-19 staging, 20-23 MMA issuers, the producer warp. Set k of the
+// fold and expansion roles takes the groups gc with gc % kSets == k, MMA warp m those with gc % kMmaWarps == m,
+// so several groups are in every stage of the hand-over at once
+constexpr int kExpWarp0 = 4 * kSets, kStgWarp0 = 8 * kSets, kMmaWarp0 = kStgWarp0 + 4,
+              kProducerWarp = kMmaWarp0 + kMmaWarps;
 constexpr int kGThreads = 32 * (kProducerWarp + 1);
 constexpr int kAcols = kGroup / 4;               // TMEM columns of one group of the A operand (4 codes each)
 constexpr int kDcols = kBN;                      // TMEM columns of one group's accumulator
@@ -64,7 +66,8 @@ constexpr int kDNStage = 17664, kDNScale = 16384, kDNZero = 17408;
 constexpr int kMaxGroupedRows = 1024;            // routed rows per launch
 constexpr int kGroupedChunk = 128;               // tokens per launch
 constexpr unsigned kGWait = 1u << 17;            // suspending mbarrier tries before a wait gives up
-constexpr int kNB = 6;                           // operand / accumulator buffers in flight
+constexpr unsigned kGSpin = 1u << 26;            // mbarrier polls before a spin gives up (well over a second)
+constexpr int kNB = 8;                           // operand / accumulator buffers in flight
 constexpr int kTmemCols = 512;                   // A: kNB x kAcols columns, then kNB accumulators of kDcols
 static_assert(kNB * (kAcols + kDcols) <= kTmemCols, "tensor memory");
 // kind::i8 instruction descriptor: s32 accumulator, A and B s8 (the codes 0..3 are non-negative s8), both
@@ -121,7 +124,9 @@ __device__ __forceinline__ void g_mbar_arrive(uint32_t bar) {
 __device__ __forceinline__ void g_mbar_arrive_tx(uint32_t bar, unsigned bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
 }
-// Bounded wait for the phase of the given parity (error bit 1 when it gives up).
+// Bounded waits for the phase of the given parity (error bit 1 when they give up): suspending tries for the many
+// threads of a role, non-suspending polls for the one MMA thread (a thread suspended in try_wait resumes some
+// time after the phase completes, and the MMA thread's waits are on the hand-over chain of every group).
 __device__ __forceinline__ void g_mbar_wait(uint32_t bar, unsigned parity, unsigned* err) {
   for (unsigned it = 0;; ++it) {
     uint32_t ok;
@@ -132,6 +137,21 @@ __device__ __forceinline__ void g_mbar_wait(uint32_t bar, unsigned parity, unsig
         : "memory");
     if (ok) return;
     if (it > kGWait) {
+      flag_error(err, 2u);
+      return;
+    }
+  }
+}
+__device__ __forceinline__ void g_mbar_spin(uint32_t bar, unsigned parity, unsigned* err) {
+  for (unsigned it = 0;; ++it) {
+    uint32_t ok;
+    asm volatile(
+        "{\n.reg .pred p;\nmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (ok) return;
+    if (it > kGSpin) {
       flag_error(err, 2u);
       return;
     }
@@ -270,7 +290,7 @@ __global__ void __launch_bounds__(kGThreads, 1) proj_kernel(const __grid_constan
       g_mbar_init(empty(s), 4 * kGPS);                // per group of the stage, its expansion set's 4 warps
     }
     for (int b = 0; b < kNB; ++b) {
-      g_mbar_init(ready(b), 8);                       // the group's expansion set and staging set, 4 warps each
+      g_mbar_init(ready(b), 8);                       // the group's expansion set and the staging warps, 4 each
       g_mbar_init(mmab(b), 1);
       g_mbar_init(freeb(b), 4);                       // the group's fold set
     }
@@ -336,31 +356,28 @@ __global__ void __launch_bounds__(kGThreads, 1) proj_kernel(const __grid_constan
     return;
   }
 
-  if (warp == kMmaWarp) {
-    // MMA issuer: per group, once its operands are in place, 4 MMAs of K = 32 into the group's accumulator,
+  if (warp >= kMmaWarp0) {
+    // MMA issuers: per group, once its operands are in place, 4 MMAs of K = 32 into the group's accumulator,
     // committed to the buffer's MMA barrier (the fold set waits on it)
     if (lane == 0) {
+      const unsigned m = (unsigned)(warp - kMmaWarp0);
       unsigned gc = 0;
       for (int w = blockIdx.x; w < nitems; w += gridDim.x)
         for (int g = 0; g < G; ++g, ++gc) {
+          if (gc % kMmaWarps != m) continue;
           const int b = buf(gc);
-          g_mbar_wait(ready(b), par(gc), p.err);
+          g_mbar_spin(ready(b), par(gc), p.err);
           tc_after();
-          const uint32_t b0 = s_u32(bbuf + b * kBBytes);
-          const uint32_t dt = tacc + (uint32_t)(b * kDcols);
+          const uint64_t bd = kmajor_desc(s_u32(bbuf + b * kBBytes));
+          const uint32_t at = tmem + (uint32_t)(b * kAcols), dt = tacc + (uint32_t)(b * kDcols);
+          asm volatile("tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, 0;\n" ::"r"(dt), "r"(at), "l"(bd),
+                       "r"(kIdesc)
+                       : "memory");
 #pragma unroll
-          for (int k32 = 0; k32 < kGroup / 32; ++k32) {
-            const uint32_t at = tmem + (uint32_t)(b * kAcols + k32 * 8);
-            const uint64_t bd = kmajor_desc(b0 + k32 * 1024);
-            if (k32 == 0)
-              asm volatile("tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, 0;\n" ::"r"(dt), "r"(at), "l"(bd),
-                           "r"(kIdesc)
-                           : "memory");
-            else
-              asm volatile("tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, 1;\n" ::"r"(dt), "r"(at), "l"(bd),
-                           "r"(kIdesc)
-                           : "memory");
-          }
+          for (int k32 = 1; k32 < kGroup / 32; ++k32)   // K slice k32: 8 TMEM columns, 1024 B of B (64 descriptor units)
+            asm volatile("tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, 1;\n" ::"r"(dt), "r"(at + 8u * k32),
+                         "l"(bd + 64ull * k32), "r"(kIdesc)
+                         : "memory");
           asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(mmab(b))
                        : "memory");
         }
@@ -441,45 +458,55 @@ __global__ void __launch_bounds__(kGThreads, 1) proj_kernel(const __grid_constan
       fold_sync2();                                     // set 0 has read the exchange before set 1 writes again
     }
   } else if (warp >= kStgWarp0) {
-    // ---------------------------------------------------------------- staging sets: the B operand
-    // thread: routed row bn of the group (B rows bn and kGN + bn), 16-value word bs of each group
-    const int set = (warp - kStgWarp0) >> 2;
-    const int r = tid - 32 * (kStgWarp0 + 4 * set);
+    // ---------------------------------------------------------------- staging warps: the B operand
+    // thread: routed row bn of the group (B rows bn and kGN + bn), 16-value word bs of each group; the table
+    // pieces of the next two groups are in flight while a group is stored
+    const int r = tid - 32 * kStgWarp0;
     const int bn = r >> 3, bs = r & 7;
     unsigned gc0 = 0;
+    struct Piece { uint4 h, l; float e; int s; };
     for (int w = blockIdx.x; w < nitems; w += gridDim.x, gc0 += (unsigned)G) {
       const int gi = w / ntiles;
       const int g0 = rv.gstart()[gi], cnt = rv.gcnt()[gi];
       const int trow = bn < cnt ? rv.order()[g0 + bn] / p.act_row_div : -1;   // table row, -1 = padding
-      const int gfirst = (int)(((unsigned)set + kSets - gc0 % kSets) % kSets);
-      uint4 ph = make_uint4(0, 0, 0, 0), pl = ph;
-      float e = 0.f;
-      int sx = 0;
-      auto fetch = [&](int g) {
+      auto fetch = [&](int g, Piece& pc) {
+        pc.h = pc.l = make_uint4(0, 0, 0, 0);
+        pc.e = 0.f;
+        pc.s = 0;
+        if (trow < 0 || g >= G) return;
         const unsigned char* src = p.tab + ((size_t)trow * G + g) * 256 + bs * 16;
-        ph = *reinterpret_cast<const uint4*>(src);
-        pl = *reinterpret_cast<const uint4*>(src + 128);
+        pc.h = *reinterpret_cast<const uint4*>(src);
+        pc.l = *reinterpret_cast<const uint4*>(src + 128);
         if (bs == 0) {
-          e = p.xe[(size_t)trow * G + g];
-          sx = p.xs[(size_t)trow * G + g];
+          pc.e = p.xe[(size_t)trow * G + g];
+          pc.s = p.xs[(size_t)trow * G + g];
         }
       };
-      if (trow >= 0 && gfirst < G) fetch(gfirst);
-      for (int g = gfirst; g < G; g += kSets) {
+      auto store = [&](int g, const Piece& pc) {
         const unsigned gc = gc0 + (unsigned)g;
         const int b = buf(gc);
         if (gc >= kNB) g_mbar_wait(freeb(b), par(gc - kNB), p.err);   // buffer b's previous group is folded
         unsigned char* B = bbuf + b * kBBytes + (bs >> 1) * 1024;
-        *reinterpret_cast<uint4*>(B + canon_off(bn, bs & 1)) = ph;
-        *reinterpret_cast<uint4*>(B + canon_off(kGN + bn, bs & 1)) = pl;
+        *reinterpret_cast<uint4*>(B + canon_off(bn, bs & 1)) = pc.h;
+        *reinterpret_cast<uint4*>(B + canon_off(kGN + bn, bs & 1)) = pc.l;
         if (bs == 0) {
-          xe_of(b)[bn] = e;
-          xs_of(b)[bn] = sx;
+          xe_of(b)[bn] = pc.e;
+          xs_of(b)[bn] = pc.s;
         }
-        if (trow >= 0 && g + kSets < G) fetch(g + kSets);   // this set's next group of the item
         asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");   // generic writes -> the MMA's reads
         __syncwarp();
         if (lane == 0) g_mbar_arrive(ready(b));
+      };
+      Piece pa, pb;
+      fetch(0, pa);
+      fetch(1, pb);
+      for (int g = 0; g < G; g += 2) {
+        store(g, pa);
+        fetch(g + 2, pa);
+        if (g + 1 < G) {
+          store(g + 1, pb);
+          fetch(g + 3, pb);
+        }
       }
     }
   } else {
