@@ -905,9 +905,21 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
     if (pt < 6 && (p.map13.has_zeros || (pt != 2 && pt != 5)))
       asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&p.tm[pt])) : "memory");
   }
+  // The slot table, staged into shared memory while the previous kernel may still be finishing: the kernels
+  // that let this one start early (this library's layer, INT8 and all-reduce kernels, which trigger their
+  // dependents before they end) never write a slot table, and any other kernel -- or a copy -- that writes
+  // one has completed before this kernel starts.
+  const bool one_warp = g.R <= 32;
+  int* sltab = reinterpret_cast<int*>(smem + p.off_slots);    // staged slot table (g.stab entries)
+  if (one_warp && g.stab > 0) {
+    if (warp == 0) stage_slots(sltab, p.map13.slots, g.stab, lane);
+    if (kTma && warp >= kWarps && private_routing(g))
+      stage_slots(reinterpret_cast<int*>(smem + p.off_preg) + (warp - kWarps) * preg_ints(g) + 128, p.map13.slots,
+                  g.stab, lane);
+  }
   // Launched with programmatic stream serialisation, this CTA may start while the previous kernel of the
-  // stream is finishing: everything above touches only shared memory and the kernel's own parameters;
-  // from here on it reads what earlier work wrote (routing, activations, workspace, weights).
+  // stream is finishing: everything above touches only shared memory, the kernel's own parameters and the
+  // slot table; from here on it reads what earlier work wrote (routing, activations, workspace, weights).
   asm volatile("griddepcontrol.wait;\n" ::: "memory");
 
   // the barrier generation of this call (read at entry; the count reaches it before any CTA of this call
@@ -921,8 +933,6 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
   unsigned* livebits = reinterpret_cast<unsigned*>(slotrow + g.max_units * g.top_k);
   // Routing first: expert bases of every routed row, resolved once per CTA -- by warp 0 alone when the
   // rows fit one warp (it compacts them right after, with no CTA barrier in between), else by every thread.
-  const bool one_warp = g.R <= 32;
-  int* sltab = reinterpret_cast<int*>(smem + p.off_slots);    // staged slot table (g.stab entries)
   auto resolve_row = [&](int r, int e, float wt, bool staged) {
     RowPtr rp;
     rp.wt = wt;
@@ -942,11 +952,10 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
     rows[r] = rp;
   };
   if (one_warp) {
-    // warp 0: the routing and the whole slot table in one round of loads, then lookups in shared memory
+    // warp 0: the routing in one round of loads, then lookups in the staged slot table
     if (warp == 0) {
       const int e = lane < g.R ? p.ids[lane] : -1;
       const float wt = lane < g.R ? p.topk_w[lane] : 0.f;
-      stage_slots(sltab, p.map13.slots, g.stab, lane);
       __syncwarp();
       if (lane < g.R) resolve_row(lane, e, wt, g.stab > 0);
     }
@@ -1051,15 +1060,15 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
     const int pw = warp - kWarps;
     if (private_routing(g)) {
       // This warp's own copy of the routing, by the rules warp 0 applies for the reducing warps (the same
-      // live rows in the same order): ids and slot table in one round of loads, ballot compaction.
+      // live rows in the same order): the ids in one round of loads, lookups in its staged slot table,
+      // ballot compaction.
       int* reg = reinterpret_cast<int*>(smem + p.off_preg) + pw * preg_ints(g);
       int* pslot = reg;
       int* prow = reg + 32;
       int* ptokrow = reg + 64;
       int* ptokcnt = reg + 96;
       int* pstab = reg + 128;
-      const int e = lane < g.R ? p.ids[lane] : -1;
-      stage_slots(pstab, p.map13.slots, g.stab, lane);
+      const int e = lane < g.R ? p.ids[lane] : -1;      // (the slot table was staged before the wait)
       __syncwarp();
       const bool in = lane < g.R && e >= 0 && e < p.map13.E;
       const int sl = in ? pstab[e] : -1;
