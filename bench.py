@@ -247,12 +247,26 @@ def _run_stack(args, world: int, rank: int, dev: torch.device):
         y = pkg.moe_decode_layer(x, ids_d[i, l], w_d[i, l], arenas[l], out=out if ar is None else None)
         return ar(y) if ar is not None else y
 
-    def step(i, with_dense=False, x0=None):
+    def step_unfused(i, with_dense=False, x0=None):
         x = x_d[i] if x0 is None else x0
         for l in range(L):
             y = moe(x, l, i, bufs[l & 1])
             x = pkg.int8_gemv(y, dense[l][0], dense[l][1]) if with_dense else y
         return x
+
+    def step(i, with_dense=False, x0=None):
+        """N=1: each layer writes into the next one's input buffer. N>1: the exchange folded into the kernels --
+        every layer pushes its partial into every rank's buffer and the next layer (or the INT8 projection) sums
+        the ranks' partials while it converts its activation; one all-reduce closes the step without the dense."""
+        x = x_d[i] if x0 is None else x0
+        if ar is None:
+            return step_unfused(i, with_dense, x)
+        if with_dense:
+            for l in range(L):
+                ar.layer(x, ids_d[i, l], w_d[i, l], arenas[l], y_to_peers=True)
+                x = ar.int8(dense[l][0], dense[l][1], M, out=bufs[l & 1])
+            return x
+        return ep.ep_stack_step(ar, x, ids_d[i], w_d[i], arenas, out=bufs[0])
 
     # correctness of one layer of the stack: GPU output vs the fp32 oracle (partials all-reduced over ranks)
     y0 = moe(x_d[0], 0, 0, bufs[0])
@@ -260,6 +274,14 @@ def _run_stack(args, world: int, rank: int, dev: torch.device):
     if world > 1:
         dist.all_reduce(ref)
     err = O.max_rel_err(y0.float().cpu(), ref.cpu())
+    fused_same = None
+    if ar is not None:                       # the folded exchange against (layer, all-reduce) per layer, bit for bit
+        a0 = step_unfused(0).clone()
+        b0 = step(0).clone()
+        a1 = step_unfused(1, True).clone()
+        b1 = step(1, True).clone()
+        torch.cuda.synchronize()
+        fused_same = bool(torch.equal(a0, b0) and torch.equal(a1, b1))
 
     for i in range(max(args.warmup, 3)):
         step(i % P)
@@ -305,9 +327,11 @@ def _run_stack(args, world: int, rank: int, dev: torch.device):
         x_in.copy_(xh[i], non_blocking=True)
         r_in.copy_(rh[i], non_blocking=True)
         x = x_in
-        for l in range(L):
-            y = pkg.moe_decode_layer(x, ids_in[l], w_in[l], arenas[l], out=bufs[l & 1] if ar is None else None)
-            x = ar(y) if ar is not None else y
+        if ar is None:
+            for l in range(L):
+                x = pkg.moe_decode_layer(x, ids_in[l], w_in[l], arenas[l], out=bufs[l & 1])
+        else:
+            x = ep.ep_stack_step(ar, x, ids_in, w_in, arenas, out=bufs[0])
         out_h[i].copy_(x, non_blocking=True)
 
     ge = capture(e2e_step, P)
@@ -350,7 +374,7 @@ def _run_stack(args, world: int, rank: int, dev: torch.device):
         "config": {"workload": f"config4 stack of {L} MoE layers, each config 1 (M=1 H=4096 I=1536 E=256 top-8 "
                                f"W2A16 g128 zp f16 scales), experts {E // world} per GPU",
                    "global_batch": M, "seq_len": 1,
-                   "parallelism": "single GPU" if world == 1 else f"ep{world} (peer-memory all-reduce per layer)",
+                   "parallelism": "single GPU" if world == 1 else f"ep{world} (exchange folded into the layer kernels)",
                    "l2": f"inputs larger than L2 ({(hi - lo) * L} local experts, {bpl * L * world // 2**20} MB of "
                          "routed weights per step; no expert reused within 4 layers)",
                    "layers": L, "graph_steps": P},
@@ -362,7 +386,7 @@ def _run_stack(args, world: int, rank: int, dev: torch.device):
                      "frac": round(per_gpu / peak, 4), "traffic": measured_traffic("fused_layer_config1"),
                      "kernel": "fused_layer_kernel (gate_up+SiLU*mul, grid barrier, down+weighted top-k sum): one "
                                "cooperative launch per layer; achieved = algorithmic layer bytes / device time per "
-                               "layer" + ("" if world == 1 else " / N GPUs (includes the all-reduce)"),
+                               "layer" + ("" if world == 1 else " / N GPUs (includes the exchange)"),
                      "peak_kind": peak_kind},
         "e2e": {"value": round(bpl * L / (e2e_us_step * 1e-6) / 1e9, 1), "unit": "GB/s",
                 "us_per_layer": round(e2e_us_step / L, 3), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
@@ -373,7 +397,7 @@ def _run_stack(args, world: int, rank: int, dev: torch.device):
                        "gbs": round((bpl + (H // 4) * H * 4 + H * 2) * L / (us_step_dense * 1e-6) / 1e9, 1),
                        "what": "config 4 step: every MoE layer followed by the INT8 dense [4096 -> 4096] GEMV "
                                "(replicated on every rank)"},
-        "gpu_launches": steps * L * (1 if world == 1 else 2),
+        "gpu_launches": steps * L if world == 1 else steps * (L + 1),
         "clocks": clk.summary(),
         "check_max_rel_err": err,
         "setup_s": round(setup_s, 1),
@@ -381,8 +405,10 @@ def _run_stack(args, world: int, rank: int, dev: torch.device):
     if cpu:
         line["cpu_baseline"] = cpu
     if ar is not None:
-        line["allreduce"] = {"impl": "w2a16_allreduce_peers_bf16 (one-shot over NVLink peer memory)",
-                             "device_error": ar_flag}
+        line["exchange"] = {"impl": "folded into the layer kernels (w2a16_moe_decode_layer_slots_ep: partials pushed "
+                                    "into every rank's buffer over NVLink, summed by the next layer / projection), "
+                                    "one w2a16_allreduce_peers_bf16 closing the step",
+                            "equals_layer_allreduce_bit_for_bit": fused_same, "device_error": ar_flag}
     print(json.dumps(line), flush=True)
 
 

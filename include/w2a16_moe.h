@@ -253,6 +253,50 @@ int w2a16_allreduce_peers_bf16(const void* in, void* out, int n, int n_max, cons
                                unsigned int spin_limit, void* stream);
 
 /*
+ * Exchange channel of an expert-parallel step. Each rank's peer-visible buffer holds, at tag_offset bytes (a
+ * multiple of 16), 2 parity slots x world rows x n_max / 2 tagged 8-byte words: word j of row r carries values 2j
+ * and 2j + 1 (bf16, low 32 bits) of rank r's partial of a call with that parity and the call number (high 32
+ * bits), written and read as one single-copy-atomic access, so a reader polls the words it needs until they hold
+ * its call -- no fences, counters or flags. Call e uses parity slot e & 1; epoch (device word, zero at the start)
+ * counts the channel's calls on this rank. The same buffer and epoch word may serve w2a16_allreduce_peers_bf16
+ * (its bf16 slots and flags below tag_offset), so a step can mix the calls.
+ */
+typedef struct w2a16_exchange {
+  const uint64_t* peer_bufs;   /* device array [world] of the peer buffer addresses */
+  size_t tag_offset;
+  int n_max, rank, world;
+  unsigned int* epoch;
+  unsigned int spin_limit;     /* polls of a word before a wait gives up (bit 1 of err); 0 = library default */
+} w2a16_exchange;
+
+/* The slot-form decode layer of one expert-parallel rank with the exchange folded in (M * H <= n_max, one
+ * per-token launch; no counterpart in the reference, which runs on one GPU). x_from_peers: x is not read; the
+ * layer's activation is the sum, in rank order (fp32, rounded to bf16), of the ranks' rows of the channel's call
+ * e = *epoch -- the all-reduce of the previous layer's partials, each word taken once it holds call e.
+ * y_to_peers: y is not written; the layer's partial goes out as this rank's tagged row of call e + 1 into every
+ * rank's buffer as its 32-column units finish, and *epoch becomes e + 1. With both, one launch per layer replaces
+ * (layer, all-reduce). Other arguments as w2a16_moe_decode_layer_slots. */
+int w2a16_moe_decode_layer_slots_ep(const void* x, int M, int H, int I, int top_k,
+                                    const int32_t* topk_ids, const float* topk_w,
+                                    const int32_t* slots, int num_experts, int num_slots,
+                                    const void* codes13, int64_t codes13_slot_bytes,
+                                    const void* scales13, int64_t scales13_slot_bytes,
+                                    const void* zeros13, int64_t zeros13_slot_bytes,
+                                    const void* codes2, int64_t codes2_slot_bytes,
+                                    const void* scales2, int64_t scales2_slot_bytes,
+                                    const void* zeros2, int64_t zeros2_slot_bytes,
+                                    int scale_bf16, float routed_scaling_factor,
+                                    void* y, void* workspace, size_t workspace_bytes,
+                                    int x_from_peers, int y_to_peers, const w2a16_exchange* exchange,
+                                    unsigned int* err, void* stream);
+
+/* w2a16_int8_gemv with x the sum of the ranks' tagged rows of the channel's call *epoch (rows of K values,
+ * M * K <= n_max): the dense projection after a pushing layer. */
+int w2a16_int8_gemv_from_peers(const w2a16_exchange* exchange, const int32_t* qweight, const void* scales, int group,
+                               int zero, int M, int K, int N, void* y, int64_t stride_ym, unsigned int* err,
+                               void* stream);
+
+/*
  * Native row arena for expert residency. Replaces RowArena (gemv/row_arena.py:34-123) and the virtual-memory
  * plumbing it borrows from SGLang: virtual addresses for max_rows rows of row_bytes are reserved once, and a
  * prefix of them is backed by physical memory in chunks (the device granularity rounds chunk_bytes up; 0 picks

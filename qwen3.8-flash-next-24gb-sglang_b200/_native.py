@@ -44,6 +44,12 @@ SIGNATURES = {
                                                 c_vp, c_i64, c_vp, c_i64, c_vp, c_i64,
                                                 c_vp, c_i64, c_vp, c_i64, c_vp, c_i64,
                                                 c_i32, c_f32, c_vp, c_vp, c_sz, c_i32, c_vp, c_vp]),
+    "w2a16_moe_decode_layer_slots_ep": (c_i32, [c_vp, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp, c_vp, c_i32, c_i32,
+                                                c_vp, c_i64, c_vp, c_i64, c_vp, c_i64,
+                                                c_vp, c_i64, c_vp, c_i64, c_vp, c_i64,
+                                                c_i32, c_f32, c_vp, c_vp, c_sz, c_i32, c_i32, c_vp, c_vp, c_vp]),
+    "w2a16_int8_gemv_from_peers": (c_i32, [c_vp, c_vp, c_vp, c_i32, c_i32, c_i32, c_i32, c_i32, c_vp, c_i64, c_vp,
+                                           c_vp]),
     "w2a16_moe_decode_layer_slots_noalloc": (c_i32, [c_vp, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp, c_vp, c_i32, c_i32,
                                                      c_vp, c_i64, c_vp, c_i64, c_vp, c_i64,
                                                      c_vp, c_i64, c_vp, c_i64, c_vp, c_i64,
@@ -64,6 +70,19 @@ SIGNATURES = {
     "w2a16_arena_chunk_bytes": (c_i64, [c_vp]),
     "w2a16_arena_destroy": (c_i32, [c_vp]),
 }
+
+
+class Exchange(ctypes.Structure):
+    """w2a16_exchange of include/w2a16_moe.h (an expert-parallel exchange channel)."""
+    _fields_ = [
+        ("peer_bufs", c_vp),
+        ("tag_offset", c_sz),
+        ("n_max", c_i32),
+        ("rank", c_i32),
+        ("world", c_i32),
+        ("epoch", c_vp),
+        ("spin_limit", ctypes.c_uint),
+    ]
 
 
 class VmmDriver(ctypes.Structure):

@@ -148,6 +148,47 @@ int w2a16_moe_decode_layer_slots_ex(const void* x, int M, int H, int I, int top_
   return decode_layer_fused(a);
 }
 
+namespace {
+PeerExchange exchange_of(const w2a16_exchange& e) {
+  PeerExchange x{};
+  x.peers = e.peer_bufs; x.tag_off = e.tag_offset; x.n_max = e.n_max; x.rank = e.rank; x.world = e.world;
+  x.epoch = e.epoch; x.spin_limit = e.spin_limit;
+  return x;
+}
+}  // namespace
+
+int w2a16_moe_decode_layer_slots_ep(const void* x, int M, int H, int I, int top_k, const int32_t* topk_ids,
+                                    const float* topk_w, const int32_t* slots, int num_experts, int num_slots,
+                                    const void* codes13, int64_t codes13_slot_bytes, const void* scales13,
+                                    int64_t scales13_slot_bytes, const void* zeros13, int64_t zeros13_slot_bytes,
+                                    const void* codes2, int64_t codes2_slot_bytes, const void* scales2,
+                                    int64_t scales2_slot_bytes, const void* zeros2, int64_t zeros2_slot_bytes,
+                                    int scale_bf16, float routed_scaling_factor, void* y, void* workspace,
+                                    size_t workspace_bytes, int x_from_peers, int y_to_peers,
+                                    const w2a16_exchange* exchange, unsigned int* err, void* stream) {
+  if (!slots || num_experts <= 0 || num_slots <= 0 || !codes13 || !scales13 || !codes2 || !scales2)
+    return W2A16_ERR_ARG;
+  if ((x_from_peers || y_to_peers) && !exchange) return W2A16_ERR_ARG;
+  if ((zeros13 == nullptr) != (zeros2 == nullptr)) return W2A16_ERR_ARG;
+  if (!a16(codes13) || !a16(scales13) || !a16(codes2) || !a16(scales2)) return W2A16_ERR_ALIGN;
+  if (codes13_slot_bytes % 16 || scales13_slot_bytes % 16 || codes2_slot_bytes % 16 || scales2_slot_bytes % 16)
+    return W2A16_ERR_ALIGN;
+  if (zeros13 && (!a16(zeros13) || !a16(zeros2) || zeros13_slot_bytes % 16 || zeros2_slot_bytes % 16))
+    return W2A16_ERR_ALIGN;
+  const PeerExchange ex = exchange ? exchange_of(*exchange) : PeerExchange{};
+  LayerArgs a{};
+  a.x = x_from_peers ? nullptr : x; a.M = M; a.H = H; a.I = I; a.top_k = top_k; a.ids = topk_ids; a.topk_w = topk_w;
+  a.map13 = slot_map(slots, num_experts, num_slots, codes13, codes13_slot_bytes, scales13, scales13_slot_bytes,
+                     zeros13, zeros13_slot_bytes);
+  a.map2 = slot_map(slots, num_experts, num_slots, codes2, codes2_slot_bytes, scales2, scales2_slot_bytes, zeros2,
+                    zeros2_slot_bytes);
+  a.scale_bf16 = scale_bf16; a.routed_scaling = routed_scaling_factor; a.y = y_to_peers ? nullptr : y;
+  a.workspace = workspace; a.workspace_bytes = workspace_bytes; a.err = err; a.stream = as_stream(stream);
+  a.xin = x_from_peers ? &ex : nullptr;
+  a.yout = y_to_peers ? &ex : nullptr;
+  return decode_layer_fused(a);                 // an exchange call is one per-token launch
+}
+
 int w2a16_moe_decode_layer_slots(const void* x, int M, int H, int I, int top_k, const int32_t* topk_ids,
                                  const float* topk_w, const int32_t* slots, int num_experts, int num_slots,
                                  const void* codes13, int64_t codes13_slot_bytes, const void* scales13,
@@ -187,6 +228,16 @@ int w2a16_int8_gemv(const void* x, int64_t stride_xm, const int32_t* qweight, co
   a.x = x; a.stride_xm = stride_xm; a.qweight = qweight; a.scales = scales; a.group = group; a.zero = zero;
   a.M = M; a.K = K; a.N = N; a.y = y; a.stride_ym = stride_ym; a.stream = as_stream(stream);
   return int8_gemv(a, workspace, workspace_bytes);
+}
+
+int w2a16_int8_gemv_from_peers(const w2a16_exchange* exchange, const int32_t* qweight, const void* scales, int group,
+                               int zero, int M, int K, int N, void* y, int64_t stride_ym, unsigned int* err,
+                               void* stream) {
+  if (!exchange) return W2A16_ERR_ARG;
+  Int8Args a{};
+  a.x = nullptr; a.stride_xm = K; a.qweight = qweight; a.scales = scales; a.group = group; a.zero = zero;
+  a.M = M; a.K = K; a.N = N; a.y = y; a.stride_ym = stride_ym; a.stream = as_stream(stream);
+  return int8_gemv_from_peers(a, exchange_of(*exchange), err);
 }
 
 }  // extern "C"

@@ -47,6 +47,48 @@ __device__ __forceinline__ void flag_error(unsigned* err, unsigned bit) {
   if (err) atomicOr(err, bit);
 }
 
+// ----------------------------------------------------------------------------- peer exchange (expert parallelism)
+constexpr unsigned kPeerSpinLimit = 1u << 22;   // default polls before a peer flag wait gives up
+
+__device__ __forceinline__ unsigned ld_acquire_sys_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys_u32(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_relaxed_gpu_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Tagged exchange words: (call << 32) | (two bf16 values), written and read as one 8-byte access each.
+__device__ __forceinline__ void st_tagged(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;\n" ::"l"(p), "l"(v) : "memory");
+}
+// The data of word w of call e, once it holds that call. `budget` is the calling thread's poll allowance for all
+// the words it reads (bounded: when it runs out, bit 1 of err and the stale data -- every later word is then
+// looked at once). A writer stores call e + 2 into the same word only after this rank has finished reading call e.
+__device__ __forceinline__ uint32_t wait_tagged(const unsigned long long* w, unsigned e, unsigned& budget,
+                                                unsigned* err) {
+  unsigned long long v;
+  for (;;) {
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];\n" : "=l"(v) : "l"(w) : "memory");
+    if ((unsigned)(v >> 32) == e) break;
+    if (budget == 0) {
+      flag_error(err, 2u);
+      break;
+    }
+    --budget;
+  }
+  return (uint32_t)v;
+}
+// bf16 pair -> two floats
+__device__ __forceinline__ float2 bf16x2_to_float2(uint32_t u) {
+  return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xFFFF0000u));
+}
+
 // ----------------------------------------------------------------------------- integer dot products
 __device__ __forceinline__ int dp2a_lo(uint32_t a16x2, uint32_t b8x4, int c) {
   int d;

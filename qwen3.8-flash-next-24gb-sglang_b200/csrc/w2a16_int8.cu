@@ -32,9 +32,15 @@ struct I8Params {
   const int32_t* qw; const __half* scales; int group; int zero;
   int M, K, N, slice;
   __nv_bfloat16* y; int64_t stride_ym;
+  // expert parallelism: x = the sum of the ranks' tagged rows of the exchange channel's call *xepoch (rows of
+  // K values) in this rank's buffer, each word used once it holds that call
+  const uint64_t* xpeers; size_t xtag_off; unsigned* xepoch;
+  int xrank, xworld, xn_max; unsigned xspin; unsigned* err;
 };
 }  // namespace
 
+// kPeers: x from the exchange channel; the plain variant carries none of it.
+template <bool kPeers>
 __global__ void __launch_bounds__(256) int8_gemv_kernel(I8Params p) {
   __shared__ __align__(16) int16_t xq[kTokPerCta][kMaxSlice];
   __shared__ int xsum_q[kTokPerCta][kMaxSlice / 32];
@@ -75,6 +81,13 @@ __global__ void __launch_bounds__(256) int8_gemv_kernel(I8Params p) {
   };
   load(0);
   asm volatile("griddepcontrol.wait;\n" ::: "memory");
+  const unsigned long long* xsum = nullptr;
+  unsigned e_in = 0, budget = p.xspin;
+  if (kPeers) {
+    e_in = ld_relaxed_gpu_u32(p.xepoch);
+    xsum = reinterpret_cast<const unsigned long long*>(p.xpeers[p.xrank] + p.xtag_off) +
+           (size_t)(e_in & 1u) * p.xworld * (p.xn_max / 2);
+  }
 
   // activation prep: one warp per (token, 128-wide x-group) of the slice
   const int ng = p.slice / 128;
@@ -82,10 +95,24 @@ __global__ void __launch_bounds__(256) int8_gemv_kernel(I8Params p) {
     const int m = t / ng, xg = t - m * ng;
     const int kb = k0 + xg * 128;
     if (kb >= p.K) continue;
-    const __nv_bfloat16* src = p.x + (int64_t)(m0 + m) * p.stride_xm + kb;
     float v[4];
+    if (!kPeers) {
+      const __nv_bfloat16* src = p.x + (int64_t)(m0 + m) * p.stride_xm + kb;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) v[i] = __bfloat162float(src[4 * lane + i]);
+      for (int i = 0; i < 4; ++i) v[i] = __bfloat162float(src[4 * lane + i]);
+    } else {
+      // the ranks' rows in rank order, summed in fp32 and rounded to bf16 as the all-reduce does
+      const size_t w0 = ((size_t)(m0 + m) * p.K + kb + 4 * lane) / 2;
+      float s[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int r = 0; r < p.xworld; ++r) {
+        const unsigned long long* row = xsum + (size_t)r * (p.xn_max / 2) + w0;
+        const float2 a0 = bf16x2_to_float2(wait_tagged(row, e_in, budget, p.err));
+        const float2 a1 = bf16x2_to_float2(wait_tagged(row + 1, e_in, budget, p.err));
+        s[0] += a0.x; s[1] += a0.y; s[2] += a1.x; s[3] += a1.y;
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v[i] = __bfloat162float(__float2bfloat16(s[i]));
+    }
     float mx = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
     mx = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(mx)));
     const int E = (mx > 0.f ? frexp_exponent(mx) : 0) - 15;
@@ -176,12 +203,15 @@ size_t int8_workspace_bytes(int M, int K, int N) {
   return 256;
 }
 
-int int8_gemv(const Int8Args& a, void* workspace, size_t workspace_bytes) {
-  (void)workspace; (void)workspace_bytes;
+namespace {
+int launch_int8(const Int8Args& a, const PeerExchange* xin, unsigned* err) {
   if (a.M <= 0) return kOk;
   if (a.K <= 0 || a.K % 128 != 0 || a.N <= 0 || a.N % 4 != 0) return kErrShape;
   if (a.group <= 0 || a.group % 128 != 0 || a.K % a.group != 0) return kErrShape;
-  if (!a.x || !a.qweight || !a.scales || !a.y) return kErrArg;
+  if ((!a.x && !xin) || !a.qweight || !a.scales || !a.y) return kErrArg;
+  if (xin && (!xin->peers || !xin->epoch || xin->world <= 0 || xin->rank < 0 || xin->rank >= xin->world ||
+              xin->n_max % 8 || (size_t)a.M * a.K > (size_t)xin->n_max || xin->tag_off % 16))
+    return kErrArg;
   if ((reinterpret_cast<uintptr_t>(a.qweight) & 15u)) return kErrAlign;
   // S slices of a multiple of 256 k each (at most kMaxSlice), one cluster of S CTAs per column block
   int S = (a.K + 255) / 256;
@@ -194,6 +224,16 @@ int int8_gemv(const Int8Args& a, void* workspace, size_t workspace_bytes) {
   p.qw = a.qweight; p.scales = static_cast<const __half*>(a.scales); p.group = a.group; p.zero = a.zero;
   p.M = a.M; p.K = a.K; p.N = a.N; p.slice = slice;
   p.y = static_cast<__nv_bfloat16*>(a.y); p.stride_ym = a.stride_ym;
+  if (xin) {
+    p.xpeers = xin->peers;
+    p.xtag_off = xin->tag_off;
+    p.xrank = xin->rank;
+    p.xepoch = xin->epoch;
+    p.xworld = xin->world;
+    p.xn_max = xin->n_max;
+    p.xspin = xin->spin_limit ? xin->spin_limit : kPeerSpinLimit;
+    p.err = err;
+  }
   const int ncb = (a.N + 127) / 128, nz = (a.M + kTokPerCta - 1) / kTokPerCta;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(ncb, S, nz);
@@ -208,7 +248,18 @@ int int8_gemv(const Int8Args& a, void* workspace, size_t workspace_bytes) {
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  return cudaLaunchKernelEx(&cfg, int8_gemv_kernel, p) == cudaSuccess ? kOk : kErrLaunch;
+  return cudaLaunchKernelEx(&cfg, xin ? int8_gemv_kernel<true> : int8_gemv_kernel<false>, p) == cudaSuccess
+             ? kOk : kErrLaunch;
+}
+}  // namespace
+
+int int8_gemv(const Int8Args& a, void* workspace, size_t workspace_bytes) {
+  (void)workspace; (void)workspace_bytes;
+  return launch_int8(a, nullptr, nullptr);
+}
+
+int int8_gemv_from_peers(const Int8Args& a, const PeerExchange& xin, unsigned* err) {
+  return launch_int8(a, &xin, err);
 }
 
 }  // namespace w2a16

@@ -25,6 +25,19 @@ struct GemvArgs {
 
 int gemv_plain(const GemvArgs& g);
 
+// Exchange channel between the ranks of an expert-parallel step: every rank's peer-visible buffer holds, at
+// tag_off bytes, 2 parity slots x world rows x n_max / 2 tagged words -- word j of row r carries values 2j and
+// 2j + 1 (bf16) of rank r's partial of a call with that parity in its low 32 bits and the call number in its high
+// 32 bits (one single-copy-atomic 8-byte store, so a reader that sees the call number sees the data). Call e
+// uses slot e & 1; *epoch counts the channel's calls on this rank.
+struct PeerExchange {
+  const uint64_t* peers;  // device array [world] of the peer buffer addresses
+  size_t tag_off;
+  int n_max, rank, world;
+  unsigned* epoch;        // calls made on this channel (device word)
+  unsigned spin_limit;    // polls of a word before a wait gives up (0: the library default)
+};
+
 // Fused persistent decode layer (w2a16_layer.cu).
 struct LayerArgs {
   const void* x;          // bf16 [M, H]
@@ -40,6 +53,10 @@ struct LayerArgs {
   size_t workspace_bytes;
   unsigned* err;
   cudaStream_t stream;
+  // expert parallelism: x = the sum of the ranks' rows of the channel's call *epoch (instead of x), and/or this
+  // layer's partial pushed as this rank's row of call *epoch + 1 (instead of y)
+  const PeerExchange* xin = nullptr;
+  const PeerExchange* yout = nullptr;
 };
 size_t layer_workspace_bytes(int M, int H, int I, int top_k);
 int decode_layer_fused(const LayerArgs& a);
@@ -72,6 +89,8 @@ struct Int8Args {
   cudaStream_t stream;
 };
 int int8_gemv(const Int8Args& a, void* workspace, size_t workspace_bytes);
+// The same with x the sum of the ranks' rows of the channel's call *epoch (M * K <= n_max).
+int int8_gemv_from_peers(const Int8Args& a, const PeerExchange& xin, unsigned* err);
 size_t int8_workspace_bytes(int M, int K, int N);
 int to_word_ncontig(const void* src, void* dst, int E, int N, int K, cudaStream_t stream);
 int gather_rows_tab(const int64_t* tab, const int32_t* ids, int n, void* out, int64_t row_bytes, cudaStream_t stream);

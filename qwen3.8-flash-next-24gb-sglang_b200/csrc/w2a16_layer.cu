@@ -178,6 +178,15 @@ struct FusedParams {
   // publishes for the tail of the h-block it shares with the previous CTA
   unsigned long long* hand;
   unsigned* err;
+  // expert parallelism (a PeerExchange channel): xin -- x is the sum of the ranks' rows of the channel's call
+  // e = *xepoch; yout -- this layer's partial y goes out as this rank's tagged row of call e + 1 into every
+  // rank's buffer, and CTA 0 stores *xepoch = e + 1 when it is done
+  int xin, yout;
+  const uint64_t* xpeers;
+  size_t xtag_off;
+  int xn_max, xrank, xworld;
+  unsigned* xepoch;
+  unsigned xspin;
 };
 
 // Activation table of a K-long row: one exponent per 128-value group (gate_up, from x) ...
@@ -877,7 +886,8 @@ __device__ __forceinline__ void unit_tables(const FusedParams& p, const LiveRows
 
 // kTma = false: register mode (any expert map), 512 threads; every lane loads its item data itself.
 // kTma = true: copy-engine mode (slot arenas), 512 reducing threads + one producer warp.
-template <bool kTma>
+// kEx: the expert-parallel exchange variant (p.xin / p.yout honoured); the plain variant carries none of it.
+template <bool kTma, bool kEx>
 __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_kernel(const __grid_constant__ FusedParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
   const Geo& g = p.geo;
@@ -926,6 +936,9 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
   // can pass the barrier). The previous call stored it before it ended, so stream order alone makes it
   // visible: a relaxed load, which -- unlike an acquire -- does not hold back this thread's routing loads.
   const unsigned gen_entry = threadIdx.x == 0 ? ld_relaxed_u32(p.bar_gen) : 0u;
+  // expert parallelism: the call this layer pushes, read before any CTA can pass the grid barrier (CTA 0 advances
+  // the channel after it)
+  const unsigned e_out = kEx && p.yout && warp == 0 ? ld_relaxed_gpu_u32(p.xepoch) + 1u : 0u;
   int* rowmap = reinterpret_cast<int*>(smem + p.off_live);
   int* tokrow = rowmap + g.R;
   int* tokcnt = tokrow + g.R;
@@ -988,6 +1001,35 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
 
   // activation tables of the M rows of x (no dependence on the routing), by reducing warps 1..15
   if (warp >= 1 && warp < kWarps) {
+    // expert parallelism: x = the ranks' rows of the channel's call e, once every rank's flag has reached e
+    // expert parallelism: x = the ranks' tagged rows of the channel's call e, each word used once it holds e
+    const unsigned long long* xsum = nullptr;
+    unsigned e_in = 0, budget = p.xspin;
+    if (kEx && p.xin) {
+      e_in = ld_relaxed_gpu_u32(p.xepoch);
+      xsum = reinterpret_cast<const unsigned long long*>(p.xpeers[p.xrank] + p.xtag_off) +
+             (size_t)(e_in & 1u) * p.xworld * (p.xn_max / 2);
+    }
+    // the 4 values of x row m, group gi this lane converts
+    auto load_x4 = [&](int m, int gi, float (&v)[4]) {
+      const size_t off = (size_t)m * g.H + gi * kGroup + 4 * lane;
+      if (!kEx || xsum == nullptr) {
+        const __nv_bfloat162* src = reinterpret_cast<const __nv_bfloat162*>(p.x + off);
+        const float2 a0 = __bfloat1622float2(src[0]), a1 = __bfloat1622float2(src[1]);
+        v[0] = a0.x; v[1] = a0.y; v[2] = a1.x; v[3] = a1.y;
+      } else {
+        // the ranks' rows in rank order, summed in fp32 and rounded to bf16 as the all-reduce does
+        float s[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int r = 0; r < p.xworld; ++r) {
+          const unsigned long long* row = xsum + (size_t)r * (p.xn_max / 2) + off / 2;
+          const float2 a0 = bf16x2_to_float2(wait_tagged(row, e_in, budget, p.err));
+          const float2 a1 = bf16x2_to_float2(wait_tagged(row + 1, e_in, budget, p.err));
+          s[0] += a0.x; s[1] += a0.y; s[2] += a1.x; s[3] += a1.y;
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = __bfloat162float(__float2bfloat16(s[i]));
+      }
+    };
     constexpr int kXW = kWarps - 1, kXPre = 4;
     const int xw = warp - 1, nxt = g.M * g.G1;
     float xv[kXPre][4];
@@ -1000,10 +1042,7 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
       gl[j] = -1;
       toff[j] = 0;
       if (t < nxt) {
-        const __nv_bfloat162* src =
-            reinterpret_cast<const __nv_bfloat162*>(p.x + (int64_t)m * g.H + gi * kGroup + 4 * lane);
-        const float2 a0 = __bfloat1622float2(src[0]), a1 = __bfloat1622float2(src[1]);
-        xv[j][0] = a0.x; xv[j][1] = a0.y; xv[j][2] = a1.x; xv[j][3] = a1.y;
+        load_x4(m, gi, xv[j]);
         gl[j] = gi;
         toff[j] = m * (int)token_table_bytes(g.H);
       }
@@ -1011,9 +1050,8 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
     prep_groups<kXPre>(xv, gl, toff, smem + p.off_tabs, g.H, lane);
     for (int tt = xw + kXPre * kXW; tt < nxt; tt += kXW) {
       const int m = fdiv(tt, g.d_G1), gi = tt - m * g.G1;
-      const __nv_bfloat16* src = p.x + (int64_t)m * g.H + gi * kGroup + 4 * lane;
-      const float v[4] = {__bfloat162float(src[0]), __bfloat162float(src[1]), __bfloat162float(src[2]),
-                          __bfloat162float(src[3])};
+      float v[4];
+      load_x4(m, gi, v);
       prep_group_regs(v, gi, table_at(smem + p.off_tabs + (size_t)m * token_table_bytes(g.H), g.H), lane);
     }
   }
@@ -1170,9 +1208,25 @@ __global__ void __launch_bounds__(kTma ? kTmaThreads : kThreads, 1) fused_layer_
       const int u = cta + g.grid * q, m = fdiv(u, g.d_nb2), b = u - m * g.nb2;
       float acc = 0.f;
       for (int j = 0; j < g.s2; ++j) acc += mail2[(size_t)j * 32 + lane];
-      p.y[(int64_t)m * g.H + b * 32 + lane] = __float2bfloat16(acc * p.rsf);
+      const __nv_bfloat16 v = __float2bfloat16(acc * p.rsf);
+      if (kEx && p.yout) {                    // this rank's tagged row of call e_out, into every rank's buffer
+        const uint32_t mine = (uint32_t)__bfloat16_as_ushort(v);
+        const uint32_t next = __shfl_down_sync(0xffffffffu, mine, 1);
+        if ((lane & 1) == 0) {
+          const unsigned long long word = ((unsigned long long)e_out << 32) | (next << 16) | mine;
+          const size_t wi = ((size_t)(e_out & 1u) * p.xworld + p.xrank) * (p.xn_max / 2) +
+                            ((size_t)m * g.H + b * 32 + lane) / 2;
+          for (int r = 0; r < p.xworld; ++r)
+            st_tagged(reinterpret_cast<unsigned long long*>(p.xpeers[r] + p.xtag_off) + wi, word);
+        }
+      } else {
+        p.y[(int64_t)m * g.H + b * 32 + lane] = v;
+      }
     }
   }
+  // the next kernel reads *xepoch only after this grid has completed; no CTA reads it after the grid barrier
+  if (kEx && p.yout && cta == 0 && warp == 0 && lane == 0)
+    asm volatile("st.relaxed.gpu.global.u32 [%0], %1;\n" ::"l"(p.xepoch), "r"(e_out) : "memory");
 }
 
 }  // namespace
@@ -1320,6 +1374,14 @@ int launch_fused(const LayerArgs& a, int M, const void* x, const int32_t* ids, c
   p.x = static_cast<const __nv_bfloat16*>(x); p.ids = ids; p.topk_w = w;
   p.map13 = a.map13; p.map2 = a.map2; p.scale_bf16 = a.scale_bf16; p.rsf = a.routed_scaling;
   p.y = static_cast<__nv_bfloat16*>(y); p.geo = g; p.err = a.err;
+  const PeerExchange* ex = a.xin ? a.xin : a.yout;
+  if (ex) {
+    p.xin = a.xin != nullptr;
+    p.yout = a.yout != nullptr;
+    p.xpeers = ex->peers; p.xtag_off = ex->tag_off; p.xn_max = ex->n_max; p.xrank = ex->rank;
+    p.xworld = ex->world; p.xepoch = ex->epoch;
+    p.xspin = ex->spin_limit ? ex->spin_limit : kPeerSpinLimit;
+  }
   size_t base = 0, total = sp.total;
   if (tma) {
     const TmaPlan tp = tma_plan(g);
@@ -1344,7 +1406,8 @@ int launch_fused(const LayerArgs& a, int M, const void* x, const int32_t* ids, c
   p.hand = reinterpret_cast<unsigned long long*>(static_cast<unsigned char*>(a.workspace) + 256);
   p.htab = static_cast<unsigned char*>(a.workspace) + 256 + kHandBytes;
 
-  auto kern = tma ? fused_layer_kernel<true> : fused_layer_kernel<false>;
+  auto kern = ex ? (tma ? fused_layer_kernel<true, true> : fused_layer_kernel<false, true>)
+                 : (tma ? fused_layer_kernel<true, false> : fused_layer_kernel<false, false>);
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)total) != cudaSuccess)
     return kErrLaunch;
   cudaLaunchConfig_t cfg{};
@@ -1369,7 +1432,13 @@ bool layer_arena_maps(const LayerArgs& a, CUtensorMap (&tm)[6]) { return tma_eli
 int decode_layer_fused(const LayerArgs& a) {
   if (a.M <= 0) return kOk;
   if (a.H % kGroup != 0 || a.I % kGroup != 0 || a.top_k <= 0) return kErrShape;
-  if (!a.x || !a.ids || !a.topk_w || !a.y) return kErrArg;
+  if ((!a.x && !a.xin) || !a.ids || !a.topk_w || (!a.y && !a.yout)) return kErrArg;
+  if (a.xin && a.yout && a.xin != a.yout) return kErrArg;        // one channel per layer
+  if (const PeerExchange* ex = a.xin ? a.xin : a.yout) {
+    if (!ex->peers || !ex->epoch || ex->world <= 0 || ex->rank < 0 || ex->rank >= ex->world || ex->n_max % 8 ||
+        (size_t)a.M * a.H > (size_t)ex->n_max || ex->tag_off % 16)
+      return kErrArg;
+  }
   if (!a.workspace || a.workspace_bytes < layer_workspace_bytes(a.M, a.H, a.I, a.top_k)) return kErrWorkspace;
   if (reinterpret_cast<uintptr_t>(a.workspace) & 255u) return kErrAlign;
 
@@ -1392,6 +1461,7 @@ int decode_layer_fused(const LayerArgs& a) {
   int mmax = a.M;
   while (mmax > 1 && !fits(mmax)) --mmax;
   if (!fits(mmax)) return kErrShape;
+  if ((a.xin || a.yout) && mmax < a.M) return kErrShape;       // an exchange call is one launch
   for (int m0 = 0; m0 < a.M; m0 += mmax) {
     const int mc = a.M - m0 < mmax ? a.M - m0 : mmax;
     const int st = launch_fused(a, mc, static_cast<const __nv_bfloat16*>(a.x) + (size_t)m0 * a.H,
