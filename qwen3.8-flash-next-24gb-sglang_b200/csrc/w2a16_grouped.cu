@@ -188,66 +188,82 @@ __device__ __forceinline__ uint64_t kmajor_desc(uint32_t addr) {
 __device__ __forceinline__ int canon_off(int row, int half) { return (row >> 3) * 256 + half * 128 + (row & 7) * 16; }
 
 // ----------------------------------------------------------------------------------------------- routing
+// One CTA of 1024 threads: the routed rows' (slot, row) keys sorted in shared memory (bitonic; rows whose expert
+// is not resident sort last), a group starting at every kGN-th row of one slot, group indices by a block scan.
 __global__ void __launch_bounds__(1024) route_kernel(const int32_t* ids, const int32_t* slots, int E, int S, int R,
                                                      int* route, unsigned* err) {
-  __shared__ int key[kMaxGroupedRows];
-  __shared__ int srt[kMaxGroupedRows];
-  __shared__ int start[kMaxGroupedRows];
+  __shared__ unsigned long long key[kMaxGroupedRows];
+  __shared__ int warp_sum[32];
   const RouteView rv{route, R};
   const int t = threadIdx.x;
-  for (int r = t; r < R; r += blockDim.x) {
-    const int e = ids[r];
-    int sl = -1;
-    if (e < 0 || e >= E) {
-      flag_error(err, 1u);
-    } else {
-      sl = slots[e];
-      if (sl >= S) {                                   // past the arena: masked, flagged
+  {
+    unsigned long long kv = ~0ull;                      // padding sorts last
+    if (t < R) {
+      const int e = ids[t];
+      int sl = -1;
+      if (e < 0 || e >= E) {
         flag_error(err, 1u);
-        sl = -1;
+      } else {
+        sl = slots[e];
+        if (sl >= S) {                                  // past the arena: masked, flagged
+          flag_error(err, 1u);
+          sl = -1;
+        }
       }
+      kv = ((unsigned long long)(sl >= 0 ? (unsigned)sl : 0x7FFFFFFFu) << 32) | (unsigned)t;
     }
-    key[r] = sl >= 0 ? sl : INT_MAX;
+    key[t] = kv;
   }
   __syncthreads();
-  for (int r = t; r < R; r += blockDim.x) {           // rank by (slot, row): live rows first
-    const int k = key[r];
-    int rank = 0;
-    for (int j = 0; j < R; ++j) {
-      const int kj = key[j];
-      rank += (kj < k) || (kj == k && j < r);
+  for (int k = 2; k <= kMaxGroupedRows; k <<= 1)
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      const int p = t ^ j;
+      if (p > t) {
+        const unsigned long long a = key[t], b = key[p];
+        if ((a > b) == ((t & k) == 0)) {
+          key[t] = b;
+          key[p] = a;
+        }
+      }
+      __syncthreads();
     }
-    srt[rank] = r;
+  // position t of the sorted order: its slot, whether it opens a group (every kGN-th row of a slot's run)
+  const bool live = t < R && (unsigned)(key[t] >> 32) != 0x7FFFFFFFu;
+  const int k0 = live ? (int)(key[t] >> 32) : -1;
+  int first = t;
+  if (live)
+    while (first > 0 && (int)(key[first - 1] >> 32) == k0) --first;
+  const int st = live && (t - first) % kGN == 0 ? 1 : 0;
+  // exclusive scan of the group starts: the group index of a starting position
+  const int lane = t & 31, w = t >> 5;
+  int inc = st;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += v;
+  }
+  if (lane == 31) warp_sum[w] = inc;
+  __syncthreads();
+  if (w == 0) {
+    int ws = warp_sum[lane], wi = ws;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += v;
+    }
+    warp_sum[lane] = wi - ws;                           // exclusive prefix of the warp totals
   }
   __syncthreads();
-  for (int q = t; q < R; q += blockDim.x) {           // a group starts every kGN rows of one slot
-    const int k = key[srt[q]];
-    int st = 0;
-    if (k != INT_MAX) {
-      int first = q;
-      while (first > 0 && key[srt[first - 1]] == k) --first;
-      st = (q - first) % kGN == 0;
-    }
-    start[q] = st;
-  }
-  __syncthreads();
-  for (int q = t; q < R; q += blockDim.x) {
-    rv.order()[q] = srt[q];
-    if (!start[q]) continue;
-    int gid = 0;
-    for (int j = 0; j < q; ++j) gid += start[j];
-    const int k = key[srt[q]];
+  const int gid = warp_sum[w] + inc - st;
+  if (t < R) rv.order()[t] = (int)(unsigned)key[t];
+  if (st) {
     int cnt = 1;
-    while (q + cnt < R && cnt < kGN && !start[q + cnt] && key[srt[q + cnt]] == k) ++cnt;
-    rv.gslot()[gid] = k;
-    rv.gstart()[gid] = q;
+    while (t + cnt < R && cnt < kGN && (int)(key[t + cnt] >> 32) == k0) ++cnt;
+    rv.gslot()[gid] = k0;
+    rv.gstart()[gid] = t;
     rv.gcnt()[gid] = cnt;
   }
-  if (t == 0) {
-    int n = 0;
-    for (int j = 0; j < R; ++j) n += start[j];
-    route[0] = n;
-  }
+  if (t == kMaxGroupedRows - 1) route[0] = warp_sum[w] + inc;   // the number of groups
 }
 
 // ----------------------------------------------------------------------------------------------- projection
@@ -653,20 +669,30 @@ __global__ void __launch_bounds__(256) xtab_kernel(const __nv_bfloat16* act, int
   }
 }
 
-// y[m, c] = routed_scaling * sum over the token's live routed rows (routing order) of y rows.
-__global__ void sum_kernel(const float* yrows, const int32_t* ids, const int32_t* slots, int E, int S, int M, int H,
-                           int top_k, float rsf, __nv_bfloat16* y) {
-  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= (int64_t)M * H) return;
-  const int m = (int)(idx / H), c = (int)(idx - (int64_t)m * H);
-  float a = 0.f;
-  for (int j = 0; j < top_k; ++j) {
-    const int r = m * top_k + j, e = ids[r];
-    if (e < 0 || e >= E) continue;
-    const int sl = slots[e];
-    if (sl >= 0 && sl < S) a += yrows[(int64_t)r * H + c];
+// y[m, c] = routed_scaling * sum over the token's live routed rows (routing order) of y rows. One CTA per token:
+// the token's rows are resolved once into shared memory.
+__global__ void __launch_bounds__(256) sum_kernel(const float* yrows, const int32_t* ids, const int32_t* slots, int E,
+                                                  int S, int M, int H, int top_k, float rsf, __nv_bfloat16* y) {
+  __shared__ int live_rows[kMaxGroupedRows];
+  __shared__ int nlive;
+  const int m = blockIdx.x;
+  if (threadIdx.x == 0) {
+    int n = 0;
+    for (int j = 0; j < top_k; ++j) {
+      const int r = m * top_k + j, e = ids[r];
+      if (e < 0 || e >= E) continue;
+      const int sl = slots[e];
+      if (sl >= 0 && sl < S) live_rows[n++] = r;
+    }
+    nlive = n;
   }
-  y[idx] = __float2bfloat16(a * rsf);
+  __syncthreads();
+  const int n = nlive;
+  for (int c = threadIdx.x; c < H; c += blockDim.x) {
+    float a = 0.f;
+    for (int j = 0; j < n; ++j) a += yrows[(int64_t)live_rows[j] * H + c];
+    y[(int64_t)m * H + c] = __float2bfloat16(a * rsf);
+  }
 }
 
 int chunk_tokens(int M, int top_k) {
@@ -765,10 +791,8 @@ int decode_layer_grouped(const LayerArgs& a) {
     dn.has_zeros = hz; dn.scale_bf16 = a.scale_bf16;
     dn.topk_w = a.topk_w + (size_t)m0 * a.top_k; dn.yrows = yrows; dn.err = a.err;
     proj_kernel<false><<<sms, kGThreads, proj_smem(false), a.stream>>>(dn);
-    const int64_t n = (int64_t)mc * a.H;
-    sum_kernel<<<(unsigned)((n + 255) / 256), 256, 0, a.stream>>>(yrows, ids, a.map13.slots, a.map13.E, a.map13.S, mc, a.H,
-                                                                  a.top_k, a.routed_scaling,
-                                                                  static_cast<__nv_bfloat16*>(a.y) + (size_t)m0 * a.H);
+    sum_kernel<<<(unsigned)mc, 256, 0, a.stream>>>(yrows, ids, a.map13.slots, a.map13.E, a.map13.S, mc, a.H, a.top_k,
+                                                  a.routed_scaling, static_cast<__nv_bfloat16*>(a.y) + (size_t)m0 * a.H);
     if (cudaGetLastError() != cudaSuccess) return kErrLaunch;
   }
   return kOk;
