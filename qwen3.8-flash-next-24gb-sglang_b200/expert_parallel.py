@@ -134,8 +134,12 @@ class PeerAllReduce:
         I = arena.codes13.shape[2] // 2
         if M * H > self.n_max:
             raise ValueError(f"M * H = {M * H} exceeds the channel's n_max {self.n_max}")
-        if not x_from_peers and (x is None or x.dtype != torch.bfloat16 or tuple(x.shape) != (M, H)):
-            raise ValueError("x must be a bf16 [M, H] tensor unless x_from_peers")
+        if not x_from_peers and (x is None or x.dtype != torch.bfloat16 or tuple(x.shape) != (M, H)
+                                 or x.device != self.device):
+            raise ValueError("x must be a bf16 [M, H] tensor on the channel's device unless x_from_peers")
+        for t in (ids, w, arena.slots, arena.codes13, arena.scales13, arena.codes2, arena.scales2):
+            if t.device != self.device:
+                raise ValueError("routing and arena tensors must be on the channel's device")
         xx = None if x_from_peers else x.contiguous()
         y = None
         if not y_to_peers:
@@ -160,6 +164,8 @@ class PeerAllReduce:
         """The INT8 projection of the sum of the ranks' rows of the channel's current call (w2a16_int8_gemv_from_peers):
         rows of K = 4 * qweight.shape[0] values -> bf16 [M, N]."""
         K, N = qweight.shape[0] * 4, qweight.shape[1]
+        if qweight.device != self.device or scales.device != self.device or not qweight.is_contiguous():
+            raise ValueError("qweight (contiguous) and scales must be on the channel's device")
         if M * K > self.n_max:
             raise ValueError(f"M * K = {M * K} exceeds the channel's n_max {self.n_max}")
         group = K if scales.shape[0] == 1 else K // scales.shape[0]
