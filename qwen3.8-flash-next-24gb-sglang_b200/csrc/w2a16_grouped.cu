@@ -44,12 +44,12 @@ namespace {
 constexpr int kGN = 16;                          // routed rows of one group (tokens of one expert)
 constexpr int kBN = 2 * kGN;                     // MMA N: a high-byte and a low-byte row per routed row
 constexpr int kTileCols = 128;                   // MMA M: weight columns of a tile
-constexpr int kSets = 2;                         // fold and expansion sets (4 warps each, one per TMEM lane quarter)
-constexpr int kMmaWarps = 4;                     // MMA issuers, one per SM sub-partition
-// warps: 0-7 fold sets, 8-15 expansion sets, 16-19 staging, 20-23 MMA issuers, the producer warp. Set k of the
-// fold and expansion roles takes the groups gc with gc % kSets == k, MMA warp m those with gc % kMmaWarps == m,
-// so several groups are in every stage of the hand-over at once
-constexpr int kExpWarp0 = 4 * kSets, kStgWarp0 = 8 * kSets, kMmaWarp0 = kStgWarp0 + 4,
+constexpr int kSets = 2;                         // fold, expansion and staging sets (4 warps each)
+constexpr int kMmaWarps = 2;                     // MMA issuers
+// warps: 0-7 fold sets, 8-15 expansion sets, 16-23 staging sets, 24-25 MMA issuers, the producer warp. Set k of
+// a role takes the groups gc with gc % kSets == k, MMA warp m those with gc % kMmaWarps == m, so several groups
+// are in every stage of the hand-over at once
+constexpr int kExpWarp0 = 4 * kSets, kStgWarp0 = 8 * kSets, kMmaWarp0 = 12 * kSets,
               kProducerWarp = kMmaWarp0 + kMmaWarps;
 constexpr int kGThreads = 32 * (kProducerWarp + 1);
 constexpr int kAcols = kGroup / 4;               // TMEM columns of one group of the A operand (4 codes each)
@@ -306,7 +306,7 @@ __global__ void __launch_bounds__(kGThreads, 1) proj_kernel(const __grid_constan
       g_mbar_init(empty(s), 4 * kGPS);                // per group of the stage, its expansion set's 4 warps
     }
     for (int b = 0; b < kNB; ++b) {
-      g_mbar_init(ready(b), 8);                       // the group's expansion set and the staging warps, 4 each
+      g_mbar_init(ready(b), 8);                       // the group's expansion set and staging set, 4 warps each
       g_mbar_init(mmab(b), 1);
       g_mbar_init(freeb(b), 4);                       // the group's fold set
     }
@@ -474,10 +474,11 @@ __global__ void __launch_bounds__(kGThreads, 1) proj_kernel(const __grid_constan
       fold_sync2();                                     // set 0 has read the exchange before set 1 writes again
     }
   } else if (warp >= kStgWarp0) {
-    // ---------------------------------------------------------------- staging warps: the B operand
-    // thread: routed row bn of the group (B rows bn and kGN + bn), 16-value word bs of each group; the table
-    // pieces of the next two groups are in flight while a group is stored
-    const int r = tid - 32 * kStgWarp0;
+    // ---------------------------------------------------------------- staging sets: the B operand
+    // thread: routed row bn of the group (B rows bn and kGN + bn), 16-value word bs of each group; a set's table
+    // pieces of its next two groups are in flight while it stores one
+    const int set = (warp - kStgWarp0) >> 2;
+    const int r = tid - 32 * (kStgWarp0 + 4 * set);
     const int bn = r >> 3, bs = r & 7;
     unsigned gc0 = 0;
     struct Piece { uint4 h, l; float e; int s; };
@@ -485,6 +486,7 @@ __global__ void __launch_bounds__(kGThreads, 1) proj_kernel(const __grid_constan
       const int gi = w / ntiles;
       const int g0 = rv.gstart()[gi], cnt = rv.gcnt()[gi];
       const int trow = bn < cnt ? rv.order()[g0 + bn] / p.act_row_div : -1;   // table row, -1 = padding
+      const int gfirst = (int)(((unsigned)set + kSets - gc0 % kSets) % kSets);
       auto fetch = [&](int g, Piece& pc) {
         pc.h = pc.l = make_uint4(0, 0, 0, 0);
         pc.e = 0.f;
@@ -513,15 +515,16 @@ __global__ void __launch_bounds__(kGThreads, 1) proj_kernel(const __grid_constan
         __syncwarp();
         if (lane == 0) g_mbar_arrive(ready(b));
       };
+      constexpr int kStep = kSets;
       Piece pa, pb;
-      fetch(0, pa);
-      fetch(1, pb);
-      for (int g = 0; g < G; g += 2) {
+      fetch(gfirst, pa);
+      fetch(gfirst + kStep, pb);
+      for (int g = gfirst; g < G; g += 2 * kStep) {
         store(g, pa);
-        fetch(g + 2, pa);
-        if (g + 1 < G) {
-          store(g + 1, pb);
-          fetch(g + 3, pb);
+        fetch(g + 2 * kStep, pa);
+        if (g + kStep < G) {
+          store(g + kStep, pb);
+          fetch(g + 3 * kStep, pb);
         }
       }
     }
