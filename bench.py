@@ -198,6 +198,12 @@ def cpu_baseline(arena, x, ids, w, budget_s: float):
     return sec, n, O.cpu_info()
 
 
+def stack_workload(E: int, world: int) -> str:
+    """The workload string of the default case (both arms)."""
+    return (f"config4 stack of {LAYERS} MoE layers, each config 1 (M=1 H=4096 I=1536 E=256 top-8 W2A16 g128 zp "
+            f"f16 scales), experts {E // world} per GPU")
+
+
 # ----------------------------------------------------------------------------- the layer stack, any N
 def run_stack(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -371,8 +377,7 @@ def _run_stack(args, world: int, rank: int, dev: torch.device):
         "warmup": max(args.warmup, 3), "ms_per_step": round(us_step / 1e3, 6), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": DTYPE,
         "data": "synthetic (seeded; BASELINE config 1 / config 4 distributions)",
-        "config": {"workload": f"config4 stack of {L} MoE layers, each config 1 (M=1 H=4096 I=1536 E=256 top-8 "
-                               f"W2A16 g128 zp f16 scales), experts {E // world} per GPU",
+        "config": {"workload": stack_workload(E, world),
                    "global_batch": M, "seq_len": 1,
                    "parallelism": "single GPU" if world == 1 else f"ep{world} (exchange folded into the layer kernels)",
                    "l2": f"inputs larger than L2 ({(hi - lo) * L} local experts, {bpl * L * world // 2**20} MB of "
@@ -538,13 +543,13 @@ def run_reference(args):
     info = O.cpu_info()
     gbs = bps / sec / 1e9
     line = {
-        "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": 0,
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus,
         "steps": n, "warmup": max(args.warmup, 1), "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
         "data": "synthetic (seeded; BASELINE config 1 distributions)",
-        "config": {"workload": f"config4 stack of {LAYERS} MoE layers, each config 1 (M=1 H=4096 I=1536 E=256 "
-                               "top-8 W2A16 g128 zp f16 scales); timed per layer on the host",
-                   "global_batch": 1, "seq_len": 1, "parallelism": "host CPU"},
+        # the same workload as this bench's own arm at N=1 (stack_workload), each sampled layer timed on the host
+        "config": {"workload": stack_workload(E, 1), "global_batch": M, "seq_len": 1,
+                   "parallelism": "host CPU (the reference's torch formulation, all host threads)", "layers": LAYERS},
         "us_per_layer": round(sec * 1e6, 1),
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": info["torch_threads"], "kind": "port",
                          "sample": f"{n} layers: 8 routed experts dequantised in fp32 + matmuls (torch CPU)",
