@@ -547,8 +547,8 @@ def run_reference(args):
         "steps": n, "warmup": max(args.warmup, 1), "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
         "data": "synthetic (seeded; BASELINE config 1 distributions)",
-        # the same workload as this bench's own arm at N=1 (stack_workload), each sampled layer timed on the host
-        "config": {"workload": stack_workload(E, 1), "global_batch": M, "seq_len": 1,
+        # the same workload string as this bench's own arm at the launch's N; each sampled layer timed on the host
+        "config": {"workload": stack_workload(E, max(1, args.gpus)), "global_batch": M, "seq_len": 1,
                    "parallelism": "host CPU (the reference's torch formulation, all host threads)", "layers": LAYERS},
         "us_per_layer": round(sec * 1e6, 1),
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": info["torch_threads"], "kind": "port",
