@@ -159,3 +159,31 @@ def test_layer_path_choice(pkg):
         assert ml._workspace_bytes(M, H, I, k, -1) == (bat(M) if M >= 64 else per(M))
         assert ml._workspace_bytes(M, H, I, k, 1) == (bat(M) if M >= 16 else per(M))
     assert ml.BATCHED_MIN_TOKENS == nat.BATCHED_AUTO_TOKENS == 64
+
+
+def _slots_ep(lib, ex, x_from, y_to, M=1, H=4096, I=1536, k=8, ws_bytes=1 << 30):
+    fake = ctypes.c_void_p(0x1000)
+    return lib.w2a16_moe_decode_layer_slots_ep(fake, M, H, I, k, fake, fake, fake, 256, 256, fake, 4096, fake, 256,
+                                               None, 0, fake, 4096, fake, 256, None, 0, 0, 1.0, fake, fake,
+                                               ws_bytes, x_from, y_to, ex, None, None)
+
+
+def test_exchange_entry_points_refuse_bad_channels(pkg):
+    """The expert-parallel entry points refuse, before any device work: an exchange mode without a channel, a
+    channel whose n_max cannot hold the layer's M x H values, a misaligned tag offset, a rank outside the world
+    (argument); the INT8 projection from peers without a channel (argument)."""
+    nat = pkg._native
+    lib = nat.lib()
+    fake = 0x1000
+    assert _slots_ep(lib, None, 1, 0) == 4
+    assert _slots_ep(lib, None, 0, 1) == 4
+    good = nat.Exchange(fake, 4096, 8192, 0, 2, fake, 0)
+    small = nat.Exchange(fake, 4096, 1024, 0, 2, fake, 0)          # n_max < M * H
+    skew = nat.Exchange(fake, 4100, 8192, 0, 2, fake, 0)           # tag offset not a multiple of 16
+    stray = nat.Exchange(fake, 4096, 8192, 2, 2, fake, 0)          # rank 2 of a world of 2
+    for ex in (small, skew, stray):
+        assert _slots_ep(lib, ctypes.byref(ex), 1, 1) == 4
+    # a well-formed channel passes the argument checks and stops at the workspace check (no launch)
+    assert _slots_ep(lib, ctypes.byref(good), 1, 1, ws_bytes=64) == 5
+    assert lib.w2a16_int8_gemv_from_peers(None, ctypes.c_void_p(fake), ctypes.c_void_p(fake), 128, 128, 1, 4096, 4096,
+                                          ctypes.c_void_p(fake), 4096, None, None) == 4
