@@ -510,6 +510,66 @@ def run_case_int8(args):
     return 0 if err < 1e-2 else 1
 
 
+def run_case_config(args):
+    """BASELINE config 0 (H=2048, I=768, E=64, top-8, M=1) or config 2 (config-1 shapes, S=184 of 256 experts
+    resident in a random permutation of arena rows, Zipf(1.1) routing, misses masked through slot -1, plus the
+    INT8 dense [4096 -> 4096]): the layer per call in a CUDA graph of `--calls` calls with a fresh routing each
+    (and the dense after each layer for config 2), bytes = the routed experts that are resident; the last call
+    checked against the oracle."""
+    import __graft_entry__ as graft
+    import oracle as O
+    pkg = graft.load_package()
+    dev = torch.device("cuda", 0)
+    k, M, P = 8, 1, max(args.calls, 8)
+    if args.case == "config0":
+        E, H, I, S = 64, 2048, 768, 64
+        slots = None
+        pop = None
+    else:
+        E, H, I, S = 256, 4096, 1536, 184
+        pop = pkg.synth.zipf_popularity(E, 1.1, seed=2)
+        slots = pkg.synth.resident_slots(pop, S, seed=2)
+    arena = pkg.synth.make_arena(S, H, I, seed=7, zeros=True, scale_dtype=torch.float16, device=dev, gen_device=dev,
+                                 slots=slots)
+    if pop is None:
+        routes = [pkg.synth.route_softmax(M, E, k, seed=100 + c, device=dev, gen_device=dev) for c in range(P)]
+    else:
+        routes = [pkg.synth.route_zipf(M, E, k, pop, seed=100 + c, device=dev) for c in range(P)]
+    ids = torch.stack([r[0] for r in routes])
+    w = torch.stack([r[1] for r in routes])
+    x = pkg.synth.make_activation(P * M, H, seed=3, device=dev, gen_device=dev).reshape(P, M, H)
+    y = torch.empty(P, M, H, dtype=torch.bfloat16, device=dev)
+    g = capture(lambda c: pkg.moe_decode_layer(x[c], ids[c], w[c], arena, out=y[c]), P)
+    us = sorted(time_replays(g, 1)[0] * 1e3 / P for _ in range(3))[1]
+    del g
+    st = arena.slots.cpu()
+    resident = [[int(e) for e in ids[c, 0].tolist() if int(st[e]) >= 0] for c in range(P)]
+    nbytes = sum(len(r) for r in resident) / P * arena.bytes_per_expert() + 2 * M * H * 2
+    err = O.max_rel_err(y[P - 1].float().cpu(), O.moe_layer_from_arena(arena, x[P - 1], ids[P - 1], w[P - 1]))
+    peak, kind = peaks()
+    line = {"case": args.case, "E": E, "S": S, "H": H, "I": I, "M": M, "top_k": k, "us_per_layer": round(us, 3),
+            "resident_routed_per_call": round(sum(len(r) for r in resident) / P, 2),
+            "gbs": round(nbytes / us / 1e3, 1), "hbm_frac": round(nbytes / us / 1e3 / peak, 4), "peak_kind": kind,
+            "max_rel_err": err}
+    rc = 0 if err < 1e-2 else 1
+    if args.case == "config2":
+        q, sc = pkg.synth.make_int8_dense(H, H, seed=11, device=dev, gen_device=dev)
+        z = torch.empty(P, M, H, dtype=torch.bfloat16, device=dev)
+
+        def both(c):
+            pkg.moe_decode_layer(x[c], ids[c], w[c], arena, out=y[c])
+            pkg.int8_gemv(y[c], q, sc, out=z[c])
+        g = capture(both, P)
+        us2 = sorted(time_replays(g, 1)[0] * 1e3 / P for _ in range(3))[1]
+        del g
+        ref = O.int8_gemv(y[P - 1].float().cpu(), q.cpu(), sc.float().cpu())
+        err2 = O.max_rel_err(z[P - 1].float().cpu(), ref)
+        line.update({"us_layer_plus_dense": round(us2, 3), "dense_max_rel_err": err2})
+        rc |= 0 if err2 < 1e-2 else 1
+    print(json.dumps(line))
+    return rc
+
+
 # ----------------------------------------------------------------------------- reference arm
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
@@ -565,7 +625,7 @@ def main():
     ap.add_argument("--steps", type=int, default=40)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--case", choices=["stack", "layer", "batched", "int8"], default="stack")
+    ap.add_argument("--case", choices=["stack", "layer", "batched", "int8", "config0", "config2"], default="stack")
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU baseline sampling")
     ap.add_argument("--experts", type=int, default=256, help="case layer: experts in the arena")
     ap.add_argument("--calls", type=int, default=6, help="case layer / batched: calls")
@@ -583,6 +643,8 @@ def main():
         return run_case_batched(args)
     if args.case == "int8":
         return run_case_int8(args)
+    if args.case in ("config0", "config2"):
+        return run_case_config(args)
     run_stack(args)
     return 0
 

@@ -27,15 +27,34 @@ def test_int8_grouped_scales_and_repeat(pkg, golden, dev):
         assert O.max_rel_err(y.float().cpu(), ref) < 1e-2
 
 
+def _int8_torch_fp32(x, qw, sc, zero=128):
+    """Plain PyTorch fp32 reference of the INT8 projection on the GPU, 16,384 columns at a time: byte i of int32
+    word kw is weight row 4 kw + i, (q - zero) * scale of its 128-row group."""
+    K, N = 4 * qw.shape[0], qw.shape[1]
+    group = K // sc.shape[0]
+    out = torch.empty(x.shape[0], N, dtype=torch.float32, device=x.device)
+    xf = x.float()
+    for n0 in range(0, N, 16384):
+        q = qw[:, n0:n0 + 16384]
+        b = torch.stack([(q >> (8 * i)) & 0xFF for i in range(4)], dim=1).reshape(K, -1).float() - zero
+        s = sc[:, n0:n0 + 16384].float().repeat_interleave(group, dim=0)
+        out[:, n0:n0 + 16384] = xf @ (b * s)
+    return out
+
+
 def test_int8_lm_head_sized(pkg, dev):
     """An lm_head-sized projection, K = 4096 -> N = 151,936 (1,187 column blocks of 128), with g128 scales
-    and the checkpoint's zero point 128: a spread of column blocks checked against the oracle."""
+    and the checkpoint's zero point 128: every column against a plain PyTorch fp32 reference, and a spread of
+    column blocks against the oracle."""
     K, N, M = 4096, 151936, 2
     qw, sc1 = pkg.synth.make_int8_dense(K, N, seed=9, device=dev, gen_device=dev)
     sc = (sc1.float().repeat(K // 128, 1) * torch.linspace(0.5, 1.5, K // 128, device=dev)[:, None]).to(torch.float16)
     x = pkg.synth.make_activation(M, K, seed=9, device=dev, gen_device=dev)
     y = pkg.int8_gemv(x, qw, sc)
+    ref_all = _int8_torch_fp32(x, qw, sc)
     torch.cuda.synchronize()
+    rel = float((y.float() - ref_all).abs().max() / ref_all.abs().max())
+    assert rel < 1e-2, rel
     blocks = torch.tensor([0, 1, 500, 1000, 1186])
     cols = (blocks[:, None] * 128 + torch.arange(128)[None]).reshape(-1).to(dev)
     ref = O.int8_gemv(x.cpu(), qw[:, cols].cpu(), sc[:, cols].cpu())
