@@ -5,7 +5,7 @@
 // top-k sum, with the slot-table indirection of row_arena.py.
 //
 // route_kernel (one CTA): the live routed rows (slot >= 0) sorted by (slot, row) and cut into groups of at
-// most kGN rows of one expert.
+// most kGN rows of one expert. xtab_kernel: the activation tables (below).
 //
 // proj_kernel<kGateUp> (persistent, one CTA per SM): work items (group, tile of 128 weight columns -- gate_up:
 // 64 gate columns and the matching 64 up columns; down: 128 output columns), dealt round-robin. A producer warp
@@ -20,8 +20,8 @@
 //     and sum. xtab_kernel builds the tables once per call (x) and once between the projections (h): every
 //     row's 128 values of a group in 15-bit fixed point with one power-of-two scale, split into a signed high
 //     and a signed low byte (x16 = 256 hi + lo), in the K order of the A operand;
-//   * one MMA thread issues 4 tcgen05.mma (A from tensor memory, M = 128 columns, N = 32, K = 32) per group
-//     into the group's own accumulator in tensor memory;
+//   * an MMA thread (two MMA warps take alternate groups) issues 4 tcgen05.mma (A from tensor memory, M = 128
+//     columns, N = 32, K = 32) per group into the group's own accumulator in tensor memory;
 //   * two fold sets (taking alternate groups) read the accumulator (tcgen05.ld) and fold it exactly as the
 //     reference folds its zero point (gemv/moe_gemv_int2_tab.py:61-66): T = 256 D_hi + D_lo - zp sum x16
 //     (exact int32), acc += T * s * 2^e in fp32; at the end of an item the sets add their partial sums and
@@ -125,8 +125,8 @@ __device__ __forceinline__ void g_mbar_arrive_tx(uint32_t bar, unsigned bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
 }
 // Bounded waits for the phase of the given parity (error bit 1 when they give up): suspending tries for the many
-// threads of a role, non-suspending polls for the one MMA thread (a thread suspended in try_wait resumes some
-// time after the phase completes, and the MMA thread's waits are on the hand-over chain of every group).
+// threads of a role, non-suspending polls for the MMA threads (a thread suspended in try_wait resumes some
+// time after the phase completes, and the MMA threads' waits are on the hand-over chain of every group).
 __device__ __forceinline__ void g_mbar_wait(uint32_t bar, unsigned parity, unsigned* err) {
   for (unsigned it = 0;; ++it) {
     uint32_t ok;
