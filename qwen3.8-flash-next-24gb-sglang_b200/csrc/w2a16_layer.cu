@@ -28,6 +28,12 @@
 // phase-1 items, so the down weights are in flight while phase 1 finishes. Register mode (int64 address
 // tables): at launch every CTA asks L2 to fetch its 1/grid share of each routed expert's arrays, and each
 // lane loads its own item data into registers one item ahead of the one it is reducing.
+//
+// Expert parallelism (the kEx variant; the plain variant carries none of it). With a PeerExchange channel the
+// prologue's table warps take x as the sum, in rank order, of the ranks' tagged rows of the channel's call
+// (each 8-byte word -- two bf16 values and the call number -- polled until it holds the call), and phase 2
+// pushes each finished unit of y as this rank's tagged row of the next call into every rank's buffer instead
+// of writing y; the all-reduce of the ranks' partials thereby rides on the layers' own loads and stores.
 #include <cuda.h>
 #include <type_traits>
 #include <cudaTypedefs.h>
