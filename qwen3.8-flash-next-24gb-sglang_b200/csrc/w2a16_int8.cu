@@ -6,14 +6,28 @@
 // multiply the four weight bytes by 16-bit fixed-point activations (power-of-two scale per 128
 // values, as in the W2 kernels). The zero point folds as T - zero * sum x_fixed per 32-k quarter.
 //
-// Split-K inside a thread-block cluster: the S <= 8 CTAs of a cluster take the K slices of one block of
-// 128 columns (8 warps x slice/8 k each); every CTA leaves its 128-column partial in shared memory and,
-// after a cluster barrier, cluster rank 0 adds the S partials in rank order through distributed shared
-// memory -> deterministic bf16 output, no workspace, no atomics. Launched with programmatic stream
-// serialisation: the weight loads are issued before the kernel waits for the previous one, so the
-// 16-byte-per-lane weight stream overlaps that kernel's tail (the weights are never written by a kernel
-// that triggers this one early).
+// Two kernels.
+//
+// Column-slice kernel (K <= 4096, at most 8 tokens; the decode shapes): each CTA owns 32 output columns over
+// all of K. Before it waits for the previous kernel (the weights are never written by a kernel that lets this
+// one start early) thread 0 issues tensor copies of the CTA's whole weight slice ([K/4] word rows x 128 bytes)
+// and its scale rows into shared memory; the activation rows are converted to fixed point meanwhile. Lane
+// (kq, cq) of warp w reduces one 128-k group (4 w + kq) for 4 columns (cq) against every token, folds the
+// zero point and the group's scale in once per group, and the CTA sums its groups in a fixed order (lanes,
+// then warps): no split-K across CTAs, no cluster barrier, deterministic. (Measured against variants: 16
+// columns on 4 warps with two CTAs per SM, the activation loads of several groups batched, one mbarrier per
+// copy -- all slower in the graph-replayed bench.)
+//
+// Cluster kernel (any other shape): split-K inside a thread-block cluster: the S <= 8 CTAs of a cluster take
+// the K slices of one block of 128 columns (8 warps x slice/8 k each); every CTA leaves its 128-column partial
+// in shared memory and, after a cluster barrier, cluster rank 0 adds the S partials in rank order through
+// distributed shared memory -> deterministic bf16 output, no workspace, no atomics. Its weight loads are
+// issued before the dependency wait as well.
+//
+// Both are launched with programmatic stream serialisation.
 #include <cooperative_groups.h>
+#include <cuda.h>
+#include <cudaTypedefs.h>
 
 #include "w2a16_kernels.h"
 
@@ -197,6 +211,273 @@ __global__ void __launch_bounds__(256) int8_gemv_kernel(I8Params p) {
   cluster.sync();                                    // every partial stays readable until rank 0 is done
 }
 
+// ----------------------------------------------------------------------------- column-slice kernel
+namespace {
+constexpr int kSCols = 32;                 // output columns per CTA: one 128-byte word row of the weights
+constexpr int kSWarps = 8;                 // warps per CTA: 4 groups of 128 k each
+constexpr int kSMaxK = 4096;
+constexpr int kSMaxTok = 8;
+constexpr int kSBoxRows = 256;             // word rows per tensor copy (the box limit)
+
+struct I8SParams {
+  CUtensorMap wmap;                        // int32 [K/4][N], box 32 columns x min(K/4, 256) rows
+  CUtensorMap smap;                        // f16 [K/group][N], box 32 columns x K/group rows
+  const __nv_bfloat16* x; int64_t stride_xm;
+  const __half* scales; int group; int zero;
+  int M, K, N, box_rows, nbox, srows;
+  size_t off_s, off_xq, off_xsum, off_xscl, off_red, off_bar;
+  __nv_bfloat16* y; int64_t stride_ym;
+  const uint64_t* xpeers; size_t xtag_off; unsigned* xepoch;
+  int xrank, xworld, xn_max; unsigned xspin; unsigned* err;
+};
+
+__device__ __forceinline__ uint32_t s_u32(const void* ptr) { return static_cast<uint32_t>(__cvta_generic_to_shared(ptr)); }
+
+template <bool kPeers>
+__global__ void __launch_bounds__(256, 1) int8_slice_kernel(const __grid_constant__ I8SParams p) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * kSCols;
+  const int G = p.K / 128;
+  const uint32_t bar = s_u32(smem + p.off_bar);
+  if (threadIdx.x == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(bar) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&p.wmap)) : "memory");
+    const unsigned bytes = (unsigned)(p.nbox * p.box_rows * kSCols * 4 + (p.group < p.K ? p.srows * kSCols * 2 : 0));
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;\n" : "=l"(pol));
+    for (int b = 0; b < p.nbox; ++b)
+      asm volatile(
+          "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, "
+          "{%2, %3}], [%4], %5;\n" ::"r"(s_u32(smem + (size_t)b * p.box_rows * kSCols * 4)),
+          "l"(reinterpret_cast<uint64_t>(&p.wmap)), "r"(n0), "r"(b * p.box_rows), "r"(bar), "l"(pol)
+          : "memory");
+    if (p.group < p.K)
+      asm volatile(
+          "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+          "[%4];\n" ::"r"(s_u32(smem + p.off_s)), "l"(reinterpret_cast<uint64_t>(&p.smap)), "r"(n0), "r"(0), "r"(bar)
+          : "memory");
+  }
+  asm volatile("griddepcontrol.wait;\n" ::: "memory");
+  int16_t* xq = reinterpret_cast<int16_t*>(smem + p.off_xq);                // [M][K]
+  int* xsum = reinterpret_cast<int*>(smem + p.off_xsum);                    // [M][G]
+  float* xscl = reinterpret_cast<float*>(smem + p.off_xscl);                // [M][G]
+  float* red = reinterpret_cast<float*>(smem + p.off_red);                  // [M][8][32]
+  const unsigned long long* xw = nullptr;
+  unsigned e_in = 0, budget = p.xspin;
+  if (kPeers) {
+    e_in = ld_relaxed_gpu_u32(p.xepoch);
+    xw = reinterpret_cast<const unsigned long long*>(p.xpeers[p.xrank] + p.xtag_off) +
+         (size_t)(e_in & 1u) * p.xworld * (p.xn_max / 2);
+  }
+  // activations: one warp per (token, 128-k group), the conversion of the cluster kernel
+  for (int t = warp; t < p.M * G; t += kSWarps) {
+    const int m = t / G, g = t - m * G;
+    const int kb = g * 128 + 4 * lane;
+    float v[4];
+    if (!kPeers) {
+      const __nv_bfloat16* src = p.x + (int64_t)m * p.stride_xm + kb;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v[i] = __bfloat162float(src[i]);
+    } else {
+      // the ranks' rows in rank order, summed in fp32 and rounded to bf16 as the all-reduce does
+      const size_t w0 = ((size_t)m * p.K + kb) / 2;
+      float sm[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int r = 0; r < p.xworld; ++r) {
+        const unsigned long long* row = xw + (size_t)r * (p.xn_max / 2) + w0;
+        const float2 a0 = bf16x2_to_float2(wait_tagged(row, e_in, budget, p.err));
+        const float2 a1 = bf16x2_to_float2(wait_tagged(row + 1, e_in, budget, p.err));
+        sm[0] += a0.x; sm[1] += a0.y; sm[2] += a1.x; sm[3] += a1.y;
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v[i] = __bfloat162float(__float2bfloat16(sm[i]));
+    }
+    float mx = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+    mx = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(mx)));
+    const int E = (mx > 0.f ? frexp_exponent(mx) : 0) - 15;
+    const float inv = pow2f(-E);
+    int s = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int qv = max(-32767, min(32767, __float2int_rn(v[i] * inv)));
+      xq[(size_t)m * p.K + kb + i] = (int16_t)qv;
+      s += qv;
+    }
+    s = __reduce_add_sync(0xffffffffu, s);
+    if (lane == 0) {
+      xsum[m * G + g] = s;
+      xscl[m * G + g] = pow2f(E);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {                                  // the weight slice is in (bounded wait: error bit 1)
+    unsigned ok = 0, it = 0;
+    while (!ok) {
+      asm volatile(
+          "{\n .reg .pred q;\n mbarrier.try_wait.parity.shared::cta.b64 q, [%1], 0, 10000;\n selp.u32 %0, 1, 0, q;\n}\n"
+          : "=r"(ok)
+          : "r"(bar)
+          : "memory");
+      if (!ok && ++it > (1u << 17)) {
+        if (p.err) atomicOr(p.err, 2u);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+
+  // lane (kq, cq): group g = 4 warp + kq, columns 4 cq .. 4 cq + 3 of the slice
+  const int kq = lane >> 3, cq = lane & 7, g = 4 * warp + kq;
+  float v[kSMaxTok][4];
+#pragma unroll
+  for (int m = 0; m < kSMaxTok; ++m)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) v[m][c] = 0.f;
+  if (g < G) {
+    const uint4* wrow = reinterpret_cast<const uint4*>(smem + (size_t)g * 32 * 128) + cq;   // word row 32 g
+    float sc[4] = {1.f, 1.f, 1.f, 1.f};
+    if (p.group < p.K) {
+      const __half* srow = reinterpret_cast<const __half*>(smem + p.off_s) + (size_t)((g * 128) / p.group) * kSCols + 4 * cq;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) sc[c] = __half2float(srow[c]);
+    }
+#pragma unroll
+    for (int m = 0; m < kSMaxTok; ++m) {
+      if (m >= p.M) break;
+      const uint32_t* x32 = reinterpret_cast<const uint32_t*>(xq + (size_t)m * p.K + g * 128);
+      int acc[4] = {0, 0, 0, 0};
+#pragma unroll 8
+      for (int i = 0; i < 32; ++i) {
+        const uint4 w = wrow[i * 8];                       // word row 32 g + i: 4 k x 4 columns
+        const uint32_t xa = x32[2 * i], xb = x32[2 * i + 1];
+        acc[0] = dp2a_hi(xb, w.x, dp2a_lo(xa, w.x, acc[0]));
+        acc[1] = dp2a_hi(xb, w.y, dp2a_lo(xa, w.y, acc[1]));
+        acc[2] = dp2a_hi(xb, w.z, dp2a_lo(xa, w.z, acc[2]));
+        acc[3] = dp2a_hi(xb, w.w, dp2a_lo(xa, w.w, acc[3]));
+      }
+      const int zf = -p.zero * xsum[m * G + g];
+      const float es = xscl[m * G + g];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) v[m][c] = (float)(acc[c] + zf) * es * sc[c];
+    }
+  }
+  // groups of the warp in kq order (fixed shuffle tree), then warps in order
+#pragma unroll
+  for (int m = 0; m < kSMaxTok; ++m) {
+    if (m >= p.M) break;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      v[m][c] += __shfl_xor_sync(0xffffffffu, v[m][c], 8);
+      v[m][c] += __shfl_xor_sync(0xffffffffu, v[m][c], 16);
+    }
+    if (kq == 0)
+      *reinterpret_cast<float4*>(red + ((size_t)m * kSWarps + warp) * kSCols + 4 * cq) =
+          make_float4(v[m][0], v[m][1], v[m][2], v[m][3]);
+  }
+  __syncthreads();
+  for (int t = threadIdx.x; t < p.M * kSCols; t += blockDim.x) {
+    const int m = t / kSCols, col = t - m * kSCols, n = n0 + col;
+    if (n >= p.N) continue;
+    float acc = 0.f;
+#pragma unroll
+    for (int w = 0; w < kSWarps; ++w) acc += red[((size_t)m * kSWarps + w) * kSCols + col];
+    if (p.group >= p.K) acc *= __half2float(p.scales[n]);
+    p.y[(int64_t)m * p.stride_ym + n] = __float2bfloat16(acc);
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 i8_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<PFN_cuTensorMapEncodeTiled_v12000>(nullptr);
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  }();
+  return fn;
+}
+
+// Tensor maps of one weight matrix, cached per thread by (weights, scales, K, N, group) in a small
+// direct-mapped table (a model's dense projections are few and never move).
+bool slice_maps(const Int8Args& a, int box_rows, int srows, CUtensorMap& wm, CUtensorMap& sm) {
+  struct Entry {
+    const void* q; const void* s; int K, N, group; bool ok;
+    CUtensorMap wm, sm;
+  };
+  static thread_local Entry cache[64] = {};
+  Entry& e = cache[(reinterpret_cast<uintptr_t>(a.qweight) >> 8) & 63];
+  if (!(e.ok && e.q == a.qweight && e.s == a.scales && e.K == a.K && e.N == a.N && e.group == a.group)) {
+    e.ok = false;
+    const auto enc = i8_encoder();
+    if (!enc) return false;
+    const cuuint32_t es[2] = {1, 1};
+    const cuuint64_t dw[2] = {(cuuint64_t)a.N, (cuuint64_t)(a.K / 4)}, sw[1] = {(cuuint64_t)a.N * 4};
+    const cuuint32_t bw[2] = {kSCols, (cuuint32_t)box_rows};
+    if (enc(&e.wm, CU_TENSOR_MAP_DATA_TYPE_INT32, 2, const_cast<int32_t*>(a.qweight), dw, sw, bw, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return false;
+    const cuuint64_t ds[2] = {(cuuint64_t)a.N, (cuuint64_t)srows}, ss[1] = {(cuuint64_t)a.N * 2};
+    const cuuint32_t bs[2] = {kSCols, (cuuint32_t)srows};
+    if (enc(&e.sm, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(a.scales), ds, ss, bs, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return false;
+    e.q = a.qweight; e.s = a.scales; e.K = a.K; e.N = a.N; e.group = a.group; e.ok = true;
+  }
+  wm = e.wm;
+  sm = e.sm;
+  return true;
+}
+
+// The column-slice kernel when the shape qualifies; kErrShape (nothing launched) when it does not.
+int launch_slice(const Int8Args& a, const PeerExchange* xin, unsigned* err) {
+  const int KW = a.K / 4;
+  const int box_rows = KW < kSBoxRows ? KW : kSBoxRows;
+  const int srows = a.group < a.K ? a.K / a.group : 1;
+  if (a.K > kSMaxK || a.M > kSMaxTok || a.N % 8 != 0 || KW % box_rows != 0 || srows > 256) return kErrShape;
+  if ((reinterpret_cast<uintptr_t>(a.scales) & 15u)) return kErrShape;
+  I8SParams p{};
+  if (!slice_maps(a, box_rows, srows, p.wmap, p.smap)) return kErrShape;
+  const int G = a.K / 128;
+  p.x = static_cast<const __nv_bfloat16*>(a.x); p.stride_xm = a.stride_xm;
+  p.scales = static_cast<const __half*>(a.scales); p.group = a.group; p.zero = a.zero;
+  p.M = a.M; p.K = a.K; p.N = a.N; p.box_rows = box_rows; p.nbox = KW / box_rows; p.srows = srows;
+  p.y = static_cast<__nv_bfloat16*>(a.y); p.stride_ym = a.stride_ym;
+  auto a16 = [](size_t v) { return (v + 127) & ~size_t(127); };
+  size_t off = a16((size_t)KW * kSCols * 4);
+  p.off_s = off; off = a16(off + (size_t)srows * kSCols * 2);
+  p.off_xq = off; off = a16(off + (size_t)a.M * a.K * 2);
+  p.off_xsum = off; off = a16(off + (size_t)a.M * G * 4);
+  p.off_xscl = off; off = a16(off + (size_t)a.M * G * 4);
+  p.off_red = off; off = a16(off + (size_t)a.M * kSWarps * kSCols * 4);
+  p.off_bar = off; off += 16;
+  if (off > 227 * 1024) return kErrShape;
+  if (xin) {
+    p.xpeers = xin->peers; p.xtag_off = xin->tag_off; p.xrank = xin->rank; p.xepoch = xin->epoch;
+    p.xworld = xin->world; p.xn_max = xin->n_max; p.xspin = xin->spin_limit ? xin->spin_limit : kPeerSpinLimit;
+  }
+  p.err = err;
+  auto kern = xin ? int8_slice_kernel<true> : int8_slice_kernel<false>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)off) != cudaSuccess) return kErrLaunch;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((a.N + kSCols - 1) / kSCols);
+  cfg.blockDim = dim3(32 * kSWarps);
+  cfg.dynamicSmemBytes = off;
+  cfg.stream = a.stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, p) == cudaSuccess ? kOk : kErrLaunch;
+}
+}  // namespace
+
 // No workspace is needed any more; the entry point keeps its workspace arguments.
 size_t int8_workspace_bytes(int M, int K, int N) {
   (void)M; (void)K; (void)N;
@@ -213,6 +494,7 @@ int launch_int8(const Int8Args& a, const PeerExchange* xin, unsigned* err) {
               xin->n_max % 8 || (size_t)a.M * a.K > (size_t)xin->n_max || xin->tag_off % 16))
     return kErrArg;
   if ((reinterpret_cast<uintptr_t>(a.qweight) & 15u)) return kErrAlign;
+  if (launch_slice(a, xin, err) == kOk) return kOk;            // the decode shapes
   // S slices of a multiple of 256 k each (at most kMaxSlice), one cluster of S CTAs per column block
   int S = (a.K + 255) / 256;
   if (S > kMaxCluster) S = kMaxCluster;
