@@ -17,6 +17,19 @@ def test_int8_per_channel(pkg, dev, M, K, N):
     assert O.max_rel_err(y.float().cpu(), ref) < 1e-2
 
 
+@pytest.mark.parametrize("M,K,N", [(9, 1024, 512), (1, 8192, 256), (2, 1024, 132)])
+def test_int8_cluster_kernel_shapes(pkg, dev, M, K, N):
+    """Shapes the column-slice kernel does not take -- more than 8 tokens, K above 4096, N not a multiple of 8 --
+    run the cluster split-K kernel: the same parity bar, with per-channel and with g128 scales."""
+    qw, sc = pkg.synth.make_int8_dense(K, N, seed=K + N, device=dev, gen_device="cpu")
+    x = pkg.synth.make_activation(M, K, seed=M + 1, device=dev, gen_device="cpu")
+    y = pkg.int8_gemv(x, qw, sc)
+    assert O.max_rel_err(y.float().cpu(), O.int8_gemv(x.cpu(), qw.cpu(), sc.cpu())) < 1e-2
+    sg = (sc.float().repeat(K // 128, 1) * torch.linspace(0.5, 1.5, K // 128, device=dev)[:, None]).to(torch.float16)
+    y = pkg.int8_gemv(x, qw, sg)
+    assert O.max_rel_err(y.float().cpu(), O.int8_gemv(x.cpu(), qw.cpu(), sg.cpu())) < 1e-2
+
+
 def test_int8_grouped_scales_and_repeat(pkg, golden, dev):
     """The reference packing with g128 scales (pack_int8_gptq), called twice (ticket counters reset)."""
     qw, sc = golden["int8_qw"].to(dev), golden["int8_sc"].to(dev)
