@@ -228,14 +228,16 @@ int w2a16_gather_rows_tab(const int64_t* tab, const int32_t* ids, int n, void* o
  * scales f16 [K/group, N] (group == K: one scale per output channel). Replaces the GPTQ Marlin INT8
  * call SGLang makes for the dense projections (third party; docs/DECODE_PERF_PLAN.md:29).
  * x bf16 [M, K] (row stride stride_xm), y bf16 [M, N] (row stride stride_ym).
- * K % 128 == 0, N % 4 == 0, group % 128 == 0 and K % group == 0.
+ * K % 128 == 0, N % 4 == 0, group % 128 == 0 and K % group == 0. Decode shapes (K <= 4096, M <= 8, N % 8 == 0,
+ * scales 16-byte aligned) run one CTA per 32 output columns over all of K; other shapes reduce K slices inside
+ * a thread-block cluster. Both are deterministic.
  */
 int w2a16_int8_gemv(const void* x, int64_t stride_xm, const int32_t* qweight, const void* scales,
                     int group, int zero, int M, int K, int N, void* y, int64_t stride_ym,
                     void* workspace, size_t workspace_bytes, void* stream);
 
-/* Workspace bytes w2a16_int8_gemv accepts (a token amount: its K slices are reduced inside a thread-block
- * cluster; the argument stays for ABI stability). */
+/* Workspace bytes w2a16_int8_gemv accepts (a token amount: neither kernel uses global scratch; the argument
+ * stays for ABI stability). */
 size_t w2a16_int8_workspace_bytes(int M, int K, int N);
 
 /* One-shot all-reduce (sum) of a small bf16 vector across the GPUs of one node over NVLink peer memory:
