@@ -23,7 +23,9 @@ import os
 import sys
 
 os.environ["TRITON_INTERPRET"] = "1"          # must precede the triton import
-REF = os.environ.get("REF", "/root/reference")
+REF = os.environ.get("REF")
+if not REF:
+    raise SystemExit("set REF to the reference checkout (see the module docstring)")
 OUT = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden.pt")
 SERIES = os.path.join(REF, "sglang/upstream/series-base/0002-feat-moe_wna16-2-bit-experts-expert-streaming-N-cont.patch")
 
