@@ -216,10 +216,17 @@ def run_stack(args):
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     try:
         _run_stack(args, world, rank, dev)
-    finally:
-        if world > 1:
-            dist.barrier()
-            dist.destroy_process_group()
+    except BaseException:
+        # A rank that fails says why and leaves at once: waiting in a barrier here would only hold it until the
+        # other ranks' next collective times out, and the launcher ends the other ranks when this one exits.
+        import traceback
+        traceback.print_exc()
+        sys.stderr.flush()
+        sys.stdout.flush()
+        os._exit(1)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def _run_stack(args, world: int, rank: int, dev: torch.device):

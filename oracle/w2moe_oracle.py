@@ -226,7 +226,7 @@ def moe_layer_routed_only(x, experts_cpu: dict, topk_ids, topk_w, routed_scaling
             if y is None:
                 y = torch.zeros(M, d.shape[-1], dtype=torch.float32)
             y[m] += d
-    return y * float(routed_scaling_factor)
+    return None if y is None else y * float(routed_scaling_factor)   # None: no routed expert is present
 
 
 def routed_experts_from_arena(arena, ids) -> dict:

@@ -71,12 +71,13 @@ def _rank_main(rank, world, port, E, H, I, k, M, out_q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2])
-def test_sum_of_rank_partials_is_the_full_layer(world):
+@pytest.mark.parametrize("world,k,M", [(2, 4, 2), (4, 1, 1)])
+def test_sum_of_rank_partials_is_the_full_layer(world, k, M):
+    """(4, 1, 1): one routed expert, so three of the four ranks hold no routed expert and contribute zeros."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29500 + (os.getpid() % 2000)
-    procs = [ctx.Process(target=_rank_main, args=(r, world, port, 16, 256, 256, 4, 2, q)) for r in range(world)]
+    port = 29500 + (os.getpid() % 2000) + 7 * world
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, 16, 256, 256, k, M, q)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:

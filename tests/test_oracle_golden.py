@@ -145,3 +145,19 @@ def test_expert_order_oracle_matches_token_order():
     a = O.moe_layer_routed_only(x, experts, ids, w, 1.5)
     b = O.moe_layer_by_expert(ar, x, ids, w, 1.5)
     assert torch.allclose(a, b, rtol=1e-5, atol=1e-6)
+
+
+def test_oracle_layer_with_no_resident_routed_expert_is_zero():
+    """A rank of an expert-parallel step may hold none of the routed experts: its partial is zero."""
+    from types import SimpleNamespace
+    H, I, M, k = 256, 128, 2, 2
+    ar = SimpleNamespace(codes13=torch.zeros(1, H // 16, 2 * I, dtype=torch.int32),
+                         scales13=torch.ones(1, H // 128, 2 * I, dtype=torch.float16), zeros13=None,
+                         codes2=torch.zeros(1, I // 16, H, dtype=torch.int32),
+                         scales2=torch.ones(1, I // 128, H, dtype=torch.float16), zeros2=None,
+                         slots=torch.tensor([-1, -1, -1, 0], dtype=torch.int32))
+    x = torch.randn(M, H, generator=torch.Generator().manual_seed(3)).to(torch.bfloat16)
+    ids = torch.tensor([[0, 1], [2, 1]], dtype=torch.int32)
+    w = torch.full((M, k), 0.5)
+    y = O.moe_layer_from_arena(ar, x, ids, w, 2.0)
+    assert y.shape == (M, H) and torch.equal(y, torch.zeros(M, H))
