@@ -100,7 +100,7 @@ def test_argument_errors_return_status(pkg):
 def test_workspace_sizes(pkg):
     lib = pkg._native.lib()
     assert lib.w2a16_moe_layer_workspace_bytes(1, 4096, 1536, 8) >= 8 * 1536 * 4
-    # the INT8 GEMV reduces its K slices inside a thread-block cluster: no scratch beyond a token amount
+    # neither INT8 kernel uses global scratch (column slices reduce inside a CTA, K slices inside a cluster)
     assert 0 < lib.w2a16_int8_workspace_bytes(1, 4096, 4096) <= 4096
 
 
