@@ -4,7 +4,8 @@
 // Weights int32 [K/4, N]: byte i of word kw = value 4*kw + i (auto_gptq INT8 packing,
 // scripts/requant_int8.py:32-50). One 16-byte load per lane covers 4 columns x 4 k; dp2a.lo/hi
 // multiply the four weight bytes by 16-bit fixed-point activations (power-of-two scale per 128
-// values, as in the W2 kernels). The zero point folds as T - zero * sum x_fixed per 32-k quarter.
+// values, as in the W2 kernels). The zero point folds as T - zero * sum x_fixed, per 32-k quarter (cluster
+// kernel) or per 128-k group (column-slice kernel).
 //
 // Two kernels.
 //
@@ -24,7 +25,8 @@
 // distributed shared memory -> deterministic bf16 output, no workspace, no atomics. Its weight loads are
 // issued before the dependency wait as well.
 //
-// Both are launched with programmatic stream serialisation.
+// Both are launched with programmatic stream serialisation, and both have an exchange variant (kPeers) whose x
+// is the sum, in rank order, of the ranks' tagged rows of an expert-parallel channel.
 #include <cooperative_groups.h>
 #include <cuda.h>
 #include <cudaTypedefs.h>
