@@ -1,6 +1,7 @@
 """Benchmark: W2A16 g128 MoE decode layers on B200 (device-timed), with e2e, roofline and a CPU baseline.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--case stack|layer|batched|int8]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--case stack|layer|batched|int8|config0|config2|gemv]
 
 Default case ("stack"), the same workload at every N: the decode step of BASELINE config 4 -- a stack of L=48
 distinct MoE layers (M=1, H=4096, I=1536, E=256 experts per layer, top-8, W2A16 g128 with per-group zero points,
@@ -20,7 +21,10 @@ reference`` times the reference's CPU path alone and prints its own line.
 
 Other cases (profiling drivers; one GPU): ``layer`` runs `--calls` config-1 layers over an arena of
 `--experts` experts (a small arena keeps an ncu capture small); ``batched`` times config 3's token counts on the
-per-token and batched paths; ``int8`` times the INT8 dense GEMV cycling 16 distinct weight matrices.
+per-token and batched paths; ``int8`` times the INT8 dense GEMV cycling 16 distinct weight matrices; ``config0``
+and ``config2`` time those configurations' layers (config 2 also with the INT8 dense after it); ``gemv`` times
+config 1 through the three entry forms (the reference's two-GEMV composite on the drop-in GEMV, the fused layer on
+int64 address tables, the fused layer on the slot arena).
 """
 from __future__ import annotations
 
@@ -485,6 +489,56 @@ def run_case_batched(args):
     return rc
 
 
+def run_case_gemv(args):
+    """Config 1 (E=256, M=1, top-8) through the three entry forms a caller has, CUDA-graph replay over 16 routings
+    (no expert reused within 4 calls, the 1.3 GB arena > L2), µs per layer:
+      `two_gemv`  -- the reference's `_apply_gemv` composite on the drop-in `moe_gemv_int2_tab` (gate_up GEMV,
+                     silu*mul and the top-k sum in torch, down GEMV with the routed weight), as the shim of the
+                     integration notes runs it;
+      `table`     -- `apply_gemv` on the reference's int64 address tables (one fused launch, register mode);
+      `slots`     -- `moe_decode_layer` on the slot arena (one fused launch, copy-engine mode)."""
+    import __graft_entry__ as graft
+    import oracle as O
+    import torch.nn.functional as F
+    pkg = graft.load_package()
+    dev = torch.device("cuda", 0)
+    E, H, I, k = 256, SHAPE["H"], SHAPE["I"], SHAPE["top_k"]
+    arena = pkg.synth.make_arena(E, H, I, seed=0, zeros=True, scale_dtype=torch.float16, device=dev)
+    P = 16
+    ids_pool, w_pool = routing_pool(P, E, k, window=4, seed=0)
+    ids, ws = ids_pool.to(dev).reshape(P, 1, k), w_pool.to(dev).reshape(P, 1, k)
+    x = pkg.synth.make_activation(P, H, seed=0, device=dev).reshape(P, 1, H)
+    wt13, st13, sw13, ss13 = pkg.make_tables(arena.codes13, arena.scales13)
+    wt2, st2, sw2, ss2 = pkg.make_tables(arena.codes2, arena.scales2)
+    zt13, zs13 = pkg.make_zero_table(arena.zeros13)
+    zt2, zs2 = pkg.make_zero_table(arena.zeros2)
+    tabs = ((wt13, st13, sw13, ss13), (wt2, st2, sw2, ss2), 2 * I, H, H, I, False)
+    y = torch.empty(P, 1, H, dtype=torch.bfloat16, device=dev)
+
+    def two_gemv(i):
+        gu = pkg.moe_gemv_int2_tab(x[i], wt13, st13, ids[i], ws[i], 2 * I, H, sw13, ss13, k, False,
+                                   scale_bf16=False, ztab=zt13, stride_zg=zs13)
+        h = (F.silu(gu[:, :I].float()) * gu[:, I:].float()).to(torch.bfloat16)
+        dn = pkg.moe_gemv_int2_tab(h, wt2, st2, ids[i], ws[i], H, I, sw2, ss2, 1, True,
+                                   scale_bf16=False, ztab=zt2, stride_zg=zs2)
+        y[i].copy_(dn.float().sum(0, keepdim=True))
+
+    forms = {"two_gemv": two_gemv,
+             "table": lambda i: y[i].copy_(pkg.apply_gemv(x[i], ids[i], ws[i], tabs, None, zero_tabs=(zt13, zt2))),
+             "slots": lambda i: pkg.moe_decode_layer(x[i], ids[i], ws[i], arena, out=y[i])}
+    out = {"case": "gemv", "E": E, "H": H, "I": I, "top_k": k, "M": 1}
+    for name, fn in forms.items():
+        g = capture(fn, P)
+        times = [time_replays(g, 1)[0] * 1e3 / P for _ in range(5)]
+        del g
+        torch.cuda.synchronize()
+        ref = O.moe_layer_from_arena(arena, x[P - 1], ids[P - 1], ws[P - 1])
+        out[name] = {"us_per_layer": round(sorted(times)[2], 2),
+                     "max_rel_err": O.max_rel_err(y[P - 1].float().cpu(), ref)}
+    print(json.dumps(out))
+    return 0 if all(out[n]["max_rel_err"] < 1e-2 for n in forms) else 1
+
+
 def run_case_int8(args):
     """The INT8 dense [4096 -> 4096] GEMV (config 2/4) over 16 distinct weight matrices cycled (269 MB > L2):
     µs per call and GB/s of algorithmic bytes (weights + scales + x + y), CUDA-graph replay; checked once."""
@@ -632,7 +686,8 @@ def main():
     ap.add_argument("--steps", type=int, default=40)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--case", choices=["stack", "layer", "batched", "int8", "config0", "config2"], default="stack")
+    ap.add_argument("--case", choices=["stack", "layer", "batched", "int8", "config0", "config2", "gemv"],
+                    default="stack")
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU baseline sampling")
     ap.add_argument("--experts", type=int, default=256, help="case layer: experts in the arena")
     ap.add_argument("--calls", type=int, default=6, help="case layer / batched: calls")
@@ -650,6 +705,8 @@ def main():
         return run_case_batched(args)
     if args.case == "int8":
         return run_case_int8(args)
+    if args.case == "gemv":
+        return run_case_gemv(args)
     if args.case in ("config0", "config2"):
         return run_case_config(args)
     run_stack(args)
