@@ -293,7 +293,8 @@ int w2a16_moe_decode_layer_slots_ep(const void* x, int M, int H, int I, int top_
                                     unsigned int* err, void* stream);
 
 /* w2a16_int8_gemv with x the sum of the ranks' tagged rows of the channel's call *epoch (rows of K values,
- * M * K <= n_max): the dense projection after a pushing layer. */
+ * M * K <= n_max): the dense projection after a pushing layer. Every shape runs the cluster kernel, whose CTAs
+ * each poll only their K slice of every rank's row. */
 int w2a16_int8_gemv_from_peers(const w2a16_exchange* exchange, const int32_t* qweight, const void* scales, int group,
                                int zero, int M, int K, int N, void* y, int64_t stride_ym, unsigned int* err,
                                void* stream);
