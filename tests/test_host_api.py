@@ -28,6 +28,17 @@ def test_cpu_tensors_are_rejected(pkg):
                       torch.zeros(1, 8, dtype=torch.float16))
 
 
+def test_missing_library_raises(pkg, monkeypatch, tmp_path):
+    """Without the built library every op raises at its first call; nothing computes elsewhere."""
+    nat = pkg._native
+    monkeypatch.setattr(nat, "_lib", None)
+    monkeypatch.setattr(nat, "LIB_PATH", str(tmp_path / "absent" / "libw2a16_moe.so"))
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        nat.lib()
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        pkg.version()
+
+
 def test_synth_distributions(pkg):
     s = pkg.synth
     pop = s.zipf_popularity(256, 1.1, seed=0)
