@@ -71,6 +71,16 @@ def test_per_group_zero_points_match_reference_helpers(golden):
         assert torch.equal(deq.to(torch.bfloat16), golden[f"zp_{w}_ref"].transpose(1, 2))
 
 
+def test_package_zero_point_relayout_matches_oracle(pkg, golden):
+    """The package's loader conversion of qzeros (zeros_to_ncontig, a host-side transpose the GEMV form is
+    made with) equals the oracle's on the reference's golden per-group zero points, byte for byte."""
+    for w in ("w1", "w2"):
+        qz = golden[f"zp_{w}_zp"]
+        got = pkg.zeros_to_ncontig(qz)
+        assert got.dtype == torch.uint8 and got.is_contiguous()
+        assert torch.equal(got, O.zeros_to_ncontig(qz))
+
+
 def test_moe_layer_matches_reference_torch_moe(golden):
     """torch_moe (series-0002:1957-1973, bf16 math, softmax without renormalisation) vs the fp32 oracle."""
     topk = int(golden["zp_topk"])
