@@ -9,7 +9,8 @@
 //
 // Two kernels.
 //
-// Column-slice kernel (K <= 4096, at most 8 tokens; the decode shapes): each CTA owns 32 output columns over
+// Column-slice kernel (K <= 4096, at most 8 tokens, x in local memory; the single-GPU decode shapes): each CTA
+// owns 32 output columns over
 // all of K. Before it waits for the previous kernel (the weights are never written by a kernel that lets this
 // one start early) thread 0 issues tensor copies of the CTA's whole weight slice ([K/4] word rows x 128 bytes)
 // and its scale rows into shared memory; the activation rows are converted to fixed point meanwhile. Lane
