@@ -1,4 +1,5 @@
-"""Error envelope of the W2 kernels' activation format, on the CPU (no kernel runs here).
+"""Error envelope of the kernels' activation format (the W2 layer and the INT8 projection), on the CPU (no kernel
+runs here).
 
 The kernels hold x in 16-bit block fixed point: per 128-value group, x16 = round(x / 2^e) clamped to +-32767,
 with e the frexp exponent of the group's max |x| minus 15 (the activation tables of csrc/w2a16_common.cuh).
@@ -92,5 +93,22 @@ def test_activation_format_error_at_config1(pkg, case):
         x[5::128] *= 1000.0                                    # every group's exponent set by an outlier
     x = x.to(torch.bfloat16)
     ref, mod = _oracle_and_model(experts, x, ids[0], w[0])
+    assert O.max_rel_err(mod.float(), ref) < FORMAT_TOL
+    assert O.max_rel_err(mod.float().to(torch.bfloat16), ref) < TOL
+
+
+@pytest.mark.parametrize("case", ["normal", "x1000_per_group"])
+def test_int8_activation_format_error(pkg, case):
+    """The INT8 dense kernels convert x the same way (per 128-value group); the projection 4096 -> 4096 with x in
+    that format stays within the same envelope of the fp32 oracle."""
+    K = N = 4096
+    qw, sc = pkg.synth.make_int8_dense(K, N, seed=0, device="cpu")
+    x = pkg.synth.make_activation(1, K, seed=1, device="cpu").float()
+    if case == "x1000_per_group":
+        x[:, 9::128] *= 1000.0
+    x = x.to(torch.bfloat16)
+    ref = O.int8_gemv(x, qw, sc)
+    W = (O.int8_unpack(qw).double() - 128.0) * sc.double()
+    mod = fixed_point(x.float(), 128) @ W
     assert O.max_rel_err(mod.float(), ref) < FORMAT_TOL
     assert O.max_rel_err(mod.float().to(torch.bfloat16), ref) < TOL
