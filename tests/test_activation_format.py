@@ -22,14 +22,16 @@ import oracle as O
 
 TOL = 1e-2
 FORMAT_TOL = 1e-3          # the format's own share (measured at most 1.6e-4 over the cases below)
+BATCHED_FORMAT_TOL = 5e-3  # the batched path's (measured 1.7e-3, nearly all from h rounded to bf16)
 
 
-def fixed_point(v: torch.Tensor, block: int) -> torch.Tensor:
-    """The values the format represents v by (fp64): one exponent per `block` values, round half to even."""
+def fixed_point(v: torch.Tensor, block: int, frac: int = 15) -> torch.Tensor:
+    """The values the format represents v by (fp64): one exponent per `block` values, round half to even.
+    frac 15: the per-token kernels (|x16| <= 32767); 14: the batched path (|x16| <= 2^14, split into bytes)."""
     b = v.reshape(-1, block).double()
     mx = b.abs().amax(dim=1, keepdim=True)
     _, ex = torch.frexp(mx)                                    # mx = f * 2^ex, f in [0.5, 1)
-    e = torch.where(mx > 0, ex, torch.zeros_like(ex)) - 15
+    e = torch.where(mx > 0, ex, torch.zeros_like(ex)) - frac
     step = torch.pow(2.0, e.double())
     return (torch.clamp(torch.round(b / step), -32767, 32767) * step).reshape(v.shape)
 
@@ -46,12 +48,14 @@ def _experts(pkg, E, H, I, seed):
     return c13, s13, z13, c2, s2, z2
 
 
-def _oracle_and_model(experts, x, ids, w):
-    """(fp32 oracle layer, fp64 layer with x and h in the kernels' format) for one token."""
+def _oracle_and_model(experts, x, ids, w, batched=False):
+    """(fp32 oracle layer, fp64 layer with x and h in the kernels' format) for one token. batched: the batched
+    path's format (xtab_kernel in csrc/w2a16_grouped.cu): 15-bit values, and h rounded to bf16 by the gate_up
+    epilogue, then converted per 128-value group like x."""
     c13, s13, z13, c2, s2, z2 = experts
     I = s13.shape[-1] // 2
     xf = x.float()
-    xq = fixed_point(xf, 128)
+    xq = fixed_point(xf, 128, 14 if batched else 15)
     ref = torch.zeros(c2.shape[-1], dtype=torch.float64)
     mod = torch.zeros_like(ref)
     for e, we in zip(ids.tolist(), w.tolist()):
@@ -61,7 +65,10 @@ def _oracle_and_model(experts, x, ids, w):
         ref += we * (F.silu(gu[:I]) * gu[I:] @ W2).double()
         gq = xq @ W13.double()
         hq = (F.silu(gq[:I]) * gq[I:]).float()                # the kernels form h in fp32
-        mod += we * (fixed_point(hq, 32) @ W2.double())
+        if batched:
+            mod += we * (fixed_point(hq.to(torch.bfloat16).float(), 128, 14) @ W2.double())
+        else:
+            mod += we * (fixed_point(hq, 32) @ W2.double())
     return ref.float(), mod
 
 
@@ -111,4 +118,19 @@ def test_int8_activation_format_error(pkg, case):
     W = (O.int8_unpack(qw).double() - 128.0) * sc.double()
     mod = fixed_point(x.float(), 128) @ W
     assert O.max_rel_err(mod.float(), ref) < FORMAT_TOL
+    assert O.max_rel_err(mod.float().to(torch.bfloat16), ref) < TOL
+
+
+@pytest.mark.parametrize("case", ["normal", "x1000_per_group"])
+def test_batched_activation_format_error_at_config1(pkg, case):
+    """The batched path's format (x and bf16 h, 15-bit per 128-value group) at config 1's size."""
+    E, H, I, k = 16, 4096, 1536, 8
+    experts = _experts(pkg, E, H, I, seed=0)
+    ids, w = pkg.synth.route_softmax(1, E, k, seed=0, device="cpu")
+    x = pkg.synth.make_activation(1, H, seed=0, device="cpu").float()[0]
+    if case == "x1000_per_group":
+        x[5::128] *= 1000.0
+    x = x.to(torch.bfloat16)
+    ref, mod = _oracle_and_model(experts, x, ids[0], w[0], batched=True)
+    assert O.max_rel_err(mod.float(), ref) < BATCHED_FORMAT_TOL
     assert O.max_rel_err(mod.float().to(torch.bfloat16), ref) < TOL
